@@ -1,0 +1,177 @@
+/*
+ * ijb200 — C ABI of the B200 (sm_100a) decode hot path for inferencer-jetson
+ * style Llama-3.2 GGUF models (Q4_K / Q6_K weights).
+ *
+ * This is the drop-in boundary for the reference's C++ runner classes in
+ * inferencer.cu: FastGPU (:1101-1180) and FastRunner (:1182-1532).  A thin C++
+ * shim with the reference's method signatures sits on top of it
+ * (inferencer-jetson_b200/host/fast_runner.hpp).
+ *
+ * Conventions
+ *   - Every call returns an int status: IJB_OK (0) or an IJB_ERR_* code.  The
+ *     message of the last failure is available from ijb_last_error().  No C++
+ *     exception crosses this boundary (the reference throws
+ *     std::runtime_error from cuda_check, inferencer.cu:126-128, and from its
+ *     shape checks; the shim turns a non-zero status back into that).
+ *   - Pointers named *_dev are device pointers on the engine's device; all
+ *     other pointers are host pointers.  `stream` is a cudaStream_t passed as
+ *     void* (NULL = the engine's own stream).
+ *   - Tensor dims follow GGUF: dims[0] is the row length (cols), dims[1] the
+ *     row count (Tensor::cols()/rows(), inferencer.cu:184-185).
+ *   - Type ids are GGML's: 0 F32, 1 F16, 12 Q4_K, 14 Q6_K (inferencer.cu:194-201).
+ */
+#ifndef IJB200_H
+#define IJB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IJB_OK 0
+#define IJB_ERR_INVALID 1   /* bad argument, shape, type or range */
+#define IJB_ERR_CUDA 2      /* a CUDA runtime call failed */
+#define IJB_ERR_NOMEM 3     /* device or host allocation failed */
+#define IJB_ERR_CAPACITY 4  /* KV page pool, sequence table or batch limit exhausted */
+#define IJB_ERR_DEVICE 5    /* a kernel reported an error (bounded wait expired, bad index) */
+
+#define IJB_TYPE_F32 0
+#define IJB_TYPE_F16 1
+#define IJB_TYPE_Q4_K 12
+#define IJB_TYPE_Q6_K 14
+
+typedef struct ijb_engine ijb_engine;
+
+/* Model hyper-parameters (the GGUF keys FastRunner reads, inferencer.cu:1205-1214)
+ * plus serving limits.  The reference accepts only the 3B shape
+ * (:1215-1217); this build takes any Llama shape with dim, hidden a multiple
+ * of 256 and <= 8192, head_dim 64 or 128, and vocab <= 131072. */
+typedef struct {
+    int dim;             /* llama.embedding_length */
+    int layers;          /* llama.block_count */
+    int heads;           /* llama.attention.head_count */
+    int kv_heads;        /* llama.attention.head_count_kv */
+    int hidden;          /* llama.feed_forward_length */
+    int vocab;           /* llama.vocab_size */
+    float eps;           /* llama.attention.layer_norm_rms_epsilon */
+    float rope_base;     /* llama.rope.freq_base */
+    int context;         /* max positions per sequence (FastRunner --context) */
+    int max_batch;       /* max tokens in one packed step */
+    int max_seqs;        /* max open sequences */
+    int page_size;       /* tokens per KV page; 0 = 16 */
+    long num_pages;      /* KV page pool size; 0 = max_seqs * ceil(context/page_size) */
+    int use_dp4a;        /* Q4_K on the INT8 activation path (reference default; --float-gemv clears) */
+    int use_q6_dp4a;     /* Q6_K on the INT8 activation path (reference default; --float-q6 clears) */
+    int kv_f32;          /* 1: cache K/V as fp32 like the reference (inferencer.cu:1132); 0: fp16 (half the bytes) */
+    int device;          /* CUDA device ordinal */
+} ijb_model_desc;
+
+/* A view of one GGUF tensor already on the device (Tensor, inferencer.cu:178-186;
+ * Tensor::gpu points into the blob GGUF::upload copied, :321-339). */
+typedef struct {
+    const char *name;      /* GGUF tensor name, e.g. "blk.0.attn_q.weight" */
+    int type;              /* IJB_TYPE_* */
+    int n_dims;
+    int64_t dims[4];
+    const void *data_dev;  /* device pointer, 16-byte aligned for quantised types */
+} ijb_tensor_view;
+
+/* Builds an engine over the given tensors: validates names, types and shapes,
+ * takes engine-owned copies (Q6_K rows are repacked into a 16-byte aligned
+ * plane layout), allocates activations, the paged fp16 KV pool and the RoPE
+ * tables (computed on the host exactly as FastRunner's constructor does,
+ * inferencer.cu:1218-1230).  Replaces FastGPU::FastGPU + FastRunner::FastRunner. */
+int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n_tensors, ijb_engine **out);
+
+/* Frees everything the engine owns (FastGPU::~FastGPU, inferencer.cu:1141-1150). */
+void ijb_destroy(ijb_engine *engine);
+
+/* Message of the last failed call on `engine` (or of the last failed
+ * ijb_create in this thread when engine is NULL).  Never NULL. */
+const char *ijb_last_error(const ijb_engine *engine);
+
+/* Index of a tensor passed to ijb_create, by GGUF name; -1 if absent. */
+int ijb_tensor_index(const ijb_engine *engine, const char *name);
+
+/* y[b] = W x[b] for `batch` activations (x_dev [batch][cols] fp32, y_dev
+ * [batch][rows] fp32), with the quantised activation path the engine was
+ * created with.  Drop-in for FastGPU::matvec (inferencer.cu:1156-1171; batch
+ * > 1 replaces FastRunner::batch_matvec, :1265-1278). */
+int ijb_matvec(ijb_engine *engine, int tensor_index, const float *x_dev, float *y_dev, int cols, int rows,
+               int batch, void *stream);
+
+/* One decode token of the single-sequence runner (sequence 0): embeds
+ * `token` at position `pos`, runs every layer, and when need_logits is set,
+ * the final norm, lm_head and greedy argmax; *next_token receives the argmax
+ * (or -1 without logits).  Requires 0 <= pos < context, 0 <= token < vocab,
+ * and pos <= current length of sequence 0.  Drop-in for FastRunner::forward
+ * (inferencer.cu:1424-1531). */
+int ijb_forward(ijb_engine *engine, int token, int pos, int need_logits, int *next_token);
+
+/* Prefill of the single-sequence runner from position 0: the tokens run
+ * through packed steps of up to max_batch tokens; *next_token is the argmax
+ * after the last one.  Drop-in for FastRunner::prefill (inferencer.cu:1279-1423). */
+int ijb_prefill(ijb_engine *engine, const int *tokens, int n, int *next_token);
+
+/* Forgets sequence 0's cached positions (FastRunner::reset, inferencer.cu:1264). */
+int ijb_reset(ijb_engine *engine);
+
+/* Device pointers to the last step's fp32 logits [n][vocab] and residual
+ * stream [n][dim] (FastGPU::logits and FastGPU::x, inferencer.cu:1101-1103). */
+const float *ijb_logits_dev(const ijb_engine *engine);
+const float *ijb_residual_dev(const ijb_engine *engine);
+
+/* Ragged continuous batching (new; the reference runs one sequence). */
+int ijb_seq_open(ijb_engine *engine, int *seq_id);
+int ijb_seq_close(ijb_engine *engine, int seq_id);
+int ijb_seq_length(const ijb_engine *engine, int seq_id);
+
+/* One packed step over n entries: entry i appends tokens[i] to sequence
+ * seq_ids[i] at that sequence's next position.  Entries may repeat a
+ * sequence with consecutive tokens (chunked prefill) or name distinct
+ * sequences (decode).  With next_tokens non-NULL, each entry's greedy argmax is
+ * copied to the host; the call returns after the step completed. */
+int ijb_decode_step(ijb_engine *engine, int n, const int *seq_ids, const int *tokens, int *next_tokens);
+
+/* Prefill one sequence with n tokens (chunks of max_batch); *next_token is
+ * the argmax after the last token. */
+int ijb_seq_prefill(ijb_engine *engine, int seq_id, const int *tokens, int n, int *next_token);
+
+/* ---- standalone kernels (no engine) ---- */
+
+/* Greedy argmax with the reference's tie rule (argmax_blocks_cuda +
+ * argmax_final_cuda, inferencer.cu:1063-1099); n <= 131072. */
+int ijb_argmax(const float *values_dev, int n, int *index_dev, void *stream);
+
+/* Dequantise n_blocks super-blocks to fp32, bit-identical to q4_value /
+ * q6_value (inferencer.cu:454-487).  `blocks_dev` is GGUF layout. */
+int ijb_dequant(int type, const void *blocks_dev, long n_blocks, float *out_dev, void *stream);
+
+/* Bytes per row of the repacked Q6_K plane layout for `cols` columns
+ * (ql | qh | scales | d, padded to 16 bytes). */
+long ijb_q6k_planar_row_bytes(int cols);
+
+/* GGUF Q6_K rows -> plane layout (the load-time repack GGUF::upload feeds). */
+int ijb_repack_q6k(const void *src_dev, void *dst_dev, int rows, int cols, void *stream);
+
+/* Standalone GEMV over one matrix: w_dev is GGUF layout for Q4_K, plane
+ * layout (ijb_repack_q6k) for Q6_K; use_dp4a selects the INT8 activation path
+ * (quantize_x32_cuda + gemv_q4_dp4a / gemv_q6_dp4a) or the FP32 path
+ * (gemv_quant<T>), inferencer.cu:544-674.  batch <= 8. */
+int ijb_gemv(int type, const void *w_dev, const float *x_dev, float *y_dev, int cols, int rows, int batch,
+             int use_dp4a, void *stream);
+
+/* Number of kernels the library launched since load (for launch accounting). */
+uint64_t ijb_kernel_launches(void);
+
+/* Device time (CUDA events on the engine's stream) of the last step run by
+ * ijb_forward / ijb_prefill / ijb_decode_step, in milliseconds: the
+ * counterpart of FastGPU's event timer (start_timer/stop_timer, inferencer.cu:1172-1179). */
+float ijb_last_step_ms(const ijb_engine *engine);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IJB200_H */

@@ -1,0 +1,36 @@
+// Host-visible parameters of the paged decode-attention launch.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ijb {
+
+struct AttnParams {
+    const float *q;        // [batch][q_stride], RoPE already applied
+    long q_stride;
+    float *out;            // [batch][out_stride]
+    long out_stride;
+    const void *k_cache;   // this layer's pool base (K part of page 0)
+    const void *v_cache;   // this layer's pool base (V part of page 0)
+    int kv_f32;            // cache elements are fp32 (else fp16)
+    long page_stride;      // elements per page
+    int page_size;
+    const int *page_table; // [max_seqs][max_pages_per_seq]
+    int max_pages_per_seq;
+    const int *tok_seq;    // [batch]
+    const int *tok_pos;    // [batch]: attends to positions 0..pos
+    int batch, heads, kv_heads, head_dim;
+    float scale;           // 1/sqrt(head_dim)
+    int split_len;         // positions per split (attention_split_len())
+    int max_splits;        // grid.x; >= ceil(context / split_len)
+    float *partial;        // [batch][heads][max_splits][head_dim + 2] scratch
+    int *counters;         // [batch][kv_heads], zero between launches
+    uint32_t *status;      // device error word (bounded waits)
+};
+
+cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl);
+int attention_split_len();  // positions per split the kernel is built for
+cudaError_t attention_prepare();  // once per device, before any launch
+
+}  // namespace ijb

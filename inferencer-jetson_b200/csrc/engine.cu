@@ -1,0 +1,806 @@
+// The C-ABI engine (include/ijb200.h): weight registry and load-time repack,
+// paged fp16 KV pool, sequence table, packed decode steps captured into CUDA
+// graphs with programmatic dependent launch between kernels.
+//
+// It takes the place of FastGPU (inferencer.cu:1101-1180) and FastRunner
+// (:1182-1532).  Per layer a step launches five kernels where the reference
+// launches 13-17 (QKV + RoPE + KV write, attention, O + residual,
+// gate/up + SiLU, down + residual); the whole step is one CUDA graph.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+#include <atomic>
+
+#include "../../include/ijb200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "misc.cuh"
+
+namespace ijb {
+
+static std::atomic<uint64_t> g_launches{0};
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+static void ck(cudaError_t e, const char *where) {
+    if (e != cudaSuccess) throw Error(IJB_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+static void require(bool ok, const std::string &msg, int code = IJB_ERR_INVALID) {
+    if (!ok) throw Error(code, msg);
+}
+
+template <class T>
+static T *dev_alloc(size_t count, const char *what) {
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, count * sizeof(T) + 16);
+    if (e != cudaSuccess) throw Error(IJB_ERR_NOMEM, std::string("cudaMalloc ") + what + ": " + cudaGetErrorString(e));
+    return static_cast<T *>(p);
+}
+
+struct Weight {
+    std::string name;
+    int type = 0;
+    int rows = 0, cols = 0;
+    const uint8_t *data = nullptr;  // usable layout (Q4_K GGUF, Q6_K planar, F32)
+    int row_bytes = 0;
+    void *owned = nullptr;
+};
+
+struct StepGraph {
+    cudaGraphExec_t exec = nullptr;
+    bool need_logits = true;
+};
+
+}  // namespace ijb
+
+using namespace ijb;
+
+struct ijb_engine {
+    ijb_model_desc d{};
+    int head_dim = 0, kv_dim = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<Weight> w;
+    std::unordered_map<std::string, int> by_name;
+    struct Layer {
+        int attn_norm, ffn_norm, q, k, v, o, gate, up, down;
+    };
+    std::vector<Layer> layers;
+    int token_embd = -1, output = -1, output_norm = -1;
+
+    // KV pool: per layer, num_pages pages of [K: kv_heads x page x hd][V: same]
+    // elements, fp16 (default) or fp32
+    void *kv = nullptr;
+    int kv_f32 = 0;
+    int kv_elem = 2;
+    long page_stride = 0;
+    long num_pages = 0;
+    std::vector<int> free_pages;
+    int max_pages_per_seq = 0;
+    int *page_table_dev = nullptr;
+    int *page_table_host = nullptr;  // pinned mirror [max_seqs][max_pages_per_seq]
+    std::vector<std::vector<int>> seq_pages;
+    std::vector<int> seq_len;
+    std::vector<char> seq_used;
+
+    // RoPE tables [context][head_dim/2]
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+
+    // activations for max_batch tokens
+    float *x = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+    unsigned long long *keys = nullptr;
+    int *next_dev = nullptr;
+    int *meta_dev = nullptr;   // [4][max_batch]: token, seq, pos, slot
+    int *meta_host = nullptr;  // pinned
+    int *next_host = nullptr;  // pinned
+    float *attn_partial = nullptr;
+    int *attn_counters = nullptr;
+    int attn_split_len = 64, attn_max_splits = 1;
+    uint32_t *status = nullptr;
+    unsigned long long *scratch_key = nullptr;
+
+    std::unordered_map<int, StepGraph> graphs;  // key: n * 2 + need_logits
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+    bool pdl = false;  // programmatic dependent launch between the step's kernels
+    float last_step_ms = 0.f;
+    std::string err;
+    int last_n = 0;
+};
+
+namespace {
+
+thread_local std::string t_create_err;
+
+int fail(ijb_engine *e, const std::exception &ex) {
+    const Error *er = dynamic_cast<const Error *>(&ex);
+    int code = er ? er->code : IJB_ERR_INVALID;
+    if (e) e->err = ex.what();
+    else t_create_err = ex.what();
+    return code;
+}
+
+cudaStream_t pick(ijb_engine *e, void *s) { return s ? static_cast<cudaStream_t>(s) : e->stream; }
+
+// ------------------------------------------------------------ GEMV params --
+
+void add_seg(GemvParams &p, const Weight &w, const Weight *w2, int epi, float *out, long out_stride, int row_offset,
+             const ijb_model_desc &d) {
+    require(p.nseg < kMaxSegs, "too many GEMV segments");
+    GemvSeg &s = p.seg[p.nseg++];
+    s.w0 = w.data;
+    s.w1 = w2 ? w2->data : nullptr;
+    s.type = w.type;
+    s.dp4a = w.type == kQ4K ? d.use_dp4a : d.use_q6_dp4a;
+    s.rows = w.rows;
+    s.row_bytes = w.row_bytes;
+    // a work item is a gate/up pair or a RoPE row pair, else one row
+    s.item_rows = (w2 != nullptr || epi == kEpiRopeQ || epi == kEpiRopeKCache) ? 2 : 1;
+    s.item0 = p.total_items;
+    s.nitems = w2 ? w.rows : w.rows / s.item_rows;
+    s.epi = epi;
+    s.out = out;
+    s.out_stride = out_stride;
+    s.row_offset = row_offset;
+    p.total_items += s.nitems;
+    if (!s.dp4a) p.need_f = 1;
+    else if (s.type == kQ4K) p.need_q4 = 1;
+    else p.need_q6 = 1;
+}
+
+GemvParams base_params(ijb_engine *e, int cols, int batch, const float *x, long x_stride, const float *norm_w) {
+    GemvParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.cols = cols;
+    p.batch = batch;
+    p.x = x;
+    p.x_stride = x_stride;
+    p.norm_w = norm_w;
+    p.eps = e->d.eps;
+    p.rope_cos = e->rope_cos;
+    p.rope_sin = e->rope_sin;
+    p.half_head = e->head_dim / 2;
+    p.kv_heads = e->d.kv_heads;
+    p.head_dim = e->head_dim;
+    p.page_size = e->d.page_size;
+    p.page_stride = e->page_stride;
+    p.kv_f32 = e->kv_f32;
+    p.argmax_keys = e->keys;
+    p.status = e->status;
+    return p;
+}
+
+void launch_gemv(ijb_engine *e, const GemvParams &p, cudaStream_t s, bool pdl) {
+    ck(gemv_launch(p, e->num_sms, s, pdl && e->pdl), "GEMV launch");
+    ++g_launches;
+}
+
+// Every kernel of one packed step over n tokens (meta already on the device).
+void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
+    const ijb_model_desc &d = e->d;
+    const int *tok = e->meta_dev;
+    const int *tseq = e->meta_dev + d.max_batch;
+    const int *tpos = e->meta_dev + 2 * d.max_batch;
+    const int *tslot = e->meta_dev + 3 * d.max_batch;
+    const Weight &emb = e->w[e->token_embd];
+    ck(embed_launch(emb.data, emb.row_bytes, d.dim, tok, n, e->x, d.dim, e->keys, s, e->pdl), "embedding launch");
+    ++g_launches;
+    const long layer_pool = e->num_pages * e->page_stride;
+    const long v_off = static_cast<long>(d.kv_heads) * d.page_size * e->head_dim;
+    for (int l = 0; l < d.layers; ++l) {
+        const auto &L = e->layers[l];
+        char *kbase = static_cast<char *>(e->kv) + l * layer_pool * e->kv_elem;
+        // tokens go through the CUDA-core GEMV in groups of at most kMaxBatch
+        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+            const int gn = std::min(kMaxBatch, n - g0);
+            GemvParams p = base_params(e, d.dim, gn, e->x + static_cast<long>(g0) * d.dim, d.dim,
+                                       reinterpret_cast<const float *>(e->w[L.attn_norm].data));
+            p.tok_pos = tpos + g0;
+            p.tok_slot = tslot + g0;
+            p.k_cache = kbase;
+            p.v_cache = kbase + v_off * e->kv_elem;
+            add_seg(p, e->w[L.q], nullptr, kEpiRopeQ, e->q + static_cast<long>(g0) * d.dim, d.dim, 0, d);
+            add_seg(p, e->w[L.k], nullptr, kEpiRopeKCache, nullptr, 0, 0, d);
+            add_seg(p, e->w[L.v], nullptr, kEpiVCache, nullptr, 0, 0, d);
+            launch_gemv(e, p, s, true);
+        }
+        AttnParams a;
+        std::memset(&a, 0, sizeof(a));
+        a.q = e->q;
+        a.q_stride = d.dim;
+        a.out = e->attn;
+        a.out_stride = d.dim;
+        a.k_cache = kbase;
+        a.v_cache = kbase + v_off * e->kv_elem;
+        a.kv_f32 = e->kv_f32;
+        a.page_stride = e->page_stride;
+        a.page_size = d.page_size;
+        a.page_table = e->page_table_dev;
+        a.max_pages_per_seq = e->max_pages_per_seq;
+        a.tok_seq = tseq;
+        a.tok_pos = tpos;
+        a.batch = n;
+        a.heads = d.heads;
+        a.kv_heads = d.kv_heads;
+        a.head_dim = e->head_dim;
+        a.scale = 1.0f / std::sqrt(static_cast<float>(e->head_dim));
+        a.split_len = e->attn_split_len;
+        a.max_splits = e->attn_max_splits;
+        a.partial = e->attn_partial;
+        a.counters = e->attn_counters;
+        a.status = e->status;
+        ck(attention_launch(a, s, e->pdl), "attention launch");
+        ++g_launches;
+        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+            const int gn = std::min(kMaxBatch, n - g0);
+            GemvParams p = base_params(e, d.dim, gn, e->attn + static_cast<long>(g0) * d.dim, d.dim, nullptr);
+            add_seg(p, e->w[L.o], nullptr, kEpiAdd, e->x + static_cast<long>(g0) * d.dim, d.dim, 0, d);
+            launch_gemv(e, p, s, true);
+        }
+        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+            const int gn = std::min(kMaxBatch, n - g0);
+            GemvParams p = base_params(e, d.dim, gn, e->x + static_cast<long>(g0) * d.dim, d.dim,
+                                       reinterpret_cast<const float *>(e->w[L.ffn_norm].data));
+            add_seg(p, e->w[L.gate], &e->w[L.up], kEpiSiluPair, e->h + static_cast<long>(g0) * d.hidden, d.hidden, 0,
+                    d);
+            launch_gemv(e, p, s, true);
+        }
+        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+            const int gn = std::min(kMaxBatch, n - g0);
+            GemvParams p = base_params(e, d.hidden, gn, e->h + static_cast<long>(g0) * d.hidden, d.hidden, nullptr);
+            add_seg(p, e->w[L.down], nullptr, kEpiAdd, e->x + static_cast<long>(g0) * d.dim, d.dim, 0, d);
+            launch_gemv(e, p, s, true);
+        }
+    }
+    if (!need_logits) return;
+    const Weight &out = e->w[e->output >= 0 ? e->output : e->token_embd];
+    for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+        const int gn = std::min(kMaxBatch, n - g0);
+        GemvParams p = base_params(e, d.dim, gn, e->x + static_cast<long>(g0) * d.dim, d.dim,
+                                   reinterpret_cast<const float *>(e->w[e->output_norm].data));
+        p.argmax_keys = e->keys + g0;
+        add_seg(p, out, nullptr, kEpiLogitsArgmax, e->logits + static_cast<long>(g0) * d.vocab, d.vocab, 0, d);
+        launch_gemv(e, p, s, true);
+    }
+    ck(keys_to_tokens_launch(e->keys, n, e->next_dev, s, e->pdl), "argmax decode launch");
+    ++g_launches;
+}
+
+// Captures (once per n / need_logits) and replays the whole step: H2D of the
+// step's metadata, every kernel, D2H of the next tokens.
+void run_step(ijb_engine *e, int n, bool need_logits) {
+    const int key = n * 2 + (need_logits ? 1 : 0);
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaGraph_t graph;
+        ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        try {
+            ck(cudaMemcpyAsync(e->meta_dev, e->meta_host, 4 * e->d.max_batch * sizeof(int), cudaMemcpyHostToDevice,
+                               e->stream),
+               "meta H2D");
+            enqueue_step(e, n, need_logits, e->stream);
+            if (need_logits)
+                ck(cudaMemcpyAsync(e->next_host, e->next_dev, n * sizeof(int), cudaMemcpyDeviceToHost, e->stream),
+                   "next D2H");
+        } catch (...) {
+            cudaStreamEndCapture(e->stream, &graph);
+            throw;
+        }
+        ck(cudaStreamEndCapture(e->stream, &graph), "end capture");
+        StepGraph sg;
+        cudaError_t ie = cudaGraphInstantiate(&sg.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        ck(ie, "graph instantiate");
+        it = e->graphs.emplace(key, sg).first;
+    }
+    // launches inside the graph count as launches of this library
+    g_launches += static_cast<uint64_t>(e->d.layers) * (1 + 4 * ((n + kMaxBatch - 1) / kMaxBatch)) + 1 +
+                  (need_logits ? (n + kMaxBatch - 1) / kMaxBatch + 1 : 0);
+    ck(cudaEventRecord(e->ev_start, e->stream), "step timer start");
+    ck(cudaGraphLaunch(it->second.exec, e->stream), "graph launch");
+    ck(cudaEventRecord(e->ev_end, e->stream), "step timer end");
+    ck(cudaStreamSynchronize(e->stream), "step synchronize");
+    ck(cudaEventElapsedTime(&e->last_step_ms, e->ev_start, e->ev_end), "step timer");
+    uint32_t st = 0;
+    ck(cudaMemcpy(&st, e->status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
+    if (st) {
+        cudaMemset(e->status, 0, sizeof(uint32_t));
+        throw Error(IJB_ERR_DEVICE, "kernel reported device error code " + std::to_string(st));
+    }
+    e->last_n = n;
+}
+
+// Makes sure `seq` owns pages for positions [0, upto]; returns the slot of `pos`.
+int slot_for(ijb_engine *e, int seq, int pos) {
+    const int ps = e->d.page_size;
+    auto &pages = e->seq_pages[seq];
+    bool changed = false;
+    while (static_cast<int>(pages.size()) * ps <= pos) {
+        require(!e->free_pages.empty(), "KV page pool exhausted", IJB_ERR_CAPACITY);
+        require(static_cast<int>(pages.size()) < e->max_pages_per_seq, "sequence exceeds context", IJB_ERR_CAPACITY);
+        pages.push_back(e->free_pages.back());
+        e->free_pages.pop_back();
+        e->page_table_host[static_cast<long>(seq) * e->max_pages_per_seq + pages.size() - 1] = pages.back();
+        changed = true;
+    }
+    if (changed)
+        ck(cudaMemcpyAsync(e->page_table_dev + static_cast<long>(seq) * e->max_pages_per_seq,
+                           e->page_table_host + static_cast<long>(seq) * e->max_pages_per_seq,
+                           pages.size() * sizeof(int), cudaMemcpyHostToDevice, e->stream),
+           "page table H2D");
+    return pages[pos / ps] * ps + pos % ps;
+}
+
+// Fills meta for entries (seq, token) at explicit positions and runs a step.
+void packed_step(ijb_engine *e, int n, const int *seqs, const int *tokens, const int *positions, bool need_logits) {
+    const ijb_model_desc &d = e->d;
+    require(n >= 1 && n <= d.max_batch, "step size must be 1..max_batch", IJB_ERR_CAPACITY);
+    int *mt = e->meta_host;
+    // the previous step synchronised, so the pinned staging buffer is free
+    for (int i = 0; i < n; ++i) {
+        const int sq = seqs[i], pos = positions[i], tk = tokens[i];
+        require(sq >= 0 && sq < d.max_seqs && e->seq_used[sq], "unknown sequence id");
+        require(pos >= 0 && pos < d.context && tk >= 0 && tk < d.vocab, "Token or position outside model context");
+        mt[i] = tk;
+        mt[d.max_batch + i] = sq;
+        mt[2 * d.max_batch + i] = pos;
+        mt[3 * d.max_batch + i] = slot_for(e, sq, pos);
+    }
+    for (int i = n; i < d.max_batch; ++i) mt[i] = mt[d.max_batch + i] = mt[2 * d.max_batch + i] = mt[3 * d.max_batch + i] = 0;
+    run_step(e, n, need_logits);
+}
+
+void validate_weight(const Weight &w, int type_a, int type_b, int rows, int cols) {
+    require(w.type == type_a || w.type == type_b, "Unexpected quantization for " + w.name);
+    require(w.rows == rows && w.cols == cols, "Unexpected quantized matrix shape for " + w.name);
+}
+
+}  // namespace
+
+// =================================================================== C ABI ==
+
+extern "C" {
+
+int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n_tensors, ijb_engine **out) {
+    std::unique_ptr<ijb_engine> e(new ijb_engine());
+    try {
+        require(desc && out && tensors, "null argument");
+        e->d = *desc;
+        ijb_model_desc &d = e->d;
+        if (d.page_size <= 0) d.page_size = 16;
+        require(d.dim > 0 && d.dim % 256 == 0 && d.dim <= kMaxCols, "dim must be a multiple of 256, <= 8192");
+        require(d.hidden > 0 && d.hidden % 256 == 0 && d.hidden <= kMaxCols, "hidden must be a multiple of 256, <= 8192");
+        require(d.heads > 0 && d.kv_heads > 0 && d.heads % d.kv_heads == 0 && d.dim % d.heads == 0, "bad head counts");
+        e->head_dim = d.dim / d.heads;
+        e->kv_dim = e->head_dim * d.kv_heads;
+        const int G = d.heads / d.kv_heads;
+        require(e->head_dim == 64 || e->head_dim == 128, "head_dim must be 64 or 128");
+        require(G == 1 || G == 2 || G == 4 || G == 8, "heads / kv_heads must be 1, 2, 4 or 8");
+        require(d.vocab > 0 && d.vocab <= 512 * 256, "vocab must be <= 131072 (the reference's two-pass argmax)");
+        require(d.layers > 0 && d.context > 0 && d.max_batch > 0 && d.max_seqs > 0, "bad limits");
+        require(d.page_size == 16 || d.page_size == 32 || d.page_size == 8, "page_size must be 8, 16 or 32");
+        ck(cudaSetDevice(d.device), "cudaSetDevice");
+        ck(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, d.device), "SM count");
+        ck(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
+        ck(gemv_prepare(), "GEMV attributes");
+        {
+            // IJB_PDL=1 launches the step's kernels with programmatic dependent
+            // launch.  Off by default: measured on B200, a decode step of
+            // the 1B model took 0.98 ms with it and 0.79 ms without.
+            const char *env = std::getenv("IJB_PDL");
+            e->pdl = env && env[0] == '1';
+        }
+        ck(attention_prepare(), "attention attributes");
+        ck(cudaEventCreate(&e->ev_start), "event");
+        ck(cudaEventCreate(&e->ev_end), "event");
+
+        for (int i = 0; i < n_tensors; ++i) {
+            const ijb_tensor_view &t = tensors[i];
+            require(t.name != nullptr, "tensor without name");
+            Weight w;
+            w.name = t.name;
+            w.type = t.type;
+            require(t.n_dims >= 1 && t.n_dims <= 4, "Invalid tensor dimensions: " + w.name);
+            w.cols = static_cast<int>(t.dims[0]);
+            w.rows = t.n_dims >= 2 ? static_cast<int>(t.dims[1]) : 1;
+            require(t.data_dev != nullptr, "tensor without data: " + w.name);
+            if (t.type == IJB_TYPE_Q4_K) {
+                require(w.cols % 256 == 0, "Invalid quantized tensor shape: " + w.name);
+                w.row_bytes = w.cols / 256 * kQ4Bytes;
+                if (reinterpret_cast<uintptr_t>(t.data_dev) % 16 == 0) {
+                    w.data = static_cast<const uint8_t *>(t.data_dev);
+                } else {
+                    uint8_t *c = dev_alloc<uint8_t>(static_cast<size_t>(w.rows) * w.row_bytes, "Q4_K copy");
+                    ck(cudaMemcpy(c, t.data_dev, static_cast<size_t>(w.rows) * w.row_bytes, cudaMemcpyDeviceToDevice),
+                       "Q4_K copy");
+                    w.data = c;
+                    w.owned = c;
+                }
+            } else if (t.type == IJB_TYPE_Q6_K) {
+                require(w.cols % 256 == 0, "Invalid quantized tensor shape: " + w.name);
+                w.row_bytes = static_cast<int>(q6_planar_row_bytes(w.cols));
+                uint8_t *c = dev_alloc<uint8_t>(static_cast<size_t>(w.rows) * w.row_bytes, "Q6_K repack");
+                ck(repack_q6_launch(t.data_dev, c, w.rows, w.cols, e->stream), "Q6_K repack");
+                w.data = c;
+                w.owned = c;
+            } else if (t.type == IJB_TYPE_F32) {
+                w.row_bytes = w.cols * 4;
+                w.data = static_cast<const uint8_t *>(t.data_dev);
+            } else {
+                throw Error(IJB_ERR_INVALID, "Unsupported tensor storage type: " + w.name);
+            }
+            e->by_name[w.name] = static_cast<int>(e->w.size());
+            e->w.push_back(w);
+        }
+        auto find = [&](const std::string &n) {
+            auto it = e->by_name.find(n);
+            require(it != e->by_name.end(), "Missing tensor: " + n);
+            return it->second;
+        };
+        e->token_embd = find("token_embd.weight");
+        require(e->w[e->token_embd].type == IJB_TYPE_Q6_K, "Expected Q6_K token embedding");
+        validate_weight(e->w[e->token_embd], kQ6K, kQ6K, d.vocab, d.dim);
+        e->output_norm = find("output_norm.weight");
+        if (e->by_name.count("output.weight")) {
+            e->output = e->by_name["output.weight"];
+            validate_weight(e->w[e->output], kQ4K, kQ6K, d.vocab, d.dim);
+        }
+        for (int l = 0; l < d.layers; ++l) {
+            const std::string p = "blk." + std::to_string(l) + ".";
+            ijb_engine::Layer L;
+            L.attn_norm = find(p + "attn_norm.weight");
+            L.ffn_norm = find(p + "ffn_norm.weight");
+            L.q = find(p + "attn_q.weight");
+            L.k = find(p + "attn_k.weight");
+            L.v = find(p + "attn_v.weight");
+            L.o = find(p + "attn_output.weight");
+            L.gate = find(p + "ffn_gate.weight");
+            L.up = find(p + "ffn_up.weight");
+            L.down = find(p + "ffn_down.weight");
+            validate_weight(e->w[L.q], kQ4K, kQ4K, d.dim, d.dim);
+            validate_weight(e->w[L.k], kQ4K, kQ4K, e->kv_dim, d.dim);
+            validate_weight(e->w[L.v], kQ4K, kQ6K, e->kv_dim, d.dim);
+            validate_weight(e->w[L.o], kQ4K, kQ4K, d.dim, d.dim);
+            validate_weight(e->w[L.gate], kQ4K, kQ4K, d.hidden, d.dim);
+            validate_weight(e->w[L.up], kQ4K, kQ4K, d.hidden, d.dim);
+            validate_weight(e->w[L.down], kQ4K, kQ6K, d.dim, d.hidden);
+            require(e->w[L.attn_norm].type == IJB_TYPE_F32 && e->w[L.attn_norm].cols == d.dim, "bad attn_norm");
+            require(e->w[L.ffn_norm].type == IJB_TYPE_F32 && e->w[L.ffn_norm].cols == d.dim, "bad ffn_norm");
+            e->layers.push_back(L);
+        }
+        require(e->w[e->output_norm].type == IJB_TYPE_F32 && e->w[e->output_norm].cols == d.dim, "bad output_norm");
+
+        // RoPE tables, computed on the host the way FastRunner's constructor
+        // does (inferencer.cu:1218-1230): float pow, angle = pos * freq, cos/sin.
+        const int half = e->head_dim / 2;
+        std::vector<float> cs(static_cast<size_t>(d.context) * half), sn(cs.size()), freq(half);
+        for (int i = 0; i < half; ++i) freq[i] = std::pow(d.rope_base, -2.f * i / e->head_dim);
+        for (int pos = 0; pos < d.context; ++pos)
+            for (int i = 0; i < half; ++i) {
+                float angle = pos * freq[i];
+                cs[static_cast<size_t>(pos) * half + i] = std::cos(angle);
+                sn[static_cast<size_t>(pos) * half + i] = std::sin(angle);
+            }
+        e->rope_cos = dev_alloc<float>(cs.size(), "RoPE cos");
+        e->rope_sin = dev_alloc<float>(sn.size(), "RoPE sin");
+        ck(cudaMemcpy(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "RoPE upload");
+        ck(cudaMemcpy(e->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "RoPE upload");
+
+        // KV pool
+        e->max_pages_per_seq = (d.context + d.page_size - 1) / d.page_size;
+        e->num_pages = d.num_pages > 0 ? d.num_pages : static_cast<long>(d.max_seqs) * e->max_pages_per_seq;
+        e->page_stride = 2L * d.kv_heads * d.page_size * e->head_dim;
+        e->kv_f32 = d.kv_f32 ? 1 : 0;
+        e->kv_elem = e->kv_f32 ? 4 : 2;
+        const size_t kv_bytes = static_cast<size_t>(d.layers) * e->num_pages * e->page_stride * e->kv_elem;
+        e->kv = dev_alloc<char>(kv_bytes, "KV pool");
+        ck(cudaMemset(e->kv, 0, kv_bytes), "KV clear");
+        for (long p = e->num_pages - 1; p >= 0; --p) e->free_pages.push_back(static_cast<int>(p));
+        const size_t pt = static_cast<size_t>(d.max_seqs) * e->max_pages_per_seq;
+        e->page_table_dev = dev_alloc<int>(pt, "page table");
+        ck(cudaMemset(e->page_table_dev, 0, pt * sizeof(int)), "page table clear");
+        ck(cudaMallocHost(&e->page_table_host, pt * sizeof(int)), "page table mirror");
+        std::memset(e->page_table_host, 0, pt * sizeof(int));
+        e->seq_pages.resize(d.max_seqs);
+        e->seq_len.assign(d.max_seqs, 0);
+        e->seq_used.assign(d.max_seqs, 0);
+        e->seq_used[0] = 1;  // sequence 0 backs ijb_forward / ijb_prefill
+
+        // activations
+        const size_t B = d.max_batch;
+        e->x = dev_alloc<float>(B * d.dim, "residual");
+        e->q = dev_alloc<float>(B * d.dim, "query");
+        e->attn = dev_alloc<float>(B * d.dim, "attention out");
+        e->h = dev_alloc<float>(B * d.hidden, "ffn hidden");
+        e->logits = dev_alloc<float>(B * d.vocab, "logits");
+        e->keys = dev_alloc<unsigned long long>(B, "argmax keys");
+        e->next_dev = dev_alloc<int>(B, "next tokens");
+        e->meta_dev = dev_alloc<int>(4 * B, "step meta");
+        ck(cudaMemset(e->meta_dev, 0, 4 * B * sizeof(int)), "meta clear");
+        ck(cudaMallocHost(&e->meta_host, 4 * B * sizeof(int)), "meta staging");
+        ck(cudaMallocHost(&e->next_host, B * sizeof(int)), "next staging");
+        std::memset(e->meta_host, 0, 4 * B * sizeof(int));
+        // attention splits: short splits when few tokens share the GPU
+        e->attn_split_len = attention_split_len();
+        e->attn_max_splits = (d.context + e->attn_split_len - 1) / e->attn_split_len;
+        e->attn_partial = dev_alloc<float>(B * d.heads * e->attn_max_splits * (e->head_dim + 2), "attention partials");
+        e->attn_counters = dev_alloc<int>(B * d.kv_heads, "attention counters");
+        ck(cudaMemset(e->attn_counters, 0, B * d.kv_heads * sizeof(int)), "counters clear");
+        e->status = dev_alloc<uint32_t>(1, "status");
+        ck(cudaMemset(e->status, 0, sizeof(uint32_t)), "status clear");
+        e->scratch_key = dev_alloc<unsigned long long>(1, "argmax scratch");
+        ck(cudaStreamSynchronize(e->stream), "create synchronize");
+        *out = e.release();
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        int code = fail(nullptr, ex);
+        ijb_destroy(e.release());
+        return code;
+    }
+}
+
+void ijb_destroy(ijb_engine *e) {
+    if (!e) return;
+    if (e->d.device >= 0) cudaSetDevice(e->d.device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (auto &kv : e->graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (auto &w : e->w)
+        if (w.owned) cudaFree(w.owned);
+    cudaFree(e->kv);
+    cudaFree(e->page_table_dev);
+    if (e->page_table_host) cudaFreeHost(e->page_table_host);
+    cudaFree(e->rope_cos);
+    cudaFree(e->rope_sin);
+    cudaFree(e->x);
+    cudaFree(e->q);
+    cudaFree(e->attn);
+    cudaFree(e->h);
+    cudaFree(e->logits);
+    cudaFree(e->keys);
+    cudaFree(e->next_dev);
+    cudaFree(e->meta_dev);
+    if (e->meta_host) cudaFreeHost(e->meta_host);
+    if (e->next_host) cudaFreeHost(e->next_host);
+    cudaFree(e->attn_partial);
+    cudaFree(e->attn_counters);
+    cudaFree(e->status);
+    cudaFree(e->scratch_key);
+    if (e->ev_start) cudaEventDestroy(e->ev_start);
+    if (e->ev_end) cudaEventDestroy(e->ev_end);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+const char *ijb_last_error(const ijb_engine *e) { return e ? e->err.c_str() : t_create_err.c_str(); }
+
+int ijb_tensor_index(const ijb_engine *e, const char *name) {
+    if (!e || !name) return -1;
+    auto it = e->by_name.find(name);
+    return it == e->by_name.end() ? -1 : it->second;
+}
+
+int ijb_matvec(ijb_engine *e, int ti, const float *x, float *y, int cols, int rows, int batch, void *stream) {
+    try {
+        require(e != nullptr, "null engine");
+        require(ti >= 0 && ti < static_cast<int>(e->w.size()), "bad tensor index");
+        const Weight &w = e->w[ti];
+        require((w.type == kQ4K || w.type == kQ6K) && w.cols == cols && w.rows == rows,
+                "Unexpected quantized matrix shape");
+        require(batch >= 1 && cols <= kMaxCols, "bad batch or cols");
+        cudaStream_t s = pick(e, stream);
+        for (int g0 = 0; g0 < batch; g0 += kMaxBatch) {
+            const int gn = std::min(kMaxBatch, batch - g0);
+            GemvParams p = base_params(e, cols, gn, x + static_cast<long>(g0) * cols, cols, nullptr);
+            add_seg(p, w, nullptr, kEpiStore, y + static_cast<long>(g0) * rows, rows, 0, e->d);
+            launch_gemv(e, p, s, false);
+        }
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_forward(ijb_engine *e, int token, int pos, int need_logits, int *next_token) {
+    try {
+        require(e != nullptr, "null engine");
+        require(pos >= 0 && pos < e->d.context && token >= 0 && token < e->d.vocab,
+                "Token or position outside model context");
+        require(pos <= e->seq_len[0], "position beyond the cached length of the sequence");
+        const int seq = 0;
+        packed_step(e, 1, &seq, &token, &pos, need_logits != 0);
+        e->seq_len[0] = pos + 1;
+        if (next_token) *next_token = need_logits ? e->next_host[0] : -1;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_seq_prefill(ijb_engine *e, int seq, const int *tokens, int n, int *next_token) {
+    try {
+        require(e != nullptr && tokens != nullptr && n >= 1, "bad arguments");
+        require(seq >= 0 && seq < e->d.max_seqs && e->seq_used[seq], "unknown sequence id");
+        const int start = e->seq_len[seq];
+        require(start + n <= e->d.context, "prompt exceeds context", IJB_ERR_CAPACITY);
+        std::vector<int> seqs(e->d.max_batch, seq), pos(e->d.max_batch);
+        for (int c = 0; c < n; c += e->d.max_batch) {
+            const int cn = std::min(e->d.max_batch, n - c);
+            for (int i = 0; i < cn; ++i) pos[i] = start + c + i;
+            const bool last = c + cn == n;
+            packed_step(e, cn, seqs.data(), tokens + c, pos.data(), last);
+            e->seq_len[seq] = start + c + cn;
+            if (last && next_token) *next_token = e->next_host[cn - 1];
+        }
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_prefill(ijb_engine *e, const int *tokens, int n, int *next_token) {
+    if (!e) return IJB_ERR_INVALID;
+    e->seq_len[0] = 0;
+    return ijb_seq_prefill(e, 0, tokens, n, next_token);
+}
+
+int ijb_reset(ijb_engine *e) {
+    if (!e) return IJB_ERR_INVALID;
+    e->seq_len[0] = 0;
+    return IJB_OK;
+}
+
+const float *ijb_logits_dev(const ijb_engine *e) { return e ? e->logits : nullptr; }
+const float *ijb_residual_dev(const ijb_engine *e) { return e ? e->x : nullptr; }
+
+int ijb_seq_open(ijb_engine *e, int *seq_id) {
+    try {
+        require(e != nullptr && seq_id != nullptr, "bad arguments");
+        for (int s = 1; s < e->d.max_seqs; ++s)
+            if (!e->seq_used[s]) {
+                e->seq_used[s] = 1;
+                e->seq_len[s] = 0;
+                *seq_id = s;
+                return IJB_OK;
+            }
+        throw Error(IJB_ERR_CAPACITY, "sequence table full");
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_seq_close(ijb_engine *e, int seq) {
+    try {
+        require(e != nullptr && seq > 0 && seq < e->d.max_seqs && e->seq_used[seq], "unknown sequence id");
+        for (int p : e->seq_pages[seq]) e->free_pages.push_back(p);
+        e->seq_pages[seq].clear();
+        e->seq_len[seq] = 0;
+        e->seq_used[seq] = 0;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_seq_length(const ijb_engine *e, int seq) {
+    if (!e || seq < 0 || seq >= e->d.max_seqs || !e->seq_used[seq]) return -1;
+    return e->seq_len[seq];
+}
+
+int ijb_decode_step(ijb_engine *e, int n, const int *seq_ids, const int *tokens, int *next_tokens) {
+    try {
+        require(e != nullptr && seq_ids != nullptr && tokens != nullptr, "bad arguments");
+        require(n >= 1 && n <= e->d.max_batch, "step size must be 1..max_batch", IJB_ERR_CAPACITY);
+        std::vector<int> pos(n);
+        std::unordered_map<int, int> next_pos;
+        for (int i = 0; i < n; ++i) {
+            const int s = seq_ids[i];
+            require(s >= 0 && s < e->d.max_seqs && e->seq_used[s], "unknown sequence id");
+            auto it = next_pos.find(s);
+            pos[i] = it == next_pos.end() ? e->seq_len[s] : it->second;
+            next_pos[s] = pos[i] + 1;
+        }
+        packed_step(e, n, seq_ids, tokens, pos.data(), true);
+        for (auto &kv : next_pos) e->seq_len[kv.first] = kv.second;
+        if (next_tokens) std::memcpy(next_tokens, e->next_host, n * sizeof(int));
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_argmax(const float *values, int n, int *index, void *stream) {
+    try {
+        require(values && index && n >= 1 && n <= 512 * 256, "bad argmax arguments");
+        static unsigned long long *scratch[64] = {nullptr};
+        static std::mutex mu;
+        int dev = 0;
+        ck(cudaGetDevice(&dev), "cudaGetDevice");
+        require(dev >= 0 && dev < 64, "device ordinal");
+        {
+            std::lock_guard<std::mutex> lock(mu);
+            if (!scratch[dev]) scratch[dev] = dev_alloc<unsigned long long>(1, "argmax scratch");
+        }
+        ck(argmax_launch(values, n, scratch[dev], index, static_cast<cudaStream_t>(stream)), "argmax launch");
+        g_launches += 2;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(nullptr, ex);
+    }
+}
+
+int ijb_dequant(int type, const void *blocks, long n_blocks, float *out, void *stream) {
+    try {
+        require(type == IJB_TYPE_Q4_K || type == IJB_TYPE_Q6_K, "type must be Q4_K or Q6_K");
+        require(blocks && out && n_blocks >= 0, "bad dequant arguments");
+        ck(dequant_launch(type, blocks, n_blocks, out, static_cast<cudaStream_t>(stream)), "dequant launch");
+        ++g_launches;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(nullptr, ex);
+    }
+}
+
+long ijb_q6k_planar_row_bytes(int cols) { return cols > 0 && cols % 256 == 0 ? q6_planar_row_bytes(cols) : -1; }
+
+int ijb_repack_q6k(const void *src, void *dst, int rows, int cols, void *stream) {
+    try {
+        require(src && dst && rows >= 0 && cols > 0 && cols % 256 == 0, "bad repack arguments");
+        ck(repack_q6_launch(src, dst, rows, cols, static_cast<cudaStream_t>(stream)), "repack launch");
+        ++g_launches;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(nullptr, ex);
+    }
+}
+
+int ijb_gemv(int type, const void *w, const float *x, float *y, int cols, int rows, int batch, int use_dp4a,
+             void *stream) {
+    try {
+        require(type == IJB_TYPE_Q4_K || type == IJB_TYPE_Q6_K, "type must be Q4_K or Q6_K");
+        require(w && x && y && rows >= 1 && cols > 0 && cols % 256 == 0 && cols <= kMaxCols, "bad GEMV arguments");
+        require(batch >= 1 && batch <= kMaxBatch, "batch must be 1..8");
+        require(reinterpret_cast<uintptr_t>(w) % 16 == 0, "weights must be 16-byte aligned");
+        int dev = 0, sms = 0;
+        ck(cudaGetDevice(&dev), "cudaGetDevice");
+        ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+        Weight wt;
+        wt.type = type;
+        wt.rows = rows;
+        wt.cols = cols;
+        wt.data = static_cast<const uint8_t *>(w);
+        wt.row_bytes = type == IJB_TYPE_Q4_K ? cols / 256 * kQ4Bytes : static_cast<int>(q6_planar_row_bytes(cols));
+        ijb_model_desc d{};
+        d.use_dp4a = use_dp4a;
+        d.use_q6_dp4a = use_dp4a;
+        GemvParams p;
+        std::memset(&p, 0, sizeof(p));
+        p.cols = cols;
+        p.batch = batch;
+        p.x = x;
+        p.x_stride = cols;
+        add_seg(p, wt, nullptr, kEpiStore, y, rows, 0, d);
+        ck(gemv_launch(p, sms, static_cast<cudaStream_t>(stream), false), "GEMV launch");
+        ++g_launches;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(nullptr, ex);
+    }
+}
+
+uint64_t ijb_kernel_launches(void) { return g_launches.load(); }
+
+float ijb_last_step_ms(const ijb_engine *e) { return e ? e->last_step_ms : -1.f; }
+
+}  // extern "C"

@@ -1,0 +1,190 @@
+// Small kernels around the GEMVs: Q6_K load-time repack, embedding lookup,
+// bit-exact dequantisation, the stand-alone argmax and the argmax-key decode.
+#include "common.cuh"
+#include "gemv.cuh"
+#include "misc.cuh"
+
+namespace ijb {
+
+long q6_planar_row_bytes(int cols) { return q6_unit_row_bytes(cols); }
+
+// GGUF Q6_K row (nb blocks of ql[128] qh[64] scales[16] d[2]) -> the
+// lane-major unit layout described in gemv.cuh.  Bytes are only moved.
+__global__ void repack_q6_kernel(const uint8_t *src, uint8_t *dst, int rows, int nb, long dst_row_bytes) {
+    const long row = blockIdx.x;
+    if (row >= rows) return;
+    const uint8_t *s = src + row * nb * 210;
+    uint8_t *d = dst + row * dst_row_bytes;
+    for (long i = threadIdx.x; i < dst_row_bytes; i += blockDim.x) d[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb * 210; i += blockDim.x) {
+        const int blk = i / 210, o = i % 210;
+        const int u = blk / kUnitBlocks, lb = blk % kUnitBlocks;
+        const int n = min(kUnitBlocks, nb - u * kUnitBlocks), L = 4 * n;
+        const long base = static_cast<long>(u) * q6_unit_bytes(kUnitBlocks);
+        long to;
+        if (o < 128) {  // ql: g = o/64, second column half if o%64 >= 32, h = (o%32)/16
+            const int g = o / 64, half = (o % 64) / 32, h = (o % 32) / 16;
+            const int lane = 4 * lb + 2 * g + h;
+            to = base + (half ? 16 * L : 0) + lane * 16 + (o % 16);
+        } else if (o < 192) {  // qh[g*32 + 16h + j]
+            const int q = o - 128, g = q / 32, h = (q % 32) / 16;
+            to = base + 32 * L + (4 * lb + 2 * g + h) * 16 + (q % 16);
+        } else if (o < 208) {  // scales[g*8 + 2*part + h]
+            const int q = o - 192, g = q / 8, part = (q % 8) / 2, h = q % 2;
+            to = base + 48 * L + (4 * lb + 2 * g + h) * 4 + part;
+        } else {
+            to = base + 52 * L + lb * 2 + (o - 208);
+        }
+        d[to] = s[i];
+    }
+}
+
+// Weight i of block blk of a unit-layout Q6_K row, exactly q6_value
+// (inferencer.cu:473-487): d * scale * q with both products exact in fp32.
+__device__ __forceinline__ float q6_planar_value(const uint8_t *row, int nb, int blk, int i) {
+    const int u = blk / kUnitBlocks, lb = blk % kUnitBlocks;
+    const int n = min(kUnitBlocks, nb - u * kUnitBlocks), L = 4 * n;
+    const uint8_t *unit = row + static_cast<long>(u) * q6_unit_bytes(kUnitBlocks);
+    const int g = i / 128, p = i % 128, part = p / 32, l = p % 32, h = l / 16, j = l % 16;
+    const int lane = 4 * lb + 2 * g + h;
+    int low = unit[((part & 1) ? 16 * L : 0) + lane * 16 + j];
+    low = part < 2 ? (low & 15) : (low >> 4);
+    const int high = (unit[32 * L + lane * 16 + j] >> (part * 2)) & 3;
+    const int q = (low | (high << 4)) - 32;
+    const int sc = static_cast<int8_t>(unit[48 * L + lane * 4 + part]);
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(unit + 52 * L + lb * 2));
+    return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
+}
+
+// embedding_cuda / embedding_batch_cuda (inferencer.cu:806-819) over the
+// planar token_embd; also clears the per-token argmax keys of the step.
+__global__ void embed_kernel(const uint8_t *emb, long row_bytes, int dim, const int *tokens, int n, float *x,
+                             long x_stride, unsigned long long *keys) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.y;
+    if (b >= n) return;
+    const int tok = tokens[b];
+    const int nb = dim / 256;
+    const uint8_t *row = emb + static_cast<long>(tok) * row_bytes;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+        x[b * x_stride + i] = q6_planar_value(row, nb, i / 256, i % 256);
+    if (keys && blockIdx.x == 0 && threadIdx.x == 0) keys[b] = 0ull;
+}
+
+// q4_value (inferencer.cu:454-471): d*sc*q - dmin*m.  d*sc and (d*sc)*q are
+// exact in fp32 (at most 11+6+4 significant bits), so the only rounding is
+// the final subtraction, with or without a fused multiply-add.
+__global__ void dequant_kernel(int type, const uint8_t *blocks, long nblocks, float *out) {
+    const long idx = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x;
+    if (idx >= nblocks * 256) return;
+    const long blk = idx / 256;
+    const int i = static_cast<int>(idx % 256);
+    if (type == kQ4K) {
+        const uint8_t *b = blocks + blk * 144;
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(b));
+        const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t *>(b + 2));
+        const uint8_t *s = b + 4, *qs = b + 16;
+        const int sub = i / 32, qi = (i / 64) * 32 + (i % 32);
+        const int q = (i % 64) < 32 ? (qs[qi] & 15) : (qs[qi] >> 4);
+        int sc, m;
+        if (sub < 4) {
+            sc = s[sub] & 63;
+            m = s[sub + 4] & 63;
+        } else {
+            sc = (s[sub + 4] & 15) | ((s[sub - 4] >> 6) << 4);
+            m = (s[sub + 4] >> 4) | ((s[sub] >> 6) << 4);
+        }
+        out[idx] = __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q)),
+                             __fmul_rn(dmin, static_cast<float>(m)));
+    } else {
+        const uint8_t *b = blocks + blk * 210;
+        const int group = i / 128, p = i % 128, lane = p % 32, part = p / 32;
+        int low = b[group * 64 + (part % 2) * 32 + lane];
+        low = part < 2 ? (low & 15) : (low >> 4);
+        const int high = (b[128 + group * 32 + lane] >> (part * 2)) & 3;
+        const int q = (low | (high << 4)) - 32;
+        const int sc = static_cast<int8_t>(b[192 + group * 8 + part * 2 + lane / 16]);
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(b + 208));
+        out[idx] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
+    }
+}
+
+// Stand-alone argmax with the reference's tie rule (see argmax_key): one
+// pass of atomicMax over packed keys, then a one-thread decode.
+__global__ void argmax_keys_kernel(const float *v, int n, unsigned long long *key) {
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = argmax_key(v[i], i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0 && best) atomicMax(key, best);
+}
+
+// keys[b] -> tokens[b]; zero keys (all logits NaN) decode to -1.
+__global__ void keys_to_tokens_kernel(const unsigned long long *keys, int n, int *tokens) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < n) tokens[b] = keys[b] ? argmax_key_index(keys[b]) : -1;
+}
+
+static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, cudaStream_t stream, bool pdl,
+                                     cudaLaunchAttribute *attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+cudaError_t repack_q6_launch(const void *src, void *dst, int rows, int cols, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    repack_q6_kernel<<<rows, 256, 0, stream>>>(static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst), rows,
+                                               cols / 256, q6_planar_row_bytes(cols));
+    return cudaGetLastError();
+}
+
+cudaError_t embed_launch(const uint8_t *emb, long row_bytes, int dim, const int *tokens, int n, float *x,
+                         long x_stride, unsigned long long *keys, cudaStream_t stream, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3((dim + 255) / 256, n), dim3(256), stream, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, embed_kernel, emb, row_bytes, dim, tokens, n, x, x_stride, keys);
+}
+
+cudaError_t dequant_launch(int type, const void *blocks, long nblocks, float *out, cudaStream_t stream) {
+    const long total = nblocks * 256;
+    if (total <= 0) return cudaSuccess;
+    dequant_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        type, static_cast<const uint8_t *>(blocks), nblocks, out);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch, int *index, cudaStream_t stream) {
+    cudaError_t e = cudaMemsetAsync(key_scratch, 0, sizeof(unsigned long long), stream);
+    if (e != cudaSuccess) return e;
+    int blocks = (n + 255) / 256;
+    if (blocks > 1024) blocks = 1024;
+    argmax_keys_kernel<<<blocks, 256, 0, stream>>>(v, n, key_scratch);
+    keys_to_tokens_kernel<<<1, 32, 0, stream>>>(key_scratch, 1, index);
+    return cudaGetLastError();
+}
+
+cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *tokens, cudaStream_t stream,
+                                  bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3((n + 127) / 128), dim3(128), stream, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, keys_to_tokens_kernel, keys, n, tokens);
+}
+
+}  // namespace ijb

@@ -1,0 +1,16 @@
+// Launchers of the small kernels (misc.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ijb {
+
+long q6_planar_row_bytes(int cols);
+cudaError_t repack_q6_launch(const void *src, void *dst, int rows, int cols, cudaStream_t stream);
+cudaError_t embed_launch(const uint8_t *emb, long row_bytes, int dim, const int *tokens, int n, float *x,
+                         long x_stride, unsigned long long *keys, cudaStream_t stream, bool pdl);
+cudaError_t dequant_launch(int type, const void *blocks, long nblocks, float *out, cudaStream_t stream);
+cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch, int *index, cudaStream_t stream);
+cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *tokens, cudaStream_t stream, bool pdl);
+
+}  // namespace ijb

@@ -60,6 +60,7 @@ def lib():
         L.orc_model_set_global.argtypes = [P, P, P, i32, P]
         L.orc_model_set_layer.argtypes = [P, i32, P, P, P, P, P, i32, P, P, P, P, i32]
         L.orc_model_destroy.argtypes = [P]
+        L.orc_model_set_kv_fp16.argtypes = [P, i32]
         L.orc_state_create.argtypes = [P]
         L.orc_state_create.restype = P
         L.orc_state_destroy.argtypes = [P]
@@ -67,6 +68,7 @@ def lib():
         L.orc_state_logits.restype = ctypes.POINTER(ctypes.c_float)
         L.orc_state_residual.argtypes = [P]
         L.orc_state_residual.restype = ctypes.POINTER(ctypes.c_float)
+        L.orc_state_fill_kv.argtypes = [P, i32]
         L.orc_forward.argtypes = [P, i32, i32, i32, P]
         L.orc_forward.restype = i32
         _lib = L
@@ -180,17 +182,19 @@ class OracleModel:
     """A Llama-shaped model over GGUF-layout host weights, run one token at a
     time exactly as FastRunner::forward (inferencer.cu:1424-1531) does, with a
     fp32 [layer][ctx][kv_dim] KV cache per sequence (inferencer.cu:1132).
+    ``kv_fp16`` rounds cached K/V to binary16, the B200 build's cache format.
 
     ``weights`` is the dict produced by ``ijb200.synth.make_model`` (raw GGUF
     bytes per tensor name)."""
 
-    def __init__(self, cfg, weights, context, use_dp4a=True, use_q6_dp4a=True, contract=1):
+    def __init__(self, cfg, weights, context, use_dp4a=True, use_q6_dp4a=True, contract=1, kv_fp16=False):
         self.cfg = cfg
         self.w = weights  # keeps the arrays alive
         L = lib()
         self._m = L.orc_model_create(cfg.dim, cfg.layers, cfg.heads, cfg.kv_heads, cfg.hidden,
                                      cfg.vocab, context, cfg.eps, cfg.rope_base, int(use_dp4a),
                                      int(use_q6_dp4a), contract)
+        L.orc_model_set_kv_fp16(self._m, int(kv_fp16))
         self._keep = []
 
         def P(name):
@@ -234,6 +238,10 @@ class OracleState:
         if r == -2:
             raise ValueError("Token or position outside model context")
         return (r, tr) if trace else r
+
+    def fill_kv(self, length: int) -> None:
+        """Timing helper: stands in for a prefilled context of `length`."""
+        lib().orc_state_fill_kv(self._s, int(length))
 
     def logits(self):
         v = self.model.cfg.vocab

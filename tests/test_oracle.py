@@ -1,0 +1,179 @@
+"""The CPU oracle pinned against the reference: golden vectors captured from
+the reference's own kernels on a B200 (tests/golden/ref_kernels.npz) and the
+independent gguf package dequantiser."""
+import numpy as np
+import pytest
+
+import oracle as O
+from ijb200 import synth
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("name,qtype", [("q4_edge", 12), ("q6_edge", 14), ("q4_rand", 12), ("q6_rand", 14)])
+def test_dequant_bit_exact_vs_reference(golden, golden_inputs, name, qtype):
+    for contract in (0, 1):
+        got = O.dequant(qtype, golden_inputs[name], contract)
+        np.testing.assert_array_equal(bits(got), bits(golden["ref_dequant_" + name]))
+
+
+def test_dequant_bit_exact_vs_gguf():
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants, GGMLQuantizationType as T
+    rng = np.random.default_rng(5)
+    for qtype, gt, blocks in ((12, T.Q4_K, synth.q4k_blocks(rng, 128)), (14, T.Q6_K, synth.q6k_blocks(rng, 128))):
+        ref = quants.dequantize(blocks.reshape(-1), gt).reshape(-1).astype(np.float32)
+        np.testing.assert_array_equal(bits(O.dequant(qtype, blocks)), bits(ref))
+
+
+@pytest.mark.parametrize("xname", ["x2048", "x8192"])
+def test_quantize_bit_exact_vs_reference(golden, golden_inputs, xname):
+    xq, xs = O.quantize_x32(golden_inputs[xname])
+    np.testing.assert_array_equal(xq, golden["ref_xq_" + xname])
+    np.testing.assert_array_equal(bits(xs), bits(golden["ref_xscale_" + xname]))
+    assert xs[0] == 1.0 if xname == "x8192" else True  # an all-zero group keeps scale 1
+
+
+@pytest.mark.parametrize("wname,qtype,cols,rows,xname", [
+    ("w4", 12, 2048, 64, "x2048"), ("w6", 14, 2048, 64, "x2048"), ("w6k8192", 14, 8192, 16, "x8192")])
+def test_gemv_bit_exact_vs_reference(golden, golden_inputs, wname, qtype, cols, rows, xname):
+    """With the reference build's multiply-add contractions (contract=1) the
+    oracle reproduces FastGPU::matvec bit for bit in both activation paths."""
+    w, x = golden_inputs[wname], golden_inputs[xname]
+    xq, xs = O.quantize_x32(x)
+    np.testing.assert_array_equal(bits(O.gemv_dp4a(qtype, w, xq, xs, cols, rows, 1)),
+                                  bits(golden[f"ref_matvec_{wname}_dp4a"]))
+    np.testing.assert_array_equal(bits(O.gemv_f32(qtype, w, x, cols, rows, 1)),
+                                  bits(golden[f"ref_matvec_{wname}_f32"]))
+    # the un-contracted restatement stays within float rounding of it
+    ref = golden[f"ref_matvec_{wname}_f32"]
+    got = O.gemv_f32(qtype, w, x, cols, rows, 0)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
+
+
+@pytest.mark.parametrize("n", [2048, 3072])
+def test_rmsnorm_vs_reference(golden, golden_inputs, n):
+    """rsqrtf is not reproduced on the CPU (1/sqrtf is used): outputs agree to
+    a couple of ulp of the shared scale."""
+    got = O.rmsnorm(golden_inputs["norm_x"][:n], golden_inputs["norm_w"][:n], 1e-5)
+    ref = golden[f"ref_rmsnorm_{n}"]
+    np.testing.assert_allclose(got, ref, rtol=3e-7, atol=0)
+
+
+@pytest.mark.parametrize("pos", [0, 37, 63])
+def test_attention_vs_reference(golden, golden_inputs, pos):
+    d = golden_inputs
+    got = O.attention(d["att_q"], d["att_k"].reshape(64, 1024), d["att_v"].reshape(64, 1024), pos, 24, 8, 128)
+    ref = golden[f"ref_attention_pos{pos}"]
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["argmax_rand", "argmax_tie", "argmax_flat"])
+def test_argmax_vs_reference(golden, golden_inputs, name):
+    assert O.argmax(golden_inputs[name]) == int(golden["ref_" + name][0])
+
+
+def _tournament(v):
+    """Python statement of argmax_blocks_cuda + argmax_final_cuda's trees."""
+    n = len(v)
+    nb = (n + 255) // 256
+    bv, bi = [], []
+    for b in range(nb):
+        vals = [v[b * 256 + l] if b * 256 + l < n else -np.inf for l in range(256)]
+        idx = [b * 256 + l for l in range(256)]
+        s = 128
+        while s:
+            for l in range(s):
+                if vals[l + s] > vals[l]:
+                    vals[l], idx[l] = vals[l + s], idx[l + s]
+            s //= 2
+        bv.append(vals[0]); bi.append(idx[0])
+    bv += [-np.inf] * (512 - nb); bi += [2**31 - 1] * (512 - nb)
+    s = 256
+    while s:
+        for i in range(s):
+            if bv[i + s] > bv[i]:
+                bv[i], bi[i] = bv[i + s], bi[i + s]
+        s //= 2
+    return bi[0]
+
+
+def _bitrev_rule(v):
+    m = np.max(v)
+    cand = np.nonzero(v == m)[0]
+    key = lambda j: (int(f"{j >> 8:09b}"[::-1], 2), int(f"{j & 255:08b}"[::-1], 2))
+    return int(min(cand, key=key))
+
+
+@pytest.mark.parametrize("ties", [[3, 5], [256 + 7, 512 + 7], [3, 5, 256, 512], [1000, 2000, 3000, 4000],
+                                  [255, 254, 128], list(range(0, 4096, 17))])
+def test_argmax_tie_rule(ties):
+    v = np.random.default_rng(len(ties)).standard_normal(4096).astype(np.float32)
+    v[ties] = 9.0
+    assert O.argmax(v) == _tournament(list(v)) == _bitrev_rule(v)
+
+
+def test_rope_tables_match_float_formula():
+    c, s = O.rope_tables(64, 64, 500000.0)
+    freq = np.power(np.float32(500000.0), (np.float32(-2.0) * np.arange(32, dtype=np.float32)) / np.float32(64))
+    ang = (np.arange(64, dtype=np.float32)[:, None] * freq[None, :]).astype(np.float32)
+    # numpy's float32 pow/cos differ from libm's powf/cosf by a few ulp of
+    # angles up to ~64 rad
+    np.testing.assert_allclose(c, np.cos(ang), atol=2e-5)
+    np.testing.assert_allclose(s, np.sin(ang), atol=2e-5)
+
+
+def test_model_activation_range():
+    """Random-init weights keep activations, K and V well inside fp16 range."""
+    cfg = synth.TINY
+    m = O.OracleModel(cfg, synth.make_model(cfg, 0), 64)
+    st = m.new_state()
+    for i, t in enumerate(synth.prompt_tokens(24, 1, cfg.vocab)):
+        _, tr = st.forward(int(t), i, True, trace=True)
+        assert np.abs(tr).max() < 1e3
+    lg = st.logits()
+    assert np.isfinite(lg).all() and 0.5 < lg.std() < 50
+
+
+def test_oracle_threads_deterministic():
+    rng = np.random.default_rng(3)
+    w = synth.quant_matrix(rng, 12, 512, 2048)
+    x = rng.standard_normal(2048).astype(np.float32)
+    O.set_threads(1)
+    a = O.matvec(12, w, x, 2048, 512)
+    O.set_threads(4)
+    b = O.matvec(12, w, x, 2048, 512)
+    O.set_threads(1)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_forward_rejects_bad_position():
+    cfg = synth.TINY
+    m = O.OracleModel(cfg, synth.make_model(cfg, 0), 16)
+    st = m.new_state()
+    with pytest.raises(ValueError):
+        st.forward(0, 16)
+    with pytest.raises(ValueError):
+        st.forward(cfg.vocab, 0)
+
+
+def test_dp4a_path_noise_floor():
+    """The reference's INT8 path is sensitive to ulp-level changes: two oracle
+    variants that differ only in multiply-add contraction give logits ~1%
+    apart (same greedy tokens), while the FP32 path stays within 1e-4.  This
+    floor sets the DP4A-mode full-model bar of the GPU tests."""
+    cfg = synth.TINY_HD128
+    w = synth.make_model(cfg, 11)
+    prompt = synth.prompt_tokens(40, 1, cfg.vocab)
+    for dp4a, lo, hi in ((True, 3e-3, 2e-2), (False, 0.0, 1e-4)):
+        a = O.OracleModel(cfg, w, 64, dp4a, dp4a, contract=1).new_state()
+        b = O.OracleModel(cfg, w, 64, dp4a, dp4a, contract=0).new_state()
+        for i, t in enumerate(prompt):
+            ta = a.forward(int(t), i, True)
+            tb = b.forward(int(t), i, True)
+        la, lb = a.logits(), b.logits()
+        err = np.linalg.norm(la - lb) / np.linalg.norm(la)
+        assert lo <= err < hi, (dp4a, err)
+        assert ta == tb
