@@ -56,3 +56,16 @@ def test_null_arguments_are_errors_not_crashes():
     assert L.ijb_decode_step(None, 1, None, None, None) == lib.ERR_INVALID
     assert L.ijb_seq_length(None, 0) == -1
     assert L.ijb_last_error(None) is not None
+
+
+def test_cpp_shim_compiles():
+    """The FastRunner-signature shim over the C ABI compiles as C++17."""
+    import os
+    import shutil
+    import subprocess
+    gxx = shutil.which("g++")
+    if not gxx:
+        pytest.skip("no g++")
+    hdr = os.path.join(lib.PKG_ROOT, "host", "fast_runner.hpp")
+    r = subprocess.run([gxx, "-std=c++17", "-fsyntax-only", "-x", "c++", hdr], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
