@@ -162,6 +162,23 @@ int ijb_repack_q6k(const void *src_dev, void *dst_dev, int rows, int cols, void 
 int ijb_gemv(int type, const void *w_dev, const float *x_dev, float *y_dev, int cols, int rows, int batch,
              int use_dp4a, void *stream);
 
+/* The same argmax as ijb_argmax, for callers that cannot allocate device
+ * memory: code running while a CUDA graph is captured (allocation is not
+ * allowed there), host loops that cannot take the device synchronisation an
+ * allocation may cause, frameworks that own all device memory through their
+ * own allocator.  ijb_argmax allocates an 8-byte scratch key on its first
+ * call on a device; this entry point allocates nothing.  It computes one
+ * winner per 256 values into a fixed 512-slot array in device memory that the
+ * library holds on every GPU that loads it (4 KB), then the winner of those:
+ * n must be 1..131072 (512 x 256), larger n is rejected with IJB_ERR_INVALID.
+ * Its first call on a device looks up that array's device address (no
+ * allocation); make that first call before any stream capture.  Every call
+ * writes the slots it reads, so nothing carries over between calls, but all
+ * calls share the one array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.  Asynchronous
+ * on `stream`.  No counterpart in the reference. */
+int ijb_argmax_noalloc(const float *values_dev, int n, int *index_dev, void *stream);
+
 /* Number of kernels the library launched since load (for launch accounting). */
 uint64_t ijb_kernel_launches(void);
 

@@ -120,8 +120,15 @@ struct ijb_engine {
 };
 
 namespace {
-
 thread_local std::string t_create_err;
+}  // namespace
+
+namespace ijb {
+void set_thread_error(const std::string &msg) { t_create_err = msg; }
+void count_launches(uint64_t n) { g_launches += n; }
+}  // namespace ijb
+
+namespace {
 
 int fail(ijb_engine *e, const std::exception &ex) {
     const Error *er = dynamic_cast<const Error *>(&ex);

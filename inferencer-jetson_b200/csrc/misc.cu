@@ -1,5 +1,9 @@
 // Small kernels around the GEMVs: Q6_K load-time repack, embedding lookup,
 // bit-exact dequantisation, the stand-alone argmax and the argmax-key decode.
+#include <mutex>
+#include <string>
+
+#include "../../include/ijb200.h"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
@@ -187,4 +191,109 @@ cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *to
     return cudaLaunchKernelEx(&cfg, keys_to_tokens_kernel, keys, n, tokens);
 }
 
+// ------------------------------------------- argmax without allocation --
+//
+// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
+// being captured (allocation is not allowed inside a capture), host loops
+// that cannot afford the device synchronisation an allocation may cause, and
+// frameworks whose device memory is owned by their own allocator.
+// ijb_argmax allocates its 8-byte scratch key the first time it runs on a
+// device; ijb_argmax_noalloc below allocates nothing.  It keeps the
+// reference's two-pass structure (argmax_blocks_cuda, argmax_final_cuda,
+// inferencer.cu:1063-1099): one winner per 256 values, then one over the
+// winners, with the winners in a fixed array in device memory that the
+// library holds on every GPU that loads it.
+
+constexpr int kNoAllocArgmaxSlots = 512;  // 512 winners x 256 values = the reference's 131072 limit
+static __device__ __align__(256) unsigned long long g_argmax_slots[kNoAllocArgmaxSlots];
+
+// Pass 1: CTA b writes the best packed key of values [256b, 256b + 256).
+__global__ void argmax_slots_kernel(const float *v, int n, unsigned long long *slots) {
+    __shared__ unsigned long long warp_best[8];
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    unsigned long long best = i < n ? argmax_key(v[i], i) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < 8; ++w) b = warp_best[w] > b ? warp_best[w] : b;
+        slots[blockIdx.x] = b;
+    }
+}
+
+// Pass 2: one CTA reduces the winners and writes the index (-1 if every
+// value was NaN).
+__global__ void argmax_slots_final_kernel(const unsigned long long *slots, int nslots, int *index) {
+    __shared__ unsigned long long warp_best[kNoAllocArgmaxSlots / 32];
+    unsigned long long best = static_cast<int>(threadIdx.x) < nslots ? slots[threadIdx.x] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kNoAllocArgmaxSlots / 32; ++w) b = warp_best[w] > b ? warp_best[w] : b;
+        *index = b ? argmax_key_index(b) : -1;
+    }
+}
+
+// Device address of g_argmax_slots on each device, looked up once per device
+// with that device current (host code must not use the symbol's name as a
+// device pointer).
+static unsigned long long *g_slots_addr[64] = {nullptr};
+static std::mutex g_slots_mu;
+
+static cudaError_t slots_address(unsigned long long **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_slots_mu);
+    if (!g_slots_addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_argmax_slots);
+        if (e != cudaSuccess) return e;
+        g_slots_addr[dev] = static_cast<unsigned long long *>(p);
+    }
+    *out = g_slots_addr[dev];
+    return cudaSuccess;
+}
+
 }  // namespace ijb
+
+extern "C" int ijb_argmax_noalloc(const float *values_dev, int n, int *index_dev, void *stream) {
+    using namespace ijb;
+    if (!values_dev || !index_dev) {
+        set_thread_error("ijb_argmax_noalloc: null pointer");
+        return IJB_ERR_INVALID;
+    }
+    if (n < 1 || n > kNoAllocArgmaxSlots * 256) {
+        set_thread_error("ijb_argmax_noalloc: n = " + std::to_string(n) + " is outside 1.." +
+                         std::to_string(kNoAllocArgmaxSlots * 256) + " (the static scratch holds " +
+                         std::to_string(kNoAllocArgmaxSlots) + " partial winners of 256 values)");
+        return IJB_ERR_INVALID;
+    }
+    unsigned long long *slots = nullptr;
+    cudaError_t e = slots_address(&slots);
+    if (e == cudaSuccess) {
+        const int nslots = (n + 255) / 256;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        argmax_slots_kernel<<<nslots, 256, 0, s>>>(values_dev, n, slots);
+        argmax_slots_final_kernel<<<1, kNoAllocArgmaxSlots, 0, s>>>(slots, nslots, index_dev);
+        e = cudaGetLastError();
+        count_launches(2);
+    }
+    if (e != cudaSuccess) {
+        set_thread_error(std::string("ijb_argmax_noalloc: ") + cudaGetErrorString(e));
+        return IJB_ERR_CUDA;
+    }
+    return IJB_OK;
+}

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace ijb {
 
 long q6_planar_row_bytes(int cols);
@@ -11,6 +13,11 @@ cudaError_t embed_launch(const uint8_t *emb, long row_bytes, int dim, const int 
                          long x_stride, unsigned long long *keys, cudaStream_t stream, bool pdl);
 cudaError_t dequant_launch(int type, const void *blocks, long nblocks, float *out, cudaStream_t stream);
 cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch, int *index, cudaStream_t stream);
+// Error message of the last failed engine-less call on this thread
+// (ijb_last_error(NULL)), and the library's kernel launch counter.
+void set_thread_error(const std::string &msg);
+void count_launches(uint64_t n);
+
 cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *tokens, cudaStream_t stream, bool pdl);
 
 }  // namespace ijb

@@ -70,6 +70,7 @@ def load():
         "ijb_decode_step": ([P, I, IP, IP, IP], I),
         "ijb_seq_prefill": ([P, I, IP, I, IP], I),
         "ijb_argmax": ([P, I, P, P], I),
+        "ijb_argmax_noalloc": ([P, I, P, P], I),
         "ijb_dequant": ([I, P, L64, P, P], I),
         "ijb_q6k_planar_row_bytes": ([I], L64),
         "ijb_repack_q6k": ([P, P, I, I, P], I),
