@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--workload", choices=["ragged64", "decode1", "gemv_q4k", "gemv_q6k"], default="ragged64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=512, help="decode1 prompt length")
+    ap.add_argument("--prompt-max", type=int, default=1024,
+                    help="ragged64 longest prompt (1024 in the BASELINE config; smaller for profiling captures)")
     return ap.parse_args()
 
 
@@ -154,8 +156,9 @@ def barrier(world):
 class RaggedServer:
     """64 live sequences; replaces finished ones from the request stream."""
 
-    def __init__(self, eng, batch, seed, vocab_limit=128000):
+    def __init__(self, eng, batch, seed, vocab_limit=128000, prompt_max=1024):
         self.eng = eng
+        self.prompt_max = prompt_max
         self.batch = batch
         self.rng = np.random.default_rng(seed)
         self.vocab_limit = vocab_limit
@@ -166,7 +169,7 @@ class RaggedServer:
             self.live.append(self._admit())
 
     def _admit(self):
-        plen = int(self.rng.integers(16, 1025))
+        plen = int(self.rng.integers(16, self.prompt_max + 1))
         target = int(self.rng.integers(32, 257))
         prompt = self.rng.integers(0, self.vocab_limit, size=plen).astype(np.int32)
         s = self.eng.seq_open()
@@ -301,7 +304,7 @@ def run_ours(args):
     if args.workload == "ragged64":
         batch, context = 64, 1024 + 256 + 16
         eng = Engine(cfg, weights, context=context, max_batch=batch, max_seqs=batch + 1, device=local)
-        server = RaggedServer(eng, batch, seed=1000 + rank)
+        server = RaggedServer(eng, batch, seed=1000 + rank, prompt_max=args.prompt_max)
     else:
         batch, context = 1, args.prompt + 16 + args.steps + args.warmup + 8
         eng = Engine(cfg, weights, context=context, max_batch=1, max_seqs=2, device=local)
@@ -377,7 +380,7 @@ def run_ours(args):
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xq4/q6 dp4a, fp32 accumulate, fp16 KV", "data": "synthetic (random-init weights, seeded)",
-            "config": {"workload": "llama-3.2-1b Q4_K_M ragged decode, 64 seqs, prompts U[16,1024], "
+            "config": {"workload": f"llama-3.2-1b Q4_K_M ragged decode, 64 seqs, prompts U[16,{args.prompt_max}], "
                                    "outputs U[32,256], replacement" if args.workload == "ragged64"
                        else f"llama-3.2-1b Q4_K_M decode, batch 1, {args.prompt}-token prompt",
                        "batch_per_gpu": batch, "page_size": 16, "kv": "fp16 paged",

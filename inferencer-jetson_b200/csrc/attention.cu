@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     __shared__ __align__(16) float wo[kAttnWarps][G][HD];
     __shared__ __align__(8) uint64_t bar[kAttnWarps];
     __shared__ int is_last;
+    __shared__ uint32_t cta_abort;
 
     pdl_trigger();
     pdl_wait();
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const bool has = t0 < p1;
     const long head_off = static_cast<long>(kvh) * p.page_size * HD;
 
+    if (threadIdx.x == 0) cta_abort = 0u;  // read only after the __syncthreads below
     if (lane == 0) {
         mbar_init(&bar[warp], 1);
         fence_barrier_init();
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         for (int j = 0; j < DPL; ++j) o[g][j] = 0.f;
     }
     if (has) {
-        mbar_wait_bounded(&bar[warp], 0, p.status);
+        mbar_wait_bounded(&bar[warp], 0, p.status, &cta_abort);
         // ---- scores: lane -> position t0 + lane
         const int t = t0 + lane;
         float s[G];

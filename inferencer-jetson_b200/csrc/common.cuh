@@ -62,22 +62,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the barrier phase with the given parity.  Gives up after
-// kWaitLimitNs, records kDevErrWaitTimeout in *status and returns false.
-// Each poll suspends the thread for up to 1 ms; the clock and the status word
-// (a global load) are only consulted every 16 polls, so a wait that ends
-// normally costs no memory round trip.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *status) {
+// kWaitLimitNs: records kDevErrWaitTimeout in the launch's device status word
+// and raises `cta_abort` (a flag in the CTA's shared memory, zeroed at kernel
+// start), after which every later wait of the CTA returns at once, so a CTA
+// that lost one wait ends within one time limit.  Each poll suspends the
+// thread for up to 1 ms; the clock and the flag are read every 16 polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                                  volatile uint32_t *cta_abort) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (*cta_abort) return false;
     uint64_t start = 0;
     for (uint32_t n = 1;; ++n) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((n & 15u) == 0) {
+            if (*cta_abort) return false;
             const uint64_t now = global_timer_ns();
             if (start == 0) {
                 start = now;
-                // once any wait of this launch has given up, later waits return at once
-                if (status && (*reinterpret_cast<volatile uint32_t *>(status) & kDevErrWaitTimeout)) return false;
             } else if (now - start > kWaitLimitNs) {
+                *cta_abort = 1u;
                 if (status) atomicOr(status, kDevErrWaitTimeout);
                 return false;
             }

@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
+#include "mma_gemm.cuh"
 
 namespace ijb {
 
@@ -53,14 +54,17 @@ struct Weight {
     std::string name;
     int type = 0;
     int rows = 0, cols = 0;
-    const uint8_t *data = nullptr;  // usable layout (Q4_K GGUF, Q6_K planar, F32)
+    const uint8_t *data = nullptr;  // usable layout (Q4_K GGUF, Q6_K unit layout, F32)
     int row_bytes = 0;
     void *owned = nullptr;
+    bool has_mma = false;  // TMA descriptors for the tensor-core path
+    MmaWeight mma;
 };
 
 struct StepGraph {
     cudaGraphExec_t exec = nullptr;
     bool need_logits = true;
+    uint64_t launches = 0;  // kernels in the graph
 };
 
 }  // namespace ijb
@@ -107,6 +111,12 @@ struct ijb_engine {
     int *next_host = nullptr;  // pinned
     float *attn_partial = nullptr;
     int *attn_counters = nullptr;
+    uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
+    float *x_inv = nullptr;
+    float *mma_partial = nullptr;  // split-K partials of the tensor-core path
+    int *mma_counters = nullptr;
+    long mma_partial_floats = 0;
+    int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
     uint32_t *status = nullptr;
     unsigned long long *scratch_key = nullptr;
@@ -193,13 +203,115 @@ void launch_gemv(ijb_engine *e, const GemvParams &p, cudaStream_t s, bool pdl) {
     ++g_launches;
 }
 
+// One projection (the segments of `seg_fn`) over tokens [g0, g0+gn): the
+// tensor-core GEMM for 16..64 tokens, the CUDA-core GEMV in groups of 8 below.
+struct ProjSeg {
+    int w0, w1, epi;
+    float *out;
+    long out_stride;
+};
+
+void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const float *x, long x_stride,
+                       const float *norm_w, const ProjSeg *segs, int nsegs, char *kbase, long v_off) {
+    const ijb_model_desc &d = e->d;
+    const int *tpos = e->meta_dev + 2 * d.max_batch;
+    const int *tslot = e->meta_dev + 3 * d.max_batch;
+    bool mma_ok = gn >= e->mma_min_batch;
+    int dp = -1;
+    for (int i = 0; i < nsegs && mma_ok; ++i) {
+        const Weight &w = e->w[segs[i].w0];
+        const int sdp = w.type == kQ4K ? d.use_dp4a : d.use_q6_dp4a;
+        if (dp < 0) dp = sdp;
+        // a weight's TMA boxes are 64 rows when it is half of a gate/up tile
+        const int want_rows = segs[i].w1 >= 0 ? 64 : 128;
+        mma_ok = w.has_mma && w.mma.rows_per_box == want_rows && sdp == dp &&
+                 (segs[i].w1 < 0 || (e->w[segs[i].w1].has_mma && e->w[segs[i].w1].mma.rows_per_box == 64));
+    }
+    const int cols = e->w[segs[0].w0].cols;
+    if (mma_ok) {
+        for (int t0 = 0; t0 < gn; t0 += kMmaMaxN) {
+            const int tn = std::min(kMmaMaxN, gn - t0);
+            const int n_pad = (tn + 15) / 16 * 16;
+            ck(mma_prep_launch(x + static_cast<long>(t0) * x_stride, x_stride, norm_w, d.eps, cols, tn, n_pad, dp,
+                               e->x16, e->x_inv, s),
+               "activation prep launch");
+            MmaParams m;
+            std::memset(&m, 0, sizeof(m));
+            for (int i = 0; i < nsegs; ++i) {
+                const Weight &w0 = e->w[segs[i].w0];
+                MmaSeg &sg = m.seg[m.nseg];
+                m.w[2 * i] = w0.mma;
+                sg.w0 = 2 * i;
+                sg.w1 = -1;
+                if (segs[i].w1 >= 0) {
+                    m.w[2 * i + 1] = e->w[segs[i].w1].mma;
+                    sg.w1 = 2 * i + 1;
+                }
+                sg.type = w0.type;
+                sg.rows = w0.rows;
+                sg.tile0 = m.total_tiles;
+                sg.ntiles = sg.w1 >= 0 ? (w0.rows + 63) / 64 : (w0.rows + kMmaTileM - 1) / kMmaTileM;
+                sg.epi = segs[i].epi;
+                sg.out = segs[i].out ? segs[i].out + static_cast<long>(g0 + t0) * segs[i].out_stride : nullptr;
+                sg.out_stride = segs[i].out_stride;
+                sg.row_offset = 0;
+                m.total_tiles += sg.ntiles;
+                ++m.nseg;
+            }
+            m.cols = cols;
+            m.batch = tn;
+            m.n_pad = n_pad;
+            m.x16 = e->x16;
+            m.x_inv = e->x_inv;
+            m.rope_cos = e->rope_cos;
+            m.rope_sin = e->rope_sin;
+            m.half_head = e->head_dim / 2;
+            m.tok_pos = tpos + g0 + t0;
+            m.tok_slot = tslot + g0 + t0;
+            m.k_cache = kbase;
+            m.v_cache = kbase ? kbase + v_off * e->kv_elem : nullptr;
+            m.kv_f32 = e->kv_f32;
+            m.kv_heads = d.kv_heads;
+            m.head_dim = e->head_dim;
+            m.page_size = d.page_size;
+            m.page_stride = e->page_stride;
+            m.argmax_keys = e->keys + g0 + t0;
+            m.status = e->status;
+            m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->num_sms, &m.bps);
+            if (m.ksplit > 1 && (static_cast<long>(m.total_tiles) * m.ksplit * n_pad * 128 > e->mma_partial_floats ||
+                                 m.total_tiles > kMmaCounters)) {
+                m.ksplit = 1;  // no room for the partials: one part per tile
+                m.bps = cols / 256;
+            }
+            m.partial = e->mma_partial;
+            m.counters = e->mma_counters;
+            ck(mma_gemm_launch(m, e->num_sms, s), "tensor-core GEMM launch");
+            g_launches += 2;
+        }
+        return;
+    }
+    for (int q0 = 0; q0 < gn; q0 += kMaxBatch) {
+        const int qn = std::min(kMaxBatch, gn - q0);
+        GemvParams p = base_params(e, cols, qn, x + static_cast<long>(q0) * x_stride, x_stride, norm_w);
+        p.tok_pos = tpos + g0 + q0;
+        p.tok_slot = tslot + g0 + q0;
+        p.k_cache = kbase;
+        p.v_cache = kbase ? kbase + v_off * e->kv_elem : nullptr;
+        p.argmax_keys = e->keys + g0 + q0;
+        for (int i = 0; i < nsegs; ++i)
+            add_seg(p, e->w[segs[i].w0], segs[i].w1 >= 0 ? &e->w[segs[i].w1] : nullptr, segs[i].epi,
+                    segs[i].out ? segs[i].out + static_cast<long>(g0 + q0) * segs[i].out_stride : nullptr,
+                    segs[i].out_stride, 0, d);
+        launch_gemv(e, p, s, true);
+    }
+}
+
 // Every kernel of one packed step over n tokens (meta already on the device).
 void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
     const ijb_model_desc &d = e->d;
     const int *tok = e->meta_dev;
     const int *tseq = e->meta_dev + d.max_batch;
     const int *tpos = e->meta_dev + 2 * d.max_batch;
-    const int *tslot = e->meta_dev + 3 * d.max_batch;
     const Weight &emb = e->w[e->token_embd];
     ck(embed_launch(emb.data, emb.row_bytes, d.dim, tok, n, e->x, d.dim, e->keys, s, e->pdl), "embedding launch");
     ++g_launches;
@@ -208,19 +320,12 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
     for (int l = 0; l < d.layers; ++l) {
         const auto &L = e->layers[l];
         char *kbase = static_cast<char *>(e->kv) + l * layer_pool * e->kv_elem;
-        // tokens go through the CUDA-core GEMV in groups of at most kMaxBatch
-        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
-            const int gn = std::min(kMaxBatch, n - g0);
-            GemvParams p = base_params(e, d.dim, gn, e->x + static_cast<long>(g0) * d.dim, d.dim,
-                                       reinterpret_cast<const float *>(e->w[L.attn_norm].data));
-            p.tok_pos = tpos + g0;
-            p.tok_slot = tslot + g0;
-            p.k_cache = kbase;
-            p.v_cache = kbase + v_off * e->kv_elem;
-            add_seg(p, e->w[L.q], nullptr, kEpiRopeQ, e->q + static_cast<long>(g0) * d.dim, d.dim, 0, d);
-            add_seg(p, e->w[L.k], nullptr, kEpiRopeKCache, nullptr, 0, 0, d);
-            add_seg(p, e->w[L.v], nullptr, kEpiVCache, nullptr, 0, 0, d);
-            launch_gemv(e, p, s, true);
+        {
+            const ProjSeg segs[3] = {{L.q, -1, kEpiRopeQ, e->q, d.dim},
+                                     {L.k, -1, kEpiRopeKCache, nullptr, 0},
+                                     {L.v, -1, kEpiVCache, nullptr, 0}};
+            launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), segs,
+                              3, kbase, v_off);
         }
         AttnParams a;
         std::memset(&a, 0, sizeof(a));
@@ -249,36 +354,25 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
         a.status = e->status;
         ck(attention_launch(a, s, e->pdl), "attention launch");
         ++g_launches;
-        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
-            const int gn = std::min(kMaxBatch, n - g0);
-            GemvParams p = base_params(e, d.dim, gn, e->attn + static_cast<long>(g0) * d.dim, d.dim, nullptr);
-            add_seg(p, e->w[L.o], nullptr, kEpiAdd, e->x + static_cast<long>(g0) * d.dim, d.dim, 0, d);
-            launch_gemv(e, p, s, true);
+        {
+            const ProjSeg segs[1] = {{L.o, -1, kEpiAdd, e->x, d.dim}};
+            launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, segs, 1, nullptr, 0);
         }
-        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
-            const int gn = std::min(kMaxBatch, n - g0);
-            GemvParams p = base_params(e, d.dim, gn, e->x + static_cast<long>(g0) * d.dim, d.dim,
-                                       reinterpret_cast<const float *>(e->w[L.ffn_norm].data));
-            add_seg(p, e->w[L.gate], &e->w[L.up], kEpiSiluPair, e->h + static_cast<long>(g0) * d.hidden, d.hidden, 0,
-                    d);
-            launch_gemv(e, p, s, true);
+        {
+            const ProjSeg segs[1] = {{L.gate, L.up, kEpiSiluPair, e->h, d.hidden}};
+            launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), segs,
+                              1, nullptr, 0);
         }
-        for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
-            const int gn = std::min(kMaxBatch, n - g0);
-            GemvParams p = base_params(e, d.hidden, gn, e->h + static_cast<long>(g0) * d.hidden, d.hidden, nullptr);
-            add_seg(p, e->w[L.down], nullptr, kEpiAdd, e->x + static_cast<long>(g0) * d.dim, d.dim, 0, d);
-            launch_gemv(e, p, s, true);
+        {
+            const ProjSeg segs[1] = {{L.down, -1, kEpiAdd, e->x, d.dim}};
+            launch_projection(e, s, 0, n, e->h, d.hidden, nullptr, segs, 1, nullptr, 0);
         }
     }
     if (!need_logits) return;
-    const Weight &out = e->w[e->output >= 0 ? e->output : e->token_embd];
-    for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
-        const int gn = std::min(kMaxBatch, n - g0);
-        GemvParams p = base_params(e, d.dim, gn, e->x + static_cast<long>(g0) * d.dim, d.dim,
-                                   reinterpret_cast<const float *>(e->w[e->output_norm].data));
-        p.argmax_keys = e->keys + g0;
-        add_seg(p, out, nullptr, kEpiLogitsArgmax, e->logits + static_cast<long>(g0) * d.vocab, d.vocab, 0, d);
-        launch_gemv(e, p, s, true);
+    {
+        const ProjSeg segs[1] = {{e->output >= 0 ? e->output : e->token_embd, -1, kEpiLogitsArgmax, e->logits, d.vocab}};
+        launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[e->output_norm].data), segs, 1,
+                          nullptr, 0);
     }
     ck(keys_to_tokens_launch(e->keys, n, e->next_dev, s, e->pdl), "argmax decode launch");
     ++g_launches;
@@ -291,6 +385,7 @@ void run_step(ijb_engine *e, int n, bool need_logits) {
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         cudaGraph_t graph;
+        const uint64_t before = g_launches.load();
         ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
         try {
             ck(cudaMemcpyAsync(e->meta_dev, e->meta_host, 4 * e->d.max_batch * sizeof(int), cudaMemcpyHostToDevice,
@@ -306,14 +401,16 @@ void run_step(ijb_engine *e, int n, bool need_logits) {
         }
         ck(cudaStreamEndCapture(e->stream, &graph), "end capture");
         StepGraph sg;
+        sg.launches = g_launches.load() - before;
+        g_launches.store(before);  // counted at each replay instead
         cudaError_t ie = cudaGraphInstantiate(&sg.exec, graph, 0);
         cudaGraphDestroy(graph);
         ck(ie, "graph instantiate");
         it = e->graphs.emplace(key, sg).first;
     }
-    // launches inside the graph count as launches of this library
-    g_launches += static_cast<uint64_t>(e->d.layers) * (1 + 4 * ((n + kMaxBatch - 1) / kMaxBatch)) + 1 +
-                  (need_logits ? (n + kMaxBatch - 1) / kMaxBatch + 1 : 0);
+    // launches inside the graph count as launches of this library (counted
+    // once per replay, as many as the capture enqueued)
+    g_launches += it->second.launches;
     ck(cudaEventRecord(e->ev_start, e->stream), "step timer start");
     ck(cudaGraphLaunch(it->second.exec, e->stream), "graph launch");
     ck(cudaEventRecord(e->ev_end, e->stream), "step timer end");
@@ -422,8 +519,24 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             w.cols = static_cast<int>(t.dims[0]);
             w.rows = t.n_dims >= 2 ? static_cast<int>(t.dims[1]) : 1;
             require(t.data_dev != nullptr, "tensor without data: " + w.name);
-            if (t.type == IJB_TYPE_Q4_K) {
+            if (t.type == IJB_TYPE_Q4_K || t.type == IJB_TYPE_Q6_K) {
+                // power-of-two scale of the tensor-core path, from the GGUF blocks
                 require(w.cols % 256 == 0, "Invalid quantized tensor shape: " + w.name);
+                int *bits = dev_alloc<int>(1, "scale scan");
+                cudaError_t se = mma_scale_scan_launch(t.type, static_cast<const uint8_t *>(t.data_dev),
+                                                       static_cast<long>(w.rows) * (w.cols / 256), bits, e->stream);
+                unsigned int hb = 0;
+                if (se == cudaSuccess) se = cudaMemcpyAsync(&hb, bits, 4, cudaMemcpyDeviceToHost, e->stream);
+                if (se == cudaSuccess) se = cudaStreamSynchronize(e->stream);
+                cudaFree(bits);
+                ck(se, "weight scale scan");
+                float maxw;
+                std::memcpy(&maxw, &hb, 4);
+                int ex = 0;
+                if (maxw > 0.f) std::frexp(maxw, &ex);
+                w.mma.scale_exp = maxw > 0.f ? std::max(-60, std::min(60, 15 - ex)) : 0;
+            }
+            if (t.type == IJB_TYPE_Q4_K) {
                 w.row_bytes = w.cols / 256 * kQ4Bytes;
                 if (reinterpret_cast<uintptr_t>(t.data_dev) % 16 == 0) {
                     w.data = static_cast<const uint8_t *>(t.data_dev);
@@ -487,6 +600,37 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->layers.push_back(L);
         }
         require(e->w[e->output_norm].type == IJB_TYPE_F32 && e->w[e->output_norm].cols == d.dim, "bad output_norm");
+
+        // TMA descriptors of the tensor-core path (64-row boxes for gate/up,
+        // whose tiles hold 64 rows of each)
+        if (d.max_batch >= kMmaMinBatch) {
+            ck(mma_prepare(), "tensor-core GEMM attributes");
+            std::vector<int> paired(e->w.size(), 0);
+            for (auto &L : e->layers) paired[L.gate] = paired[L.up] = 1;
+            for (size_t i = 0; i < e->w.size(); ++i) {
+                Weight &w = e->w[i];
+                if (w.type != kQ4K && w.type != kQ6K) continue;
+                char msg[128];
+                const int scale_exp = w.mma.scale_exp;  // mma_make_weight clears the struct
+                if (mma_make_weight(w.type, w.data, w.rows, w.row_bytes, paired[i] ? 64 : 128, &w.mma, msg,
+                                    sizeof(msg)) == 0) {
+                    w.has_mma = true;
+                }
+                w.mma.scale_exp = scale_exp;
+            }
+            e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
+            ck(cudaMemset(e->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
+            e->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
+            // split-K scratch: at most ~num_sms parts in flight per launch plus one
+            // part per tile for tiles that need no split; 2*num_sms parts of
+            // [64 tokens][128 rows] floats covers every launch the step makes
+            e->mma_partial_floats = 4L * e->num_sms * kMmaMaxN * kMmaTileM;
+            e->mma_partial = dev_alloc<float>(e->mma_partial_floats, "split-K partials");
+            e->mma_counters = dev_alloc<int>(kMmaCounters, "split-K counters");
+            ck(cudaMemset(e->mma_counters, 0, kMmaCounters * sizeof(int)), "split-K counters clear");
+            const char *env = std::getenv("IJB_MMA_MIN_BATCH");  // diagnostic: path switch-over point
+            if (env) e->mma_min_batch = std::max(1, std::atoi(env));
+        }
 
         // RoPE tables, computed on the host the way FastRunner's constructor
         // does (inferencer.cu:1218-1230): float pow, angle = pos * freq, cos/sin.
@@ -580,6 +724,10 @@ void ijb_destroy(ijb_engine *e) {
     cudaFree(e->meta_dev);
     if (e->meta_host) cudaFreeHost(e->meta_host);
     if (e->next_host) cudaFreeHost(e->next_host);
+    cudaFree(e->x16);
+    cudaFree(e->x_inv);
+    cudaFree(e->mma_partial);
+    cudaFree(e->mma_counters);
     cudaFree(e->attn_partial);
     cudaFree(e->attn_counters);
     cudaFree(e->status);
@@ -607,12 +755,8 @@ int ijb_matvec(ijb_engine *e, int ti, const float *x, float *y, int cols, int ro
                 "Unexpected quantized matrix shape");
         require(batch >= 1 && cols <= kMaxCols, "bad batch or cols");
         cudaStream_t s = pick(e, stream);
-        for (int g0 = 0; g0 < batch; g0 += kMaxBatch) {
-            const int gn = std::min(kMaxBatch, batch - g0);
-            GemvParams p = base_params(e, cols, gn, x + static_cast<long>(g0) * cols, cols, nullptr);
-            add_seg(p, w, nullptr, kEpiStore, y + static_cast<long>(g0) * rows, rows, 0, e->d);
-            launch_gemv(e, p, s, false);
-        }
+        const ProjSeg segs[1] = {{ti, -1, kEpiStore, y, rows}};
+        launch_projection(e, s, 0, batch, x, cols, nullptr, segs, 1, nullptr, 0);
         return IJB_OK;
     } catch (const std::exception &ex) {
         return fail(e, ex);

@@ -305,9 +305,9 @@ __device__ __forceinline__ void q4_unit(const uint8_t *unit, int nb_u, int u, in
     }
 }
 
-// One Q6_K unit in the unit layout (ql | qh | scales | d of nb_u blocks).
-// Lane -> block lane/4, 128-weight group g = (lane/2)%2 and 16 positions
-// l0 = (lane%2)*16: 64 weights, one scale per part.  Weight (g, part, l) is
+// One Q6_K unit in the unit layout (gemv.cuh).  Lane -> block lane/4,
+// 128-weight group g = (lane/2)%2 and 16 positions l0 = (lane%2)*16: 64
+// weights, one scale per part.  Weight (g, part, l) is
 // d * scale[g*8+part*2+l/16] * (q - 32), q assembled as in q6_value
 // (inferencer.cu:473-487).
 template <int B>
@@ -317,12 +317,13 @@ __device__ __forceinline__ void q6_unit(const uint8_t *unit, int nb_u, int u, in
     if (blk >= nb_u) return;
     const int gblk0 = u * kUnitBlocks;
     const int g = (lane >> 1) & 1, l0 = (lane & 1) * 16;
-    const int Ln = 4 * nb_u;  // lanes with data in this unit
-    const uint4 la = reinterpret_cast<const uint4 *>(unit)[lane];
-    const uint4 lb = reinterpret_cast<const uint4 *>(unit + 16 * Ln)[lane];
-    const uint4 hh = reinterpret_cast<const uint4 *>(unit + 32 * Ln)[lane];
-    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(unit + 48 * Ln)[lane];
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(unit + 52 * Ln + blk * 2));
+    const uint8_t *body = unit + blk * 208;  // this lane's block; lane within the block = lane & 3
+    const int j = lane & 3;
+    const uint4 la = reinterpret_cast<const uint4 *>(body)[j];
+    const uint4 lb = reinterpret_cast<const uint4 *>(body + 64)[j];
+    const uint4 hh = reinterpret_cast<const uint4 *>(body + 128)[j];
+    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(body + 192)[j];
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(unit + nb_u * 208 + blk * 2));
     int sc[4];
 #pragma unroll
     for (int pt = 0; pt < 4; ++pt) sc[pt] = static_cast<int>(static_cast<int8_t>((sc4 >> (8 * pt)) & 255));
@@ -517,6 +518,7 @@ __device__ void epilogue(const GemvParams &p, const GemvSeg &s, int li, int b, f
 template <int B>
 __global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t cta_abort;
     const SmemLayout L = smem_layout(p.cols, B, p.need_q4, p.need_q6, p.need_f);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kDepth;
@@ -529,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) gemv_kernel(const 
     // previous kernel, so this runs before griddepcontrol.wait)
     Cursor pf;
     cursor_start(p, gw, pf);
+    if (threadIdx.x == 0) cta_abort = 0u;  // read only after the __syncthreads below
     if (lane == 0) {
         for (int s = 0; s < kDepth; ++s) mbar_init(bars + s, 1);
         fence_barrier_init();
@@ -557,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) gemv_kernel(const 
     unsigned long long best = 0ull;  // lane b: best argmax key of token b
     for (uint32_t k = 0; cur.item < p.total_items; ++k) {
         const int slot = k % kDepth;
-        mbar_wait_bounded(bars + slot, (k / kDepth) & 1, p.status);
+        mbar_wait_bounded(bars + slot, (k / kDepth) & 1, p.status, &cta_abort);
         const GemvSeg &sg = p.seg[cur.seg];
         const int nb_u = min(kUnitBlocks, nb - cur.u * kUnitBlocks);
         const uint8_t *unit = ring + slot * kSlotBytes;

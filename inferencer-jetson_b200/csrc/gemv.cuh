@@ -22,17 +22,18 @@ constexpr int kMaxCols = 8192;  // activation length the prologue stages
 constexpr int kUnitBlocks = 8;  // super-blocks per streamed unit (2048 weights)
 
 // Q6_K "unit" layout (repack_q6 in misc.cu): each row is a sequence of units
-// of up to 8 super-blocks, each unit laid out lane-major for the GEMV's lane
-// mapping.  With n blocks and L = 4n lanes, lane = 4*blk + 2*g + h (g: the
-// block's 128-weight half, h: positions 16h..16h+15 of its 32-wide columns):
-//   [0, 16L)    ql[g*64 + 16h .. +16]       of block blk, per lane
-//   [16L, 32L)  ql[g*64 + 32 + 16h .. +16]
-//   [32L, 48L)  qh[g*32 + 16h .. +16]
-//   [48L, 52L)  scales[g*8 + 2*part + h] for part 0..3 (4 bytes per lane)
-//   [52L, 52L+2n) d of each block
-// = 210n bytes, padded to 16 (1680 for n = 8).  Only bytes move, so every
-// weight is unchanged.  Q4_K rows keep the GGUF layout (144-byte blocks are
-// already 16-byte aligned and read without bank conflicts).
+// of up to 8 super-blocks.  A unit of n blocks holds n 208-byte block bodies,
+// then the n fp16 block scales d, padded to 16 bytes (1680 bytes for n = 8).
+// A block body is laid out for the 4 lanes that read it, lane j = 2*g + h
+// (g: the block's 128-weight half, h: positions 16h..16h+15 of each 32-wide
+// part):
+//   [0, 64)    ql[g*64 + 16h .. +16]       per lane, 16 bytes each
+//   [64, 128)  ql[g*64 + 32 + 16h .. +16]
+//   [128, 192) qh[g*32 + 16h .. +16]
+//   [192, 208) scales[g*8 + 2*part + h] for part 0..3 (4 bytes per lane)
+// Bodies start on 16-byte boundaries, so one block column of many rows is a
+// 2-D TMA box.  Only bytes move, so every weight is unchanged.  Q4_K rows keep
+// the GGUF layout (144-byte blocks are already 16-byte aligned).
 __host__ __device__ inline int q6_unit_bytes(int nblocks) { return (nblocks * 210 + 15) / 16 * 16; }
 __host__ __device__ inline long q6_unit_row_bytes(int cols) {
     const int nb = cols / 256, full = nb / kUnitBlocks, rest = nb % kUnitBlocks;

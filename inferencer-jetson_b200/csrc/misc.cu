@@ -12,8 +12,8 @@ namespace ijb {
 
 long q6_planar_row_bytes(int cols) { return q6_unit_row_bytes(cols); }
 
-// GGUF Q6_K row (nb blocks of ql[128] qh[64] scales[16] d[2]) -> the
-// lane-major unit layout described in gemv.cuh.  Bytes are only moved.
+// GGUF Q6_K row (nb blocks of ql[128] qh[64] scales[16] d[2]) -> the unit
+// layout described in gemv.cuh.  Bytes are only moved.
 __global__ void repack_q6_kernel(const uint8_t *src, uint8_t *dst, int rows, int nb, long dst_row_bytes) {
     const long row = blockIdx.x;
     if (row >= rows) return;
@@ -24,21 +24,20 @@ __global__ void repack_q6_kernel(const uint8_t *src, uint8_t *dst, int rows, int
     for (int i = threadIdx.x; i < nb * 210; i += blockDim.x) {
         const int blk = i / 210, o = i % 210;
         const int u = blk / kUnitBlocks, lb = blk % kUnitBlocks;
-        const int n = min(kUnitBlocks, nb - u * kUnitBlocks), L = 4 * n;
-        const long base = static_cast<long>(u) * q6_unit_bytes(kUnitBlocks);
+        const int n = min(kUnitBlocks, nb - u * kUnitBlocks);
+        const long body = static_cast<long>(u) * q6_unit_bytes(kUnitBlocks) + lb * 208;
         long to;
-        if (o < 128) {  // ql: g = o/64, second column half if o%64 >= 32, h = (o%32)/16
+        if (o < 128) {  // ql[g*64 + half*32 + 16h + j]
             const int g = o / 64, half = (o % 64) / 32, h = (o % 32) / 16;
-            const int lane = 4 * lb + 2 * g + h;
-            to = base + (half ? 16 * L : 0) + lane * 16 + (o % 16);
+            to = body + half * 64 + (2 * g + h) * 16 + (o % 16);
         } else if (o < 192) {  // qh[g*32 + 16h + j]
             const int q = o - 128, g = q / 32, h = (q % 32) / 16;
-            to = base + 32 * L + (4 * lb + 2 * g + h) * 16 + (q % 16);
+            to = body + 128 + (2 * g + h) * 16 + (q % 16);
         } else if (o < 208) {  // scales[g*8 + 2*part + h]
             const int q = o - 192, g = q / 8, part = (q % 8) / 2, h = q % 2;
-            to = base + 48 * L + (4 * lb + 2 * g + h) * 4 + part;
-        } else {
-            to = base + 52 * L + lb * 2 + (o - 208);
+            to = body + 192 + (2 * g + h) * 4 + part;
+        } else {  // d after the unit's bodies
+            to = static_cast<long>(u) * q6_unit_bytes(kUnitBlocks) + n * 208 + lb * 2 + (o - 208);
         }
         d[to] = s[i];
     }
@@ -48,16 +47,17 @@ __global__ void repack_q6_kernel(const uint8_t *src, uint8_t *dst, int rows, int
 // (inferencer.cu:473-487): d * scale * q with both products exact in fp32.
 __device__ __forceinline__ float q6_planar_value(const uint8_t *row, int nb, int blk, int i) {
     const int u = blk / kUnitBlocks, lb = blk % kUnitBlocks;
-    const int n = min(kUnitBlocks, nb - u * kUnitBlocks), L = 4 * n;
+    const int n = min(kUnitBlocks, nb - u * kUnitBlocks);
     const uint8_t *unit = row + static_cast<long>(u) * q6_unit_bytes(kUnitBlocks);
+    const uint8_t *body = unit + lb * 208;
     const int g = i / 128, p = i % 128, part = p / 32, l = p % 32, h = l / 16, j = l % 16;
-    const int lane = 4 * lb + 2 * g + h;
-    int low = unit[((part & 1) ? 16 * L : 0) + lane * 16 + j];
+    const int lane = 2 * g + h;
+    int low = body[(part & 1) * 64 + lane * 16 + j];
     low = part < 2 ? (low & 15) : (low >> 4);
-    const int high = (unit[32 * L + lane * 16 + j] >> (part * 2)) & 3;
+    const int high = (body[128 + lane * 16 + j] >> (part * 2)) & 3;
     const int q = (low | (high << 4)) - 32;
-    const int sc = static_cast<int8_t>(unit[48 * L + lane * 4 + part]);
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(unit + 52 * L + lb * 2));
+    const int sc = static_cast<int8_t>(body[192 + lane * 4 + part]);
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(unit + n * 208 + lb * 2));
     return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
 }
 

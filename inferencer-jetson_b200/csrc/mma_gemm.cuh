@@ -1,0 +1,96 @@
+// Host-visible description of the tensor-core (tcgen05) quantised GEMM used
+// for packed steps of 16..64 tokens.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gemv.cuh"
+
+namespace ijb {
+
+constexpr int kMmaTileM = 128;    // weight rows per tile (TMEM lanes)
+constexpr int kMmaMaxN = 64;      // tokens per launch (MMA N, padded to 16)
+constexpr int kMmaMinBatch = 16;  // below this the CUDA-core GEMV is used
+constexpr int kMmaCounters = 4096;  // split-K tile counters (tiles of one launch)
+
+// One weight matrix as the tensor-core path reads it: TMA descriptors over
+// its rows (Q4_K: one box per 144-byte block; Q6_K: one box per 208-byte
+// block body and one for the unit's 16 bytes of d), and a power-of-two scale
+// 2^scale_exp that keeps every dequantised weight in fp16's normal range.
+struct MmaWeight {
+    CUtensorMap body;   // box [rows_per_box][144 or 208 bytes]
+    CUtensorMap dvec;   // Q6_K only: box [rows_per_box][16 bytes]
+    int scale_exp;
+    int rows_per_box;   // 128, or 64 for the two halves of a gate/up tile
+};
+
+struct MmaSeg {
+    int w0, w1;        // indexes into MmaParams::w (w1 < 0 unless a gate/up pair)
+    int type;          // 12 / 14
+    int rows;          // rows of w0 (and w1)
+    int tile0, ntiles; // global tile range of this segment
+    int epi;           // Epilogue (gemv.cuh)
+    float *out;
+    long out_stride;
+    int row_offset;
+};
+
+struct MmaParams {
+    MmaWeight w[2 * kMaxSegs];
+    MmaSeg seg[kMaxSegs];
+    int nseg;
+    int total_tiles;
+    // split-K: each tile's K range is cut into ksplit parts of bps blocks; a
+    // part's fp32 partial goes to `partial` and the last part to finish sums
+    // them in part order and applies the epilogue (counters[tile] counts)
+    int ksplit;
+    int bps;
+    float *partial;  // [tiles * ksplit][n_pad][128]
+    int *counters;   // [tiles], zero between launches
+    int cols;             // K
+    int batch;            // tokens in this launch (<= kMmaMaxN)
+    int n_pad;            // MMA N: batch rounded up to 16
+    const uint8_t *x16;   // prepared activation (mma_prep_launch), [cols/128][n_pad/8][16][8][16 B]
+    const float *x_inv;   // [n_pad] 2^-kx of each token
+    // fused epilogue parameters (same meaning as GemvParams)
+    const float *rope_cos;
+    const float *rope_sin;
+    int half_head;
+    const int *tok_pos;
+    const int *tok_slot;
+    void *k_cache;
+    void *v_cache;
+    int kv_f32;
+    int kv_heads;
+    int head_dim;
+    int page_size;
+    long page_stride;
+    unsigned long long *argmax_keys;
+    uint32_t *status;
+};
+
+// Builds the fp16 activation tile of `batch` tokens: optional RMSNorm, the
+// reference's per-32 int8 quantisation then dequantisation (use_dp4a) or the
+// plain fp32 values, times a per-token power of two, in the tensor cores'
+// K-major layout.  Padding tokens up to n_pad are zero.
+cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
+                            int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream);
+
+// Exponent e with max|w| * 2^e <= 2^15 for a quantised matrix (one reduction
+// over its block scales); written to *out_exp on the device.
+cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks_gguf_layout, int *out_max_bits,
+                                  cudaStream_t stream);
+
+// Encodes the TMA descriptors of a weight (row_bytes per row, rows rows).
+int mma_make_weight(int type, const void *data, int rows, long row_bytes, int rows_per_box, MmaWeight *out,
+                    char *err, int err_len);
+
+cudaError_t mma_gemm_launch(const MmaParams &p, int num_sms, cudaStream_t stream);
+// Parts per tile for a launch of `tiles` tiles of `nblocks` K-blocks, so that
+// tiles * ksplit roughly fills the GPU; *bps receives blocks per part.
+int mma_choose_split(int tiles, int nblocks, int num_sms, int *bps);
+cudaError_t mma_prepare();
+int mma_smem_bytes();
+
+}  // namespace ijb

@@ -94,31 +94,32 @@ def test_gemv_baseline_config0_full_size(cuda):
 
 
 def q6_unit_layout(row_blocks: np.ndarray) -> np.ndarray:
-    """numpy statement of the lane-major Q6_K unit layout (gemv.cuh)."""
+    """numpy statement of the Q6_K unit layout (gemv.cuh): per unit of up to
+    8 blocks, 208-byte block bodies (lane-major), then the blocks' d."""
     nb = row_blocks.shape[0]
     out = []
     for u0 in range(0, nb, 8):
         ub = row_blocks[u0:u0 + 8]
         n = ub.shape[0]
-        L = 4 * n
         unit = np.zeros(((n * 210 + 15) // 16) * 16, dtype=np.uint8)
         for blk in range(n):
             b = ub[blk]
+            body = unit[blk * 208:(blk + 1) * 208]
             for g in range(2):
                 for h in range(2):
-                    lane = 4 * blk + 2 * g + h
-                    unit[lane * 16:(lane + 1) * 16] = b[g * 64 + 16 * h:g * 64 + 16 * h + 16]
-                    unit[16 * L + lane * 16:16 * L + (lane + 1) * 16] = b[g * 64 + 32 + 16 * h:g * 64 + 48 + 16 * h]
-                    unit[32 * L + lane * 16:32 * L + (lane + 1) * 16] = b[128 + g * 32 + 16 * h:128 + g * 32 + 16 * h + 16]
+                    j = 2 * g + h
+                    body[j * 16:(j + 1) * 16] = b[g * 64 + 16 * h:g * 64 + 16 * h + 16]
+                    body[64 + j * 16:64 + (j + 1) * 16] = b[g * 64 + 32 + 16 * h:g * 64 + 48 + 16 * h]
+                    body[128 + j * 16:128 + (j + 1) * 16] = b[128 + g * 32 + 16 * h:128 + g * 32 + 16 * h + 16]
                     for part in range(4):
-                        unit[48 * L + lane * 4 + part] = b[192 + g * 8 + 2 * part + h]
-            unit[52 * L + blk * 2:52 * L + blk * 2 + 2] = b[208:210]
+                        body[192 + j * 4 + part] = b[192 + g * 8 + 2 * part + h]
+            unit[n * 208 + blk * 2:n * 208 + blk * 2 + 2] = b[208:210]
         out.append(unit)
     return np.concatenate(out)
 
 
 def test_repack_round_trip(cuda):
-    """The Q6_K repack moves bytes into the lane-major unit layout exactly."""
+    """The Q6_K repack moves bytes into the unit layout exactly."""
     import torch
     rng = np.random.default_rng(9)
     for cols in (2048, 3072, 8192, 4352):
