@@ -61,15 +61,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the barrier phase with the given parity.  Gives up after
-// kWaitLimitNs: records kDevErrWaitTimeout in the launch's device status word
-// and raises `cta_abort` (a flag in the CTA's shared memory, zeroed at kernel
-// start), after which every later wait of the CTA returns at once, so a CTA
-// that lost one wait ends within one time limit.  Each poll suspends the
-// thread for up to 1 ms; the clock and the flag are read every 16 polls.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *status,
-                                                  volatile uint32_t *cta_abort) {
-    if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait_bounded, kept out of line so that the many wait
+// sites of a kernel stay small in the instruction cache.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                            volatile uint32_t *cta_abort) {
     if (*cta_abort) return false;
     uint64_t start = 0;
     for (uint32_t n = 1;; ++n) {
@@ -86,6 +81,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
             }
         }
     }
+}
+
+// Waits for the barrier phase with the given parity.  Gives up after
+// kWaitLimitNs: records kDevErrWaitTimeout in the launch's device status word
+// and raises `cta_abort` (a flag in the CTA's shared memory, zeroed at kernel
+// start), after which every later wait of the CTA returns at once, so a CTA
+// that lost one wait ends within one time limit.  Each poll suspends the
+// thread for up to 1 ms; the clock and the flag are read every 16 polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                                  volatile uint32_t *cta_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, status, cta_abort);
 }
 
 // 1-D bulk copy global -> shared, completing on `bar` (transaction bytes).

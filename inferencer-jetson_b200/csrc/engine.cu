@@ -113,9 +113,6 @@ struct ijb_engine {
     int *attn_counters = nullptr;
     uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
     float *x_inv = nullptr;
-    float *mma_partial = nullptr;  // split-K partials of the tensor-core path
-    int *mma_counters = nullptr;
-    long mma_partial_floats = 0;
     int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
     uint32_t *status = nullptr;
@@ -277,15 +274,8 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.page_stride = e->page_stride;
             m.argmax_keys = e->keys + g0 + t0;
             m.status = e->status;
-            m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->num_sms, &m.bps);
-            if (m.ksplit > 1 && (static_cast<long>(m.total_tiles) * m.ksplit * n_pad * 128 > e->mma_partial_floats ||
-                                 m.total_tiles > kMmaCounters)) {
-                m.ksplit = 1;  // no room for the partials: one part per tile
-                m.bps = cols / 256;
-            }
-            m.partial = e->mma_partial;
-            m.counters = e->mma_counters;
-            ck(mma_gemm_launch(m, e->num_sms, s), "tensor-core GEMM launch");
+            m.ksplit = mma_choose_split(m.total_tiles, cols / 256, &m.bps);
+            ck(mma_gemm_launch(m, s), "tensor-core GEMM launch");
             g_launches += 2;
         }
         return;
@@ -621,13 +611,6 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
             ck(cudaMemset(e->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
             e->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
-            // split-K scratch: at most ~num_sms parts in flight per launch plus one
-            // part per tile for tiles that need no split; 2*num_sms parts of
-            // [64 tokens][128 rows] floats covers every launch the step makes
-            e->mma_partial_floats = 4L * e->num_sms * kMmaMaxN * kMmaTileM;
-            e->mma_partial = dev_alloc<float>(e->mma_partial_floats, "split-K partials");
-            e->mma_counters = dev_alloc<int>(kMmaCounters, "split-K counters");
-            ck(cudaMemset(e->mma_counters, 0, kMmaCounters * sizeof(int)), "split-K counters clear");
             const char *env = std::getenv("IJB_MMA_MIN_BATCH");  // diagnostic: path switch-over point
             if (env) e->mma_min_batch = std::max(1, std::atoi(env));
         }
@@ -726,8 +709,6 @@ void ijb_destroy(ijb_engine *e) {
     if (e->next_host) cudaFreeHost(e->next_host);
     cudaFree(e->x16);
     cudaFree(e->x_inv);
-    cudaFree(e->mma_partial);
-    cudaFree(e->mma_counters);
     cudaFree(e->attn_partial);
     cudaFree(e->attn_counters);
     cudaFree(e->status);

@@ -4,50 +4,67 @@
 // (gemv_batch_dp4a, qkv_batch_cuda, gate_up_batch_cuda, inferencer.cu:678-751):
 // every weight is read from HBM once per step instead of once per token.
 //
-// One persistent CTA per SM walks 128-row tiles of the launch's matrices
-// (a gate/up tile is 64 gate rows + the same 64 up rows).  Warp roles:
-//   * warp 0, lane 0: TMA producer.  Per 256-wide block column of a tile it
+// Work is cut into 128-row tiles of the launch's matrices (a gate/up tile is
+// 64 gate rows + the same 64 up rows) and, when there are too few tiles to
+// fill the GPU, each tile's K range into `ksplit` parts run by the CTAs of one
+// thread-block cluster.  Warp roles of a CTA:
+//   * warp 0, lane 0: weight producer.  Per 256-wide block column of a tile it
 //     loads the raw quantised bytes as 2-D TMA boxes (Q4_K: [128 rows][144 B];
 //     Q6_K: the 208-byte block bodies and the unit's 16 bytes of d) into a
-//     3-stage ring, and per 128-wide half the prepared fp16 activation chunk
-//     into the fp16 stage the MMA will read.
-//   * warps 6..13: dequantise a raw block column into two fp16 K-major
-//     tiles [128 rows][128 K] in the UMMA canonical no-swizzle layout.  The
-//     fp32 weight is computed as the reference does (q4_value / q6_value,
-//     inferencer.cu:454-487, exact products, one rounding for Q4_K), times the
-//     matrix's power-of-two scale, then rounded to fp16.
+//     4-stage ring.
+//   * warp 6, lane 0: activation producer: per 64-wide K stage, one bulk copy
+//     of the prepared fp16 activation chunk into a 4-stage ring.
+//   * warps 7..14: dequantise.  Warps 7-10 convert the even 64-wide groups of
+//     a block column, warps 11-14 the odd ones, one thread per row, into fp16
+//     K-major tiles [128 rows][64 K] (UMMA canonical no-swizzle layout).
+//     Nibbles become fp16 through exponent-bias patterns (0x6400 | q is
+//     1024 + q) and one fp16 FMA applies the sub-block scale and offset; the
+//     K order inside each 8-wide core is permuted so that this needs no byte
+//     shuffles, and the activation tile is written in the same order.
 //   * warp 1, lane 0: issues tcgen05.mma (kind::f16, M=128, N = tokens
 //     rounded up to 16, K=16) into an fp32 accumulator in TMEM, double
-//     buffered across tiles; tcgen05.commit releases fp16 stages and signals
+//     buffered across tiles; tcgen05.commit releases stages and signals
 //     finished accumulators.
 //   * warps 2..5 (one per TMEM lane quadrant): read the accumulator with
 //     tcgen05.ld, undo the two power-of-two scales and apply the fused
 //     epilogue of the GEMV (store, residual add, RoPE + paged K write, V write,
-//     SiLU * up, logits + argmax key).
+//     SiLU * up, logits + argmax key).  With split K the parts first leave
+//     their partial sums in shared memory; each part then sums a slice of the
+//     tokens over the cluster's shared memory (DSMEM) in part order, so the
+//     result does not depend on timing.
 // All waits are bounded; TMEM is always released before the CTA exits.
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "mma_gemm.cuh"
 
 namespace ijb {
 
-constexpr int kKChunk = 128;  // K per fp16 stage (half a super-block)
+constexpr int kKChunk = 64;  // K per fp16 stage: one Q4_K group of 64 weights
+constexpr int kStages = 4;   // fp16 weight + activation stages: the 4 groups of one block column
 constexpr int kRawStages = 3;
-constexpr int kF16Stages = 2;  // dequantised weight stages
-constexpr int kXStages = 3;    // activation stages
 constexpr int kRawStageBytes = 128 * 208 + 128 * 16;  // Q6_K bodies + d (Q4_K uses 128 * 144)
 constexpr int kQ6DOff = 128 * 208;                    // d box within a Q6_K raw stage
-constexpr int kW16Bytes = kMmaTileM * kKChunk * 2;    // 32 KB
-constexpr int kX16Bytes = kMmaMaxN * kKChunk * 2;     // 16 KB
-constexpr int kExchStride = kMmaMaxN + 1;             // floats per row of the SiLU exchange buffer
-constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kConvWarp0 = 6, kConvWarps = 8;
+constexpr int kW16Bytes = kMmaTileM * kKChunk * 2;    // 16 KB
+constexpr int kX16Bytes = kMmaMaxN * kKChunk * 2;     // 8 KB
+constexpr int kCoreStride = 128;                      // bytes between 8-wide K cores
+constexpr int kGroupStride = (kKChunk / 8) * 128;     // bytes between 8-row groups (1 KB)
+constexpr int kMaxCluster = 8;
+// split K: a CTA receives [part][128 rows][slice tokens] fp32 partials (slice
+// = ceil(batch / parts) rounded up to 4, row stride padded to an odd number of
+// 16-byte units when that fits, for conflict-free vector access); the
+// unsplit epilogue uses the same buffer as [128 rows][kExch] floats
+constexpr int kRedBytes = 45 * 1024;
+constexpr int kExch = kMmaMaxN + 4;  // 68 floats: 17 x 16 B per row
+constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kXWarp = 6, kConvWarp0 = 7, kConvWarps = 16;
 constexpr int kMmaThreads = (kConvWarp0 + kConvWarps) * 32;
+constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 2;
 
 struct MmaSmem {
-    int raw, w16, x16, exch, bars, tmem, total;
+    int raw, w16, x16, red, tok, segs, bars, tmem, total;
 };
 
 __host__ __device__ constexpr MmaSmem mma_smem() {
@@ -56,18 +73,33 @@ __host__ __device__ constexpr MmaSmem mma_smem() {
     L.raw = off;
     off += kRawStages * kRawStageBytes;
     L.w16 = off;
-    off += kF16Stages * kW16Bytes;
+    off += kStages * kW16Bytes;
     L.x16 = off;
-    off += kXStages * kX16Bytes;
-    L.exch = off;
-    off += 64 * kExchStride * 4;
+    off += kStages * kX16Bytes;
+    L.red = off;
+    off += kRedBytes;
+    L.tok = off;  // x_inv, positions and KV slots of the launch's tokens
+    off += 3 * kMmaMaxN * 4;
+    L.segs = off;  // the launch's segments and weight scale exponents
+    off += kMaxSegs * static_cast<int>(sizeof(MmaSeg)) + 2 * kMaxSegs * 4;
     off = (off + 7) / 8 * 8;
     L.bars = off;
-    off += 20 * 8;
+    off += kNumBars * 8;
     L.tmem = off;
     off += 16;
     L.total = (off + 127) / 128 * 128;
     return L;
+}
+static_assert(mma_smem().total <= 227 * 1024, "shared memory of the tensor-core GEMM");
+static_assert(kMmaTileM * kExch * 4 <= kRedBytes, "the accumulator copy lives in the partial-sum buffer");
+
+// Tokens per part's slice and the row stride (floats) of the split-K buffer.
+__host__ __device__ constexpr int split_per(int batch, int parts) { return ((batch + parts - 1) / parts + 3) / 4 * 4; }
+__host__ __device__ constexpr int split_stride(int per, int parts) {
+    return ((per / 4) % 2 == 0 && parts * kMmaTileM * (per + 4) * 4 <= kRedBytes) ? per + 4 : per;
+}
+__host__ __device__ constexpr bool split_fits(int parts) {
+    return parts * kMmaTileM * split_stride(split_per(kMmaMaxN, parts), parts) * 4 <= kRedBytes;
 }
 
 int mma_smem_bytes() { return mma_smem().total; }
@@ -129,6 +161,87 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<const __half2 *>(&u); }
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t *>(&h); }
+
+// ------------------------------------------------------- cluster helpers --
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// All threads of all CTAs of the cluster (a plain CTA barrier without one).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void dsmem_st4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d));
+}
+// Arrives on the mbarrier at `bar` in CTA `rank`, releasing this thread's
+// earlier writes (and those it has synchronised with) at cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t *bar, uint32_t rank) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(dsmem_addr(smem_u32(bar), rank))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+static __device__ __noinline__ bool mbar_wait_cluster_slow(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                                           volatile uint32_t *cta_abort) {
+    if (*cta_abort) return false;
+    uint64_t start = 0;
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((n & 15u) == 0) {
+            if (*cta_abort) return false;
+            const uint64_t now = global_timer_ns();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kWaitLimitNs) {
+                *cta_abort = 1u;
+                if (status) atomicOr(status, kDevErrWaitTimeout);
+                return false;
+            }
+        }
+    }
+}
+// mbar_wait_bounded with acquire at cluster scope (for arrivals from peers).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                                          volatile uint32_t *cta_abort) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    return mbar_wait_cluster_slow(bar, parity, status, cta_abort);
+}
+
 // ------------------------------------------------------------ tile helpers --
 
 __device__ __forceinline__ int mma_seg_of_tile(const MmaParams &p, int t) {
@@ -149,15 +262,24 @@ __device__ __forceinline__ int tile_row(const MmaSeg &s, int lt, int r, bool &va
 }
 
 // ------------------------------------------------------------- dequantise --
+//
+// K order of a stage.  Stage g (0..3) of a block column holds the block's
+// weights 64g .. 64g+63 as 8 cores of 8; core j holds, in this order,
+//   64g + 4j + {0, 2, 1, 3}   and   64g + 32 + 4j + {0, 2, 1, 3}.
+// For Q4_K these are the low nibbles (sub-block 2g) and high nibbles
+// (sub-block 2g+1) of the 32-bit word j of the group's 32 bytes, so a mask
+// of 0x000F000F / 0x00F000F0 on the word and on the word >> 8 yields the four
+// fp16 pairs.  mma_prep_kernel writes the activation in the same order.
 
-// Q4_K half h of a raw block column -> fp16 K-major tile.  Thread (row, q)
-// covers sub-blocks 2(2h+q) (low nibbles) and 2(2h+q)+1 (high nibbles).
-__device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int row, int q, int h, float scale) {
+// Q4_K group g of a raw block column -> fp16 stage.  The weight is
+// (d*sc)*q - dmin*m as in q4_value (inferencer.cu:454-471), with the scale
+// products rounded to fp16 and one fp16 rounding of the result; q comes out
+// exact (1024 + q minus 1024, or (1024 + 16q) / 16 - 64).
+__device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int row, int g, float scale) {
     const uint8_t *bp = raw + row * 144;
     const uint4 hdr = *reinterpret_cast<const uint4 *>(bp);
-    const int gq = 2 * h + q;
-    const uint4 qa = *reinterpret_cast<const uint4 *>(bp + 16 + gq * 32);
-    const uint4 qb = *reinterpret_cast<const uint4 *>(bp + 32 + gq * 32);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(bp + 16 + g * 32);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(bp + 32 + g * 32);
     const float d = half_bits_to_float(hdr.x & 0xffff), dmin = half_bits_to_float(hdr.x >> 16);
     auto byte = [&](int k) -> int {
         const uint32_t w = k < 4 ? hdr.y : (k < 8 ? hdr.z : hdr.w);
@@ -166,7 +288,7 @@ __device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int
     int sc[2], m[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-        const int j = 2 * gq + t;
+        const int j = 2 * g + t;
         if (j < 4) {
             sc[t] = byte(j) & 63;
             m[t] = byte(j + 4) & 63;
@@ -175,121 +297,199 @@ __device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int
             m[t] = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
         }
     }
-    // w = (d*sc)*q - dmin*m: d*sc and its product with q are exact, so one
-    // fused multiply-add rounds exactly like the reference; the power-of-two
-    // scale is exact too.
-    const float s1[2] = {d * static_cast<float>(sc[0]) * scale, d * static_cast<float>(sc[1]) * scale};
-    const float s2[2] = {dmin * static_cast<float>(m[0]) * scale, dmin * static_cast<float>(m[1]) * scale};
+    const __half2 s1a = __float2half2_rn(d * static_cast<float>(sc[0]) * scale);
+    const __half2 s1b = __float2half2_rn(d * static_cast<float>(sc[1]) * scale);
+    const __half2 n2a = __float2half2_rn(-(dmin * static_cast<float>(m[0]) * scale));
+    const __half2 n2b = __float2half2_rn(-(dmin * static_cast<float>(m[1]) * scale));
+    const __half2 k1024 = __float2half2_rn(1024.f), k16th = __float2half2_rn(0.0625f), km64 = __float2half2_rn(-64.f);
     const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    uint8_t *dst = w16 + (row >> 3) * 2048 + (row & 7) * 16;
+    uint8_t *dst = w16 + (row >> 3) * kGroupStride + (row & 7) * 16;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {  // k-core q*8 + j: positions 8j..8j+7 of the 64
-        const int t = j >> 2;      // 0: low nibbles (sub 2gq), 1: high nibbles (sub 2gq+1)
-        const uint32_t w0 = words[(j & 3) * 2], w1 = words[(j & 3) * 2 + 1];
-        const uint32_t n0 = t ? (w0 >> 4) & 0x0F0F0F0Fu : w0 & 0x0F0F0F0Fu;
-        const uint32_t n1 = t ? (w1 >> 4) & 0x0F0F0F0Fu : w1 & 0x0F0F0F0Fu;
-        float f[8];
-        f[0] = fmaf(byte_to_float(n0, 0x7440), s1[t], -s2[t]);
-        f[1] = fmaf(byte_to_float(n0, 0x7441), s1[t], -s2[t]);
-        f[2] = fmaf(byte_to_float(n0, 0x7442), s1[t], -s2[t]);
-        f[3] = fmaf(byte_to_float(n0, 0x7443), s1[t], -s2[t]);
-        f[4] = fmaf(byte_to_float(n1, 0x7440), s1[t], -s2[t]);
-        f[5] = fmaf(byte_to_float(n1, 0x7441), s1[t], -s2[t]);
-        f[6] = fmaf(byte_to_float(n1, 0x7442), s1[t], -s2[t]);
-        f[7] = fmaf(byte_to_float(n1, 0x7443), s1[t], -s2[t]);
-        const uint4 o = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
-                                   pack_half2(f[6], f[7]));
-        *reinterpret_cast<uint4 *>(dst + (q * 8 + j) * 128) = o;
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t w = words[j], w8 = w >> 8;
+        const __half2 qa02 = __hsub2(bits_h2((w & 0x000F000Fu) | 0x64006400u), k1024);
+        const __half2 qa13 = __hsub2(bits_h2((w8 & 0x000F000Fu) | 0x64006400u), k1024);
+        const __half2 qb02 = __hfma2(bits_h2((w & 0x00F000F0u) | 0x64006400u), k16th, km64);
+        const __half2 qb13 = __hfma2(bits_h2((w8 & 0x00F000F0u) | 0x64006400u), k16th, km64);
+        uint4 o;
+        o.x = h2_bits(__hfma2(qa02, s1a, n2a));
+        o.y = h2_bits(__hfma2(qa13, s1a, n2a));
+        o.z = h2_bits(__hfma2(qb02, s1b, n2b));
+        o.w = h2_bits(__hfma2(qb13, s1b, n2b));
+        *reinterpret_cast<uint4 *>(dst + j * kCoreStride) = o;
     }
 }
 
-// Q6_K half h (= the block's 128-weight group g) of a raw block column ->
-// fp16 K-major tile.  Thread (row, q) is the block-body lane j = 2h + q:
-// positions part*32 + 16q + 0..15 of the group's four parts.
-__device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int row, int q, int h, int lb,
-                                           float scale) {
+// Q6_K group g of a raw block column (unit layout, gemv.cuh) -> fp16 stage.
+// Weights 64g .. 64g+63 are, in Q6_K terms, parts 2(g&1) and 2(g&1)+1 of the
+// 128-half g>>1, positions l = 0..31 (lanes 2(g>>1) and 2(g>>1)+1 of the
+// unit layout).  The 6-bit code is assembled in an fp16 mantissa (1024 + q,
+// or 1024 + 16q for the high nibbles), q - 32 is exact, and one fp16 multiply
+// by d*scale (rounded to fp16) gives the weight of q6_value
+// (inferencer.cu:473-487) with two roundings.
+__device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int row, int g, int lb, float scale) {
     const uint8_t *body = raw + row * 208;
-    const int j = 2 * h + q;
-    const uint4 la = reinterpret_cast<const uint4 *>(body)[j];
-    const uint4 lbq = reinterpret_cast<const uint4 *>(body + 64)[j];
-    const uint4 hh = reinterpret_cast<const uint4 *>(body + 128)[j];
-    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(body + 192)[j];
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(raw + kQ6DOff + row * 16 + lb * 2));
-    const uint32_t A[4] = {la.x, la.y, la.z, la.w}, Bw[4] = {lbq.x, lbq.y, lbq.z, lbq.w};
-    const uint32_t H[4] = {hh.x, hh.y, hh.z, hh.w};
-    uint8_t *dst = w16 + (row >> 3) * 2048 + (row & 7) * 16;
+    const int h = g >> 1, hi = g & 1;
+    const uint4 *A = reinterpret_cast<const uint4 *>(body) + 2 * h;
+    const uint4 *B = reinterpret_cast<const uint4 *>(body + 64) + 2 * h;
+    const uint4 *H = reinterpret_cast<const uint4 *>(body + 128) + 2 * h;
+    const uint2 scw = *reinterpret_cast<const uint2 *>(body + 192 + 8 * h);
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(raw + kQ6DOff + row * 16 + lb * 2)) * scale;
+    const __half2 k1056 = __float2half2_rn(1056.f), k16th = __float2half2_rn(0.0625f), km96 = __float2half2_rn(-96.f);
+    uint8_t *dst = w16 + (row >> 3) * kGroupStride + (row & 7) * 16;
+#pragma unroll 1
+    for (int l2 = 0; l2 < 2; ++l2) {
+        const uint32_t s4 = l2 ? scw.y : scw.x;
+        const __half2 sa = __float2half2_rn(d * static_cast<float>(static_cast<int8_t>((s4 >> (16 * hi)) & 255)));
+        const __half2 sb = __float2half2_rn(d * static_cast<float>(static_cast<int8_t>((s4 >> (16 * hi + 8)) & 255)));
+        const uint4 a4 = A[l2], b4 = B[l2], h4 = H[l2];
+        const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w}, bw[4] = {b4.x, b4.y, b4.z, b4.w};
+        const uint32_t hw[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
-    for (int pt = 0; pt < 4; ++pt) {
-        // d * scale is exact in fp32 (11 + 8 bits), and so is its product with q
-        const float s = d * static_cast<float>(static_cast<int8_t>((sc4 >> (8 * pt)) & 255)) * scale;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {  // k-core pt*4 + 2q + half: 8 positions
-            uint32_t qw[2];
-#pragma unroll
-            for (int w = 0; w < 2; ++w) {
-                const int wi = half * 2 + w;
-                const uint32_t lo = (pt & 1) ? Bw[wi] : A[wi];
-                const uint32_t low = pt < 2 ? (lo & 0x0F0F0F0Fu) : ((lo >> 4) & 0x0F0F0F0Fu);
-                qw[w] = low | (((H[wi] >> (2 * pt)) & 0x03030303u) << 4);  // codes 0..63
+        for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t a = aw[jj], b = bw[jj], q = hw[jj];
+            const uint32_t a8 = a >> 8, b8 = b >> 8;
+            const uint32_t qp4 = q << 4, qm4 = q >> 4, qp2 = q << 2, qm6 = q >> 6;
+            __half2 v02a, v13a, v02b, v13b;
+            if (!hi) {  // low nibbles, high bits 0-1 (part 0) and 2-3 (part 1)
+                v02a = __hsub2(bits_h2((a & 0x000F000Fu) | (qp4 & 0x00300030u) | 0x64006400u), k1056);
+                v13a = __hsub2(bits_h2((a8 & 0x000F000Fu) | (qm4 & 0x00300030u) | 0x64006400u), k1056);
+                v02b = __hsub2(bits_h2((b & 0x000F000Fu) | (qp2 & 0x00300030u) | 0x64006400u), k1056);
+                v13b = __hsub2(bits_h2((b8 & 0x000F000Fu) | (qm6 & 0x00300030u) | 0x64006400u), k1056);
+            } else {    // high nibbles, high bits 4-5 (part 2) and 6-7 (part 3), scaled by 16
+                v02a = __hfma2(bits_h2((a & 0x00F000F0u) | (qp4 & 0x03000300u) | 0x64006400u), k16th, km96);
+                v13a = __hfma2(bits_h2((a8 & 0x00F000F0u) | (qm4 & 0x03000300u) | 0x64006400u), k16th, km96);
+                v02b = __hfma2(bits_h2((b & 0x00F000F0u) | (qp2 & 0x03000300u) | 0x64006400u), k16th, km96);
+                v13b = __hfma2(bits_h2((b8 & 0x00F000F0u) | (qm6 & 0x03000300u) | 0x64006400u), k16th, km96);
             }
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                f[e] = (__int_as_float(__byte_perm(qw[0], 0x4B000000u, 0x7440 + e)) - 8388640.0f) * s;
-                f[4 + e] = (__int_as_float(__byte_perm(qw[1], 0x4B000000u, 0x7440 + e)) - 8388640.0f) * s;
-            }
-            const uint4 o = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
-                                       pack_half2(f[6], f[7]));
-            *reinterpret_cast<uint4 *>(dst + (pt * 4 + 2 * q + half) * 128) = o;
+            uint4 o;
+            o.x = h2_bits(__hmul2(v02a, sa));
+            o.y = h2_bits(__hmul2(v13a, sa));
+            o.z = h2_bits(__hmul2(v02b, sb));
+            o.w = h2_bits(__hmul2(v13b, sb));
+            *reinterpret_cast<uint4 *>(dst + (4 * l2 + jj) * kCoreStride) = o;
         }
     }
 }
 
 // --------------------------------------------------------------- epilogue --
+//
+// The epilogue runs once per tile, so its code is kept compact (it is cold in
+// the instruction cache every time): the accumulator is first moved to shared
+// memory, then one rolled loop per token applies the fused operation.  Token
+// positions, KV slots and activation scales are staged in shared memory at
+// kernel start; the residual add is a fire-and-forget red.global.add (one
+// writer per element, so the result is the plain fp32 sum).
 
-__device__ void mma_epilogue_value(const MmaParams &p, const MmaSeg &s, int row, bool valid, int n, float y,
-                                   float partner) {
-    switch (s.epi) {
+struct EpiTok {
+    const float *x_inv;  // [n_pad]
+    const int *pos;      // [n_pad]
+    const int *slot;     // [n_pad]
+};
+
+// Per tile row: output pointer for token 0 and everything the operation needs.
+struct EpiRow {
+    float *out;  // segment output + row offset + row; token n at out[n * stride]
+    long stride;
+    int epi, f, head, dd, row;
+    bool valid, even;
+};
+
+__device__ __forceinline__ EpiRow make_epi_row(const MmaParams &p, const MmaSeg &sg, int row, bool valid) {
+    EpiRow e;
+    e.out = sg.out + sg.row_offset + row;
+    e.stride = sg.out_stride;
+    e.epi = sg.epi;
+    e.row = sg.row_offset + row;
+    e.valid = valid;
+    e.even = (row & 1) == 0;
+    e.f = p.half_head > 0 ? (row >> 1) % p.half_head : 0;  // RoPE frequency of the pair (2j, 2j+1)
+    e.head = p.head_dim > 0 ? row / p.head_dim : 0;
+    e.dd = p.head_dim > 0 ? row % p.head_dim : 0;
+    return e;
+}
+
+// Tokens n0 .. n0+3 (those below n_end) of one tile row: values y, and z =
+// the value of row ^ 1 (RoPE pairs) or of the matching up row (SiLU pairs,
+// gate rows only).  One switch per four tokens; every lane of the warp calls
+// this with the same n0 (the logits key is a warp reduction).
+__device__ __forceinline__ void epi_apply4(const MmaParams &p, const EpiRow &e, const EpiTok &tk, int n0, int n_end,
+                                           float4 y4, float4 z4, bool gate, int lane) {
+    const float y[4] = {y4.x, y4.y, y4.z, y4.w}, z[4] = {z4.x, z4.y, z4.z, z4.w};
+    switch (e.epi) {
         case kEpiStore:
-            if (valid) s.out[n * s.out_stride + s.row_offset + row] = y;
+            if (e.valid)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (n0 + k < n_end) e.out[(n0 + k) * e.stride] = y[k];
             break;
         case kEpiAdd:
-            if (valid) s.out[n * s.out_stride + s.row_offset + row] += y;
+            if (e.valid)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (n0 + k < n_end)
+                        asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + (n0 + k) * e.stride), "f"(y[k])
+                                     : "memory");
+            break;
+        case kEpiSiluPair:
+            if (e.valid && gate)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (n0 + k < n_end) e.out[(n0 + k) * e.stride] = y[k] / (1.f + __expf(-y[k])) * z[k];
             break;
         case kEpiRopeQ:
         case kEpiRopeKCache: {
-            if (!valid) break;
-            // pair (2j, 2j+1) rotated with frequency j % (head_dim/2) (rope_cuda, inferencer.cu:906-917)
-            const int j = row >> 1, f = j % p.half_head;
-            const int pos = p.tok_pos[n];
-            const float c = p.rope_cos[pos * p.half_head + f], sn = p.rope_sin[pos * p.half_head + f];
-            const bool even = (row & 1) == 0;
-            const float a = even ? y : partner, b = even ? partner : y;
-            const float r = even ? a * c - b * sn : a * sn + b * c;
-            if (s.epi == kEpiRopeQ) {
-                s.out[n * s.out_stride + s.row_offset + row] = r;
-            } else {
-                const int slot = p.tok_slot[n];
-                const int page = slot / p.page_size, t = slot % p.page_size;
-                const int head = row / p.head_dim, dd = row % p.head_dim;
-                const long off = static_cast<long>(page) * p.page_stride +
-                                 (static_cast<long>(head) * p.page_size + t) * p.head_dim + dd;
-                if (p.kv_f32) static_cast<float *>(p.k_cache)[off] = r;
-                else static_cast<__half *>(p.k_cache)[off] = __float2half_rn(r);
+            if (!e.valid) break;
+            // rope_cuda (inferencer.cu:906-917)
+            float c[4], sn[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int pos = n0 + k < n_end ? tk.pos[n0 + k] : 0;
+                c[k] = __ldg(p.rope_cos + pos * p.half_head + e.f);
+                sn[k] = __ldg(p.rope_sin + pos * p.half_head + e.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (n0 + k >= n_end) continue;
+                const float a = e.even ? y[k] : z[k], b = e.even ? z[k] : y[k];
+                const float r = e.even ? a * c[k] - b * sn[k] : a * sn[k] + b * c[k];
+                if (e.epi == kEpiRopeQ) {
+                    e.out[(n0 + k) * e.stride] = r;
+                } else {
+                    const int slot = tk.slot[n0 + k];
+                    const long off = static_cast<long>(slot / p.page_size) * p.page_stride +
+                                     (static_cast<long>(e.head) * p.page_size + slot % p.page_size) * p.head_dim + e.dd;
+                    if (p.kv_f32) static_cast<float *>(p.k_cache)[off] = r;
+                    else static_cast<__half *>(p.k_cache)[off] = __float2half_rn(r);
+                }
             }
             break;
         }
-        case kEpiVCache: {
-            if (!valid) break;
-            const int slot = p.tok_slot[n];
-            const int page = slot / p.page_size, t = slot % p.page_size;
-            const int head = row / p.head_dim, dd = row % p.head_dim;
-            const long off = static_cast<long>(page) * p.page_stride +
-                             (static_cast<long>(head) * p.page_size + t) * p.head_dim + dd;
-            if (p.kv_f32) static_cast<float *>(p.v_cache)[off] = y;
-            else static_cast<__half *>(p.v_cache)[off] = __float2half_rn(y);
+        case kEpiVCache:
+            if (e.valid)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (n0 + k >= n_end) continue;
+                    const int slot = tk.slot[n0 + k];
+                    const long off = static_cast<long>(slot / p.page_size) * p.page_stride +
+                                     (static_cast<long>(e.head) * p.page_size + slot % p.page_size) * p.head_dim + e.dd;
+                    if (p.kv_f32) static_cast<float *>(p.v_cache)[off] = y[k];
+                    else static_cast<__half *>(p.v_cache)[off] = __float2half_rn(y[k]);
+                }
             break;
-        }
+        case kEpiLogitsArgmax:
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (n0 + k >= n_end) break;
+                if (e.valid) e.out[(n0 + k) * e.stride] = y[k];
+                unsigned long long key = e.valid ? argmax_key(y[k], e.row) : 0ull;
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = other > key ? other : key;
+                }
+                if (lane == 0 && key) atomicMax(p.argmax_keys + n0 + k, key);
+            }
+            break;
         default:
             break;
     }
@@ -297,86 +497,60 @@ __device__ void mma_epilogue_value(const MmaParams &p, const MmaSeg &s, int row,
 
 // ----------------------------------------------------------------- kernel --
 
-// Applies a tile row's epilogue from the split-K partials of its tile, summed
-// in part order (so the result does not depend on which part finished last).
-// Eight tokens at a time, so each part contributes 8 (or 16) independent loads.
-__device__ void mma_reduced_epilogue(const MmaParams &p, const MmaSeg &sg, const float *tile_part, int r, int row,
-                                     bool valid, int lane) {
-    const long part_stride = static_cast<long>(p.n_pad) * 128;
-    const bool silu = sg.epi == kEpiSiluPair;
-    const bool pairs = sg.epi == kEpiRopeQ || sg.epi == kEpiRopeKCache;
-    const int rz = silu ? (r + 64) & 127 : (r ^ 1);  // the row whose sum the epilogue also needs
-    for (int n0 = 0; n0 < p.batch; n0 += 8) {
-        float y[8], z[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = z[k] = 0.f;
-#pragma unroll 4
-        for (int s = 0; s < p.ksplit; ++s) {
-            const float *src = tile_part + s * part_stride + n0 * 128;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                y[k] += __ldcg(src + k * 128 + r);
-                if (silu || pairs) z[k] += __ldcg(src + k * 128 + rz);
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int n = n0 + k;
-            if (silu) {
-                if (r < 64 && valid && n < p.batch)
-                    sg.out[n * sg.out_stride + sg.row_offset + row] = y[k] / (1.f + __expf(-y[k])) * z[k];
-            } else if (sg.epi == kEpiLogitsArgmax) {
-                const bool ok = valid && n < p.batch;
-                if (ok) sg.out[n * sg.out_stride + sg.row_offset + row] = y[k];
-                unsigned long long key = ok ? argmax_key(y[k], sg.row_offset + row) : 0ull;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-                    key = other > key ? other : key;
-                }
-                if (lane == 0 && key) atomicMax(p.argmax_keys + n, key);
-            } else if (n < p.batch) {
-                mma_epilogue_value(p, sg, row, valid, n, y[k], z[k]);
-            }
-        }
-    }
-}
-
 __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_constant__ MmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr MmaSmem L = mma_smem();
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
-    uint64_t *full_raw = bars, *empty_raw = bars + 3, *full_w16 = bars + 6, *empty_w16 = bars + 8;
-    uint64_t *full_x = bars + 10, *empty_x = bars + 13, *acc_full = bars + 16, *acc_empty = bars + 18;
+    uint64_t *full_raw = bars, *empty_raw = full_raw + kRawStages;
+    uint64_t *full = empty_raw + kRawStages, *empty = full + kStages;  // fp16 weight + activation stage
+    uint64_t *acc_full = empty + kStages, *acc_empty = acc_full + 2;
+    uint64_t *part_ready = acc_empty + 2, *part_free = part_ready + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem);
     uint32_t *cta_abort = tmem_slot + 1;
-    int *last_flag = reinterpret_cast<int *>(tmem_slot + 2);
-    float *exch = reinterpret_cast<float *>(smem + L.exch);
+    float *red = reinterpret_cast<float *>(smem + L.red);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = p.cols / 256;
     const int n_pad = p.n_pad;
-    const int total_units = p.total_tiles * p.ksplit;
+    const int ksplit = p.ksplit;
+    const int rank = static_cast<int>(cluster_rank());
+    const int tile_first = static_cast<int>(cluster_id()), tile_step = static_cast<int>(cluster_count());
+    const int b0 = rank * p.bps, b1 = min(nb, b0 + p.bps);  // this part's block columns
     const uint32_t tmem_cols = n_pad * 2 <= 32 ? 32 : (n_pad * 2 <= 64 ? 64 : 128);
 
+    MmaSeg *seg_s = reinterpret_cast<MmaSeg *>(smem + L.segs);
+    int *wexp_s = reinterpret_cast<int *>(seg_s + kMaxSegs);
+    if (warp == kProducerWarp) {
+        // the launch's segments into shared memory, TMA descriptors fetched early
+        if (lane < p.nseg) {
+            const MmaSeg sg = p.seg[lane];
+            seg_s[lane] = sg;
+            for (int h = 0; h < 2; ++h) {
+                const int wi = h ? sg.w1 : sg.w0;
+                if (wi < 0) continue;
+                wexp_s[wi] = p.w[wi].scale_exp;
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.w[wi].body)) : "memory");
+                if (sg.type == kQ6K)
+                    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.w[wi].dvec)) : "memory");
+            }
+        }
+    }
     if (threadIdx.x == 0) {
         *cta_abort = 0u;
         for (int i = 0; i < kRawStages; ++i) {
             mbar_init(full_raw + i, 1);
             mbar_init(empty_raw + i, kConvWarps);
         }
-        for (int i = 0; i < kF16Stages; ++i) {
-            mbar_init(full_w16 + i, kConvWarps);
-            mbar_init(empty_w16 + i, 1);
-        }
-        for (int i = 0; i < kXStages; ++i) {
-            mbar_init(full_x + i, 1);
-            mbar_init(empty_x + i, 1);
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(full + i, kConvWarps / kStages + 1);  // the group's warps + the activation copy
+            mbar_init(empty + i, 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(acc_full + i, 1);
             mbar_init(acc_empty + i, 4);
         }
+        mbar_init(part_ready, ksplit);
+        mbar_init(part_free, ksplit);
         fence_barrier_init();
     }
     if (warp == kMmaWarp) {
@@ -386,25 +560,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();  // barriers of every CTA of the cluster are initialised
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            uint32_t rc = 0, xc = 0;
-            const uint32_t xbytes = static_cast<uint32_t>(n_pad) * kKChunk * 2;
-            bool waited = false;
-            for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-                const int t = u / p.ksplit, sp = u % p.ksplit;
-                const MmaSeg &sg = p.seg[mma_seg_of_tile(p, t)];
+            uint32_t rc = 0;
+            int r = 0;
+            for (int t = tile_first; t < p.total_tiles; t += tile_step) {
+                const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
                 const int lt = t - sg.tile0;
                 const bool pair = sg.w1 >= 0;
                 const int y0 = pair ? lt * 64 : lt * 128;
-                const int b0 = sp * p.bps, b1 = min(nb, b0 + p.bps);
-                for (int b = b0; b < b1; ++b) {
-                    const int r = rc % kRawStages;
+                for (int b = b0; b < b1; ++b, ++rc) {
                     if (rc >= kRawStages)
                         mbar_wait_bounded(empty_raw + r, ((rc / kRawStages) - 1) & 1, p.status, cta_abort);
                     uint8_t *dst = smem + L.raw + r * kRawStageBytes;
@@ -413,10 +583,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
                         tma_load_2d(dst, &p.w[sg.w0].body, b * 144, y0, full_raw + r);
                         if (pair) tma_load_2d(dst + 64 * 144, &p.w[sg.w1].body, b * 144, y0, full_raw + r);
                     } else {
-                        const int uu = b / kUnitBlocks, lb = b % kUnitBlocks;
-                        const int n_u = min(kUnitBlocks, nb - uu * kUnitBlocks);
-                        const int xb = uu * q6_unit_bytes(kUnitBlocks) + lb * 208;
-                        const int xd = uu * q6_unit_bytes(kUnitBlocks) + n_u * 208;
+                        const int u = b / kUnitBlocks, lb = b % kUnitBlocks;
+                        const int n_u = min(kUnitBlocks, nb - u * kUnitBlocks);
+                        const int xb = u * q6_unit_bytes(kUnitBlocks) + lb * 208;
+                        const int xd = u * q6_unit_bytes(kUnitBlocks) + n_u * 208;
                         mbar_arrive_expect_tx(full_raw + r, kRawStageBytes);
                         tma_load_2d(dst, &p.w[sg.w0].body, xb, y0, full_raw + r);
                         tma_load_2d(dst + kQ6DOff, &p.w[sg.w0].dvec, xd, y0, full_raw + r);
@@ -425,176 +595,198 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
                             tma_load_2d(dst + kQ6DOff + 64 * 16, &p.w[sg.w1].dvec, xd, y0, full_raw + r);
                         }
                     }
-                    ++rc;
-                    if (!waited) {  // the activation is written by the previous kernel
-                        pdl_wait();
-                        waited = true;
-                    }
-                    for (int h = 0; h < 2; ++h) {
-                        const int xs = xc % kXStages;
-                        if (xc >= kXStages) mbar_wait_bounded(empty_x + xs, ((xc / kXStages) - 1) & 1, p.status, cta_abort);
-                        mbar_arrive_expect_tx(full_x + xs, xbytes);
-                        bulk_g2s(smem + L.x16 + xs * kX16Bytes, p.x16 + static_cast<long>(2 * b + h) * xbytes, xbytes,
-                                 full_x + xs);
-                        ++xc;
+                    if (++r == kRawStages) r = 0;
+                }
+            }
+        }
+    } else if (warp == kXWarp) {
+        if (lane == 0) {
+            pdl_wait();  // the activation is written by the previous kernel
+            uint32_t use = 0;  // block columns done: stage g's use count
+            const uint32_t xbytes = static_cast<uint32_t>(n_pad) * kKChunk * 2;
+            for (int t = tile_first; t < p.total_tiles; t += tile_step) {
+                for (int b = b0; b < b1; ++b, ++use) {
+                    for (int g = 0; g < kStages; ++g) {
+                        if (use) mbar_wait_bounded(empty + g, (use - 1) & 1, p.status, cta_abort);
+                        mbar_arrive_expect_tx(full + g, xbytes);
+                        bulk_g2s(smem + L.x16 + g * kX16Bytes, p.x16 + static_cast<long>(b * kStages + g) * xbytes,
+                                 xbytes, full + g);
                     }
                 }
             }
-            if (!waited) pdl_wait();
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // D (fp32) [128 x n_pad] = A (fp16, K-major) * B (fp16, K-major)^T
             const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(n_pad >> 3) << 17) | (8u << 24);
-            uint32_t fc = 0, xc = 0, i = 0;
-            for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++i) {
-                const int sp = u % p.ksplit;
-                const int b0 = sp * p.bps, b1 = min(nb, b0 + p.bps);
+            const uint64_t a_desc0 = umma_desc(smem_u32(smem + L.w16), kCoreStride, kGroupStride);
+            const uint64_t b_desc0 = umma_desc(smem_u32(smem + L.x16), kCoreStride, kGroupStride);
+            uint32_t use = 0, i = 0;
+            for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
                 const int a = i & 1;
                 if (i >= 2) mbar_wait_bounded(acc_empty + a, ((i >> 1) - 1) & 1, p.status, cta_abort);
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + static_cast<uint32_t>(a * n_pad);
-                for (int b = b0; b < b1; ++b) {
-                    for (int h = 0; h < 2; ++h) {
-                        const int f = fc % kF16Stages, xs = xc % kXStages;
-                        mbar_wait_bounded(full_w16 + f, (fc / kF16Stages) & 1, p.status, cta_abort);
-                        mbar_wait_bounded(full_x + xs, (xc / kXStages) & 1, p.status, cta_abort);
+                uint32_t accumulate = 0;
+                for (int b = b0; b < b1; ++b, ++use) {
+#pragma unroll
+                    for (int g = 0; g < kStages; ++g) {
+                        mbar_wait_bounded(full + g, use & 1, p.status, cta_abort);
                         tc_fence_after();
-                        const uint32_t wa = smem_u32(smem + L.w16 + f * kW16Bytes);
-                        const uint32_t xa = smem_u32(smem + L.x16 + xs * kX16Bytes);
+                        // descriptor address fields advance by 16 B units: stage g, then K=16 steps of 256 B
+                        const uint64_t ad = a_desc0 + static_cast<uint64_t>(g * (kW16Bytes >> 4));
+                        const uint64_t bd = b_desc0 + static_cast<uint64_t>(g * (kX16Bytes >> 4));
 #pragma unroll
                         for (int kk = 0; kk < kKChunk / 16; ++kk) {
-                            umma_f16(dcol, umma_desc(wa + kk * 256, 128, 2048), umma_desc(xa + kk * 256, 128, 2048),
-                                     idesc, (b != b0 || h || kk) ? 1u : 0u);
+                            umma_f16(dcol, ad + kk * 16, bd + kk * 16, idesc, accumulate);
+                            accumulate = 1u;
                         }
-                        umma_commit(empty_w16 + f);
-                        umma_commit(empty_x + xs);
-                        ++fc;
-                        ++xc;
+                        umma_commit(empty + g);
                     }
                 }
                 umma_commit(acc_full + a);
             }
         }
-    } else if (warp < kConvWarp0) {
+    } else if (warp < kXWarp) {
         // ---------------------------------------------------------- epilogue
         const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
         const int r = quad * 32 + lane;
         pdl_wait();
+        float *xinv_s = reinterpret_cast<float *>(smem + L.tok);
+        int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxN), *slot_s = pos_s + kMmaMaxN;
+        if (r < n_pad) {
+            xinv_s[r] = p.x_inv[r];
+            pos_s[r] = p.tok_pos && r < p.batch ? p.tok_pos[r] : 0;
+            slot_s[r] = p.tok_slot && r < p.batch ? p.tok_slot[r] : 0;
+        }
+        named_bar_sync(1, 128);
+        const EpiTok tk{xinv_s, pos_s, slot_s};
+        const int per = split_per(p.batch, ksplit), stride = split_stride(per, ksplit);  // split-K slices
+        const int chunks = n_pad / 16;
         uint32_t i = 0;
-        for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++i) {
-            const int t = u / p.ksplit, sp = u % p.ksplit;
-            const MmaSeg &sg = p.seg[mma_seg_of_tile(p, t)];
+        for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
+            const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
             const int lt = t - sg.tile0;
             const int a = i & 1;
             mbar_wait_bounded(acc_full + a, (i >> 1) & 1, p.status, cta_abort);
             tc_fence_after();
             bool valid;
             const int row = tile_row(sg, lt, r, valid);
-            const float wscale = ldexpf(1.0f, -p.w[r >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0].scale_exp);
+            const EpiRow e = make_epi_row(p, sg, row, valid);
+            const bool silu = sg.epi == kEpiSiluPair, pairs = sg.epi == kEpiRopeQ || sg.epi == kEpiRopeKCache;
+            const float wscale = ldexpf(1.0f, -wexp_s[r >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * n_pad;
-            if (p.ksplit > 1) {
-                // write this part's values; the last part of the tile reduces
-                float *mine = p.partial + (static_cast<long>(t) * p.ksplit + sp) * n_pad * 128;
-                for (int c0 = 0; c0 < n_pad; c0 += 16) {
+            if (ksplit > 1) {
+                // the owners have finished reading what this CTA pushed for the previous tile
+                bool ok = i == 0 || mbar_wait_cluster_bounded(part_free, (i - 1) & 1, p.status, cta_abort);
+                // push: tokens n..n+3 go to owner o = n / per, at red[rank][r][n - o * per] there;
+                // each part starts at a different chunk so the owners are written in turn
+                const uint32_t red_row = smem_u32(red) + static_cast<uint32_t>((rank * 128 + r) * stride * 4);
+                for (int cc = 0; cc < chunks && ok; ++cc) {
+                    const int c0 = ((cc + rank) % chunks) * 16;
+                    if (c0 >= p.batch) continue;
                     float v[16];
                     tmem_ld16(taddr + c0, v);
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) __stcg(mine + (c0 + k) * 128 + r, v[k] * wscale * p.x_inv[c0 + k]);
+                    for (int q = 0; q < 4; ++q) {
+                        const int n = c0 + 4 * q;
+                        if (n < p.batch) {
+                            const int o = n / per;
+                            dsmem_st4(dsmem_addr(red_row + static_cast<uint32_t>((n - o * per) * 4), o),
+                                      v[4 * q] * wscale * xinv_s[n], v[4 * q + 1] * wscale * xinv_s[n + 1],
+                                      v[4 * q + 2] * wscale * xinv_s[n + 2], v[4 * q + 3] * wscale * xinv_s[n + 3]);
+                        }
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(acc_empty + a);
-                __threadfence();
                 named_bar_sync(1, 128);
                 if (threadIdx.x == kEpiWarp0 * 32) {
-                    const int prev = atomicAdd(p.counters + t, 1);
-                    *last_flag = prev == p.ksplit - 1;
-                    if (prev == p.ksplit - 1) p.counters[t] = 0;  // ready for the next launch
+                    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                    for (int s = 0; s < ksplit; ++s) mbar_arrive_remote(part_ready, s);
                 }
-                named_bar_sync(1, 128);
-                if (*last_flag) {
-                    __threadfence();
-                    mma_reduced_epilogue(p, sg, p.partial + static_cast<long>(t) * p.ksplit * n_pad * 128, r, row,
-                                         valid, lane);
+                ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort) && ok;
+                const int n_lo = min(p.batch, rank * per), n_end = min(p.batch, n_lo + per);
+                // this CTA's tokens, summed over the parts in part order
+                const float *mine = red + r * stride, *zrow = red + ((r + 64) & 127) * stride;
+                for (int t0 = 0; ok && n_lo + t0 < n_end; t0 += 4) {
+                    float4 y = make_float4(0.f, 0.f, 0.f, 0.f), z = y;
+                    for (int s = 0; s < ksplit; ++s) {
+                        const float4 v = *reinterpret_cast<const float4 *>(mine + s * 128 * stride + t0);
+                        y.x += v.x; y.y += v.y; y.z += v.z; y.w += v.w;
+                        if (silu && r < 64) {
+                            const float4 u = *reinterpret_cast<const float4 *>(zrow + s * 128 * stride + t0);
+                            z.x += u.x; z.y += u.y; z.z += u.z; z.w += u.w;
+                        }
+                    }
+                    if (pairs)
+                        z = make_float4(__shfl_xor_sync(0xffffffffu, y.x, 1), __shfl_xor_sync(0xffffffffu, y.y, 1),
+                                        __shfl_xor_sync(0xffffffffu, y.z, 1), __shfl_xor_sync(0xffffffffu, y.w, 1));
+                    epi_apply4(p, e, tk, n_lo + t0, n_end, y, z, r < 64, lane);
                 }
-                named_bar_sync(1, 128);  // last_flag is rewritten by the next unit
+                named_bar_sync(1, 128);  // this CTA's buffer has been read
+                if (threadIdx.x == kEpiWarp0 * 32)
+                    for (int s = 0; s < ksplit; ++s) mbar_arrive_remote(part_free, s);
                 continue;
             }
+            // whole K range here: accumulator -> exch[row][token] (scaled), then 4 tokens at a time
+            float *exch = red;
             for (int c0 = 0; c0 < n_pad; c0 += 16) {
                 float v[16];
                 tmem_ld16(taddr + c0, v);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) v[k] *= wscale * p.x_inv[c0 + k];
-                if (sg.epi == kEpiSiluPair) {
-                    // up rows live in quadrants 2 and 3: hand them to the gate rows
-                    if (quad >= 2)
-                        for (int k = 0; k < 16; ++k) exch[(r - 64) * kExchStride + c0 + k] = v[k];
-                    named_bar_sync(1, 128);
-                    if (quad < 2 && valid) {
-                        for (int k = 0; k < 16 && c0 + k < p.batch; ++k) {
-                            const float g = v[k], uu = exch[r * kExchStride + c0 + k];
-                            sg.out[(c0 + k) * sg.out_stride + sg.row_offset + row] = g / (1.f + __expf(-g)) * uu;
-                        }
-                    }
-                    named_bar_sync(1, 128);
-                } else if (sg.epi == kEpiLogitsArgmax) {
-                    for (int k = 0; k < 16 && c0 + k < p.batch; ++k) {
-                        const int n = c0 + k;
-                        if (valid) sg.out[n * sg.out_stride + sg.row_offset + row] = v[k];
-                        unsigned long long key = valid ? argmax_key(v[k], sg.row_offset + row) : 0ull;
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-                            key = other > key ? other : key;
-                        }
-                        if (lane == 0 && key) atomicMax(p.argmax_keys + n, key);
-                    }
-                } else {
-                    for (int k = 0; k < 16; ++k) {
-                        const float partner = __shfl_xor_sync(0xffffffffu, v[k], 1);
-                        if (c0 + k < p.batch) mma_epilogue_value(p, sg, row, valid, c0 + k, v[k], partner);
-                    }
-                }
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<float4 *>(exch + r * kExch + c0 + 4 * q) =
+                        make_float4(v[4 * q] * wscale * xinv_s[c0 + 4 * q], v[4 * q + 1] * wscale * xinv_s[c0 + 4 * q + 1],
+                                    v[4 * q + 2] * wscale * xinv_s[c0 + 4 * q + 2],
+                                    v[4 * q + 3] * wscale * xinv_s[c0 + 4 * q + 3]);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + a);
+            named_bar_sync(1, 128);
+            const float *mine = exch + r * kExch;
+            const float *other = exch + (silu ? (r + 64) & 127 : r ^ 1) * kExch;
+            for (int n0 = 0; n0 < p.batch; n0 += 4) {
+                const float4 y = *reinterpret_cast<const float4 *>(mine + n0);
+                const float4 z = (silu || pairs) ? *reinterpret_cast<const float4 *>(other + n0) : y;
+                epi_apply4(p, e, tk, n0, p.batch, y, z, r < 64, lane);
+            }
+            named_bar_sync(1, 128);  // exch is rewritten by the next tile
         }
     } else {
         // ---------------------------------------------------------- dequant
-        const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..255
-        const int row = ct & 127, q = ct >> 7;
-        uint32_t rc = 0, fc = 0;
-        for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-            const int t = u / p.ksplit, sp = u % p.ksplit;
-            const MmaSeg &sg = p.seg[mma_seg_of_tile(p, t)];
-            const float scale = ldexpf(1.0f, p.w[row >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0].scale_exp);
-            const int b0 = sp * p.bps, b1 = min(nb, b0 + p.bps);
-            for (int b = b0; b < b1; ++b) {
-                const int r = rc % kRawStages;
-                mbar_wait_bounded(full_raw + r, (rc / kRawStages) & 1, p.status, cta_abort);
+        // four groups of four warps; group g converts group g of every block
+        // column, warp w covers the rows of TMEM lane quadrant w % 4
+        const int g = (warp - kConvWarp0) / 4;
+        const int row = (warp & 3) * 32 + lane;
+        uint32_t use = 0;
+        int r = 0;
+        for (int t = tile_first; t < p.total_tiles; t += tile_step) {
+            const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
+            const float scale = ldexpf(1.0f, wexp_s[row >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
+            for (int b = b0; b < b1; ++b, ++use) {
+                mbar_wait_bounded(full_raw + r, (use / kRawStages) & 1, p.status, cta_abort);
+                if (use) mbar_wait_bounded(empty + g, (use - 1) & 1, p.status, cta_abort);
                 const uint8_t *raw = smem + L.raw + r * kRawStageBytes;
-                for (int h = 0; h < 2; ++h) {
-                    const int f = fc % kF16Stages;
-                    if (fc >= kF16Stages) mbar_wait_bounded(empty_w16 + f, ((fc / kF16Stages) - 1) & 1, p.status, cta_abort);
-                    uint8_t *w16 = smem + L.w16 + f * kW16Bytes;
-                    if (sg.type == kQ4K) convert_q4(raw, w16, row, q, h, scale);
-                    else convert_q6(raw, w16, row, q, h, b % kUnitBlocks, scale);
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(full_w16 + f);
-                    ++fc;
-                }
+                uint8_t *w16 = smem + L.w16 + g * kW16Bytes;
+                if (sg.type == kQ4K) convert_q4(raw, w16, row, g, scale);
+                else convert_q6(raw, w16, row, g, b % kUnitBlocks, scale);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(empty_raw + r);
-                ++rc;
+                if (lane == 0) {
+                    mbar_arrive(full + g);
+                    mbar_arrive(empty_raw + r);
+                }
+                if (++r == kRawStages) r = 0;
             }
         }
     }
 
     tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
     tc_fence_after();
     if (warp == kMmaWarp)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
@@ -603,10 +795,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
 
 // --------------------------------------------------------- activation prep --
 
-// One CTA per token: the GEMV prologue's arithmetic (RMSNorm in the
-// reference's reduction order, per-32 int8 quantisation) then x^ = q * scale
-// (DP4A semantics) or x (FP32 semantics), times 2^kx so that max|x^| lies in
-// [2^14, 2^15), rounded to fp16 into the MMA layout.
+// One CTA per token: the GEMV prologue's arithmetic (RMSNorm, the reference's
+// per-32 int8 quantisation) then x^ = q * scale (DP4A semantics) or x (FP32
+// semantics), times 2^kx so that max|x^| lies in [2^14, 2^15), rounded to
+// fp16 into the MMA layout: chunk c (64 wide) is [n/8][core j][n%8][8 values]
+// with core j holding 64c + 4j + {0,2,1,3} and 64c + 32 + 4j + {0,2,1,3}.
+// Each thread owns cores; the 8 cores of a chunk sit on 8 adjacent lanes, so
+// a 32-wide quantisation group is an 8-lane shuffle reduction.
 __global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
                                 int n_pad, int use_dp4a, uint8_t *x16, float *x_inv) {
     pdl_trigger();
@@ -615,12 +810,12 @@ __global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm
     __shared__ float red[256];
     __shared__ float amax_s[8];
     const long chunk_bytes = static_cast<long>(n_pad) * kKChunk * 2;
-    auto dst_of = [&](int k) -> uint8_t * {  // 16 bytes holding positions k..k+7 of token n
-        const int c = k / kKChunk, kc = (k % kKChunk) / 8;
-        return x16 + c * chunk_bytes + (n >> 3) * 2048 + kc * 128 + (n & 7) * 16;
+    const int cores = cols / 8;
+    auto dst_of = [&](int core) -> uint8_t * {
+        return x16 + (core >> 3) * chunk_bytes + (n >> 3) * kGroupStride + (core & 7) * kCoreStride + (n & 7) * 16;
     };
     if (n >= batch) {
-        for (int k = tid * 8; k < cols; k += 256 * 8) *reinterpret_cast<uint4 *>(dst_of(k)) = make_uint4(0, 0, 0, 0);
+        for (int c = tid; c < cores; c += 256) *reinterpret_cast<uint4 *>(dst_of(c)) = make_uint4(0, 0, 0, 0);
         if (tid == 0) x_inv[n] = 0.f;
         return;
     }
@@ -639,32 +834,42 @@ __global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm
     }
     // pass 1: values and the token's max |x^|
     float local_max = 0.f;
-    const int chunks = cols / 8;
-    float vals[kMaxCols / (256 * 8)][8];
-    for (int j = 0; j < kMaxCols / (256 * 8); ++j) {
-        const int c = tid + 256 * j;
-        if (c >= chunks) continue;
+    constexpr int kPer = kMaxCols / (256 * 8);
+    float vals[kPer][8];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int core = tid + 256 * j;
+        if (core >= cores) continue;
+        const int k0 = (core >> 3) * 64 + (core & 7) * 4;  // first of the low four; +32 for the high four
         float v[8];
-        const float4 a = *reinterpret_cast<const float4 *>(xr + c * 8);
-        const float4 b = *reinterpret_cast<const float4 *>(xr + c * 8 + 4);
+        const float4 a = *reinterpret_cast<const float4 *>(xr + k0);
+        const float4 b = *reinterpret_cast<const float4 *>(xr + k0 + 32);
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         if (norm_w) {
-            const float4 wa = *reinterpret_cast<const float4 *>(norm_w + c * 8);
-            const float4 wb = *reinterpret_cast<const float4 *>(norm_w + c * 8 + 4);
+            const float4 wa = *reinterpret_cast<const float4 *>(norm_w + k0);
+            const float4 wb = *reinterpret_cast<const float4 *>(norm_w + k0 + 32);
             const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], r), w8[e]);
         }
         if (use_dp4a) {
-            // quantize_x32_cuda (inferencer.cu:544-556) over the 32-value group = 4 lanes
-            float am = 0.f;
+            // quantize_x32_cuda (inferencer.cu:544-556): groups 64c..64c+31 (v[0..3] of
+            // the chunk's 8 lanes) and 64c+32..64c+63 (v[4..7])
+            float am0 = 0.f, am1 = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(v[e]));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-            const float scale = am > 0.f ? am / 127.f : 1.f;
+            for (int e = 0; e < 4; ++e) {
+                am0 = fmaxf(am0, fabsf(v[e]));
+                am1 = fmaxf(am1, fabsf(v[4 + e]));
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, o));
+                am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, o));
+            }
+            const float sc0 = am0 > 0.f ? am0 / 127.f : 1.f, sc1 = am1 > 0.f ? am1 / 127.f : 1.f;
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
+                const float scale = e < 4 ? sc0 : sc1;
                 int q = __float2int_rn(v[e] / scale);
                 q = max(-127, min(127, q));
                 v[e] = static_cast<float>(q) * scale;
@@ -685,12 +890,14 @@ __global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm
     if (amax > 0.f) frexpf(amax, &e2);
     const int kx = amax > 0.f ? 15 - e2 : 0;  // amax * 2^kx in [2^14, 2^15)
     const float up = ldexpf(1.0f, kx);
-    for (int j = 0; j < kMaxCols / (256 * 8); ++j) {
-        const int c = tid + 256 * j;
-        if (c >= chunks) continue;
-        const uint4 o = make_uint4(pack_half2(vals[j][0] * up, vals[j][1] * up), pack_half2(vals[j][2] * up, vals[j][3] * up),
-                                   pack_half2(vals[j][4] * up, vals[j][5] * up), pack_half2(vals[j][6] * up, vals[j][7] * up));
-        *reinterpret_cast<uint4 *>(dst_of(c * 8)) = o;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int core = tid + 256 * j;
+        if (core >= cores) continue;
+        const float *v = vals[j];
+        const uint4 o = make_uint4(pack_half2(v[0] * up, v[2] * up), pack_half2(v[1] * up, v[3] * up),
+                                   pack_half2(v[4] * up, v[6] * up), pack_half2(v[5] * up, v[7] * up));
+        *reinterpret_cast<uint4 *>(dst_of(core)) = o;
     }
     if (tid == 0) x_inv[n] = ldexpf(1.0f, -kx);
 }
@@ -779,34 +986,83 @@ int mma_make_weight(int type, const void *data, int rows, long row_bytes, int ro
     return r;
 }
 
+// Clusters of k CTAs (one CTA per SM) that can be resident at once, k = 1..8.
+static int g_cluster_cap[kMaxCluster + 1];
+static std::mutex g_cap_mu;
+
 cudaError_t mma_prepare() {
-    return cudaFuncSetAttribute(mma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem().total);
+    cudaError_t e =
+        cudaFuncSetAttribute(mma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem().total);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_cap_mu);
+    int dev = 0, sms = 0;
+    e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    g_cluster_cap[1] = sms;
+    for (int k = 2; k <= kMaxCluster; ++k) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(k);
+        cfg.blockDim = dim3(kMmaThreads);
+        cfg.dynamicSmemBytes = mma_smem().total;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = k;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, mma_gemm_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        g_cluster_cap[k] = n;
+    }
+    return cudaSuccess;
 }
 
-int mma_choose_split(int tiles, int nblocks, int num_sms, int *bps) {
-    int ks = (num_sms + tiles - 1) / tiles;
-    if (ks > nblocks) ks = nblocks;
-    if (ks < 1) ks = 1;
-    *bps = (nblocks + ks - 1) / ks;
-    return (nblocks + *bps - 1) / *bps;
+int mma_choose_split(int tiles, int nblocks, int *bps) {
+    // cost ~ waves of clusters x block columns per part, plus about one block
+    // column's time for the cluster reduction when the K range is split
+    int best_k = 1, best_cost = 0;
+    for (int k = 1; k <= kMaxCluster && k <= nblocks; ++k) {
+        const int per = (nblocks + k - 1) / k;
+        if ((nblocks + per - 1) / per != k) continue;  // every part non-empty
+        if (k > 1 && !split_fits(k)) continue;
+        const int cap = g_cluster_cap[k];
+        if (cap < 1) continue;
+        const int waves = (tiles + cap - 1) / cap;
+        const int cost = waves * per + (k > 1 ? 1 : 0);
+        if (k == 1 || cost < best_cost) {
+            best_k = k;
+            best_cost = cost;
+        }
+    }
+    *bps = (nblocks + best_k - 1) / best_k;
+    return best_k;
 }
 
-cudaError_t mma_gemm_launch(const MmaParams &p, int num_sms, cudaStream_t stream) {
+cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream) {
     if (p.n_pad < 16 || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.cols % 256 || p.total_tiles < 1 || p.ksplit < 1 ||
-        p.bps < 1 || (p.ksplit > 1 && (!p.partial || !p.counters)))
+        p.ksplit > kMaxCluster || p.bps < 1 || (p.ksplit - 1) * p.bps >= p.cols / 256 ||
+        p.ksplit * p.bps < p.cols / 256 || g_cluster_cap[p.ksplit] < 1 || (p.ksplit > 1 && !split_fits(p.ksplit)))
         return cudaErrorInvalidValue;
-    const int units = p.total_tiles * p.ksplit;
-    const int grid = num_sms < units ? num_sms : units;
+    const int clusters = p.total_tiles < g_cluster_cap[p.ksplit] ? p.total_tiles : g_cluster_cap[p.ksplit];
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(clusters * p.ksplit);
     cfg.blockDim = dim3(kMmaThreads);
     cfg.dynamicSmemBytes = mma_smem().total;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = p.ksplit;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, mma_gemm_kernel, p);
 }
 

@@ -12,7 +12,6 @@ namespace ijb {
 constexpr int kMmaTileM = 128;    // weight rows per tile (TMEM lanes)
 constexpr int kMmaMaxN = 64;      // tokens per launch (MMA N, padded to 16)
 constexpr int kMmaMinBatch = 16;  // below this the CUDA-core GEMV is used
-constexpr int kMmaCounters = 4096;  // split-K tile counters (tiles of one launch)
 
 // One weight matrix as the tensor-core path reads it: TMA descriptors over
 // its rows (Q4_K: one box per 144-byte block; Q6_K: one box per 208-byte
@@ -41,13 +40,10 @@ struct MmaParams {
     MmaSeg seg[kMaxSegs];
     int nseg;
     int total_tiles;
-    // split-K: each tile's K range is cut into ksplit parts of bps blocks; a
-    // part's fp32 partial goes to `partial` and the last part to finish sums
-    // them in part order and applies the epilogue (counters[tile] counts)
+    // split K: each tile's K range is cut into ksplit parts of bps block
+    // columns, run by the ksplit CTAs of one cluster (mma_choose_split)
     int ksplit;
     int bps;
-    float *partial;  // [tiles * ksplit][n_pad][128]
-    int *counters;   // [tiles], zero between launches
     int cols;             // K
     int batch;            // tokens in this launch (<= kMmaMaxN)
     int n_pad;            // MMA N: batch rounded up to 16
@@ -86,10 +82,14 @@ cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks_gguf_
 int mma_make_weight(int type, const void *data, int rows, long row_bytes, int rows_per_box, MmaWeight *out,
                     char *err, int err_len);
 
-cudaError_t mma_gemm_launch(const MmaParams &p, int num_sms, cudaStream_t stream);
-// Parts per tile for a launch of `tiles` tiles of `nblocks` K-blocks, so that
-// tiles * ksplit roughly fills the GPU; *bps receives blocks per part.
-int mma_choose_split(int tiles, int nblocks, int num_sms, int *bps);
+cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream);
+// Parts per tile (the cluster size) for a launch of `tiles` tiles of
+// `nblocks` 256-wide block columns, from how many clusters of each size fit
+// on the GPU at once; *bps receives block columns per part.  Needs
+// mma_prepare() first.
+int mma_choose_split(int tiles, int nblocks, int *bps);
+// Sets the kernel's shared-memory limit and measures cluster occupancy for
+// the current device.
 cudaError_t mma_prepare();
 int mma_smem_bytes();
 
