@@ -113,6 +113,8 @@ struct ijb_engine {
     int *attn_counters = nullptr;
     uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
     float *x_inv = nullptr;
+    float *mma_scratch = nullptr;  // split-K partial sums of the tensor-core path
+    long mma_scratch_floats = 0;
     int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
     uint32_t *status = nullptr;
@@ -120,7 +122,8 @@ struct ijb_engine {
 
     std::unordered_map<int, StepGraph> graphs;  // key: n * 2 + need_logits
     cudaEvent_t ev_start = nullptr, ev_end = nullptr;
-    bool pdl = false;  // programmatic dependent launch between the step's kernels
+    bool pdl = false;      // programmatic dependent launch between the step's kernels
+    bool mma_pdl = true;   // the same for the tensor-core path's prep and GEMM launches
     float last_step_ms = 0.f;
     std::string err;
     int last_n = 0;
@@ -230,7 +233,7 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             const int tn = std::min(kMmaMaxN, gn - t0);
             const int n_pad = (tn + 15) / 16 * 16;
             ck(mma_prep_launch(x + static_cast<long>(t0) * x_stride, x_stride, norm_w, d.eps, cols, tn, n_pad, dp,
-                               e->x16, e->x_inv, s),
+                               e->x16, e->x_inv, s, e->mma_pdl),
                "activation prep launch");
             MmaParams m;
             std::memset(&m, 0, sizeof(m));
@@ -275,7 +278,13 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.argmax_keys = e->keys + g0 + t0;
             m.status = e->status;
             m.ksplit = mma_choose_split(m.total_tiles, cols / 256, &m.bps);
-            ck(mma_gemm_launch(m, s), "tensor-core GEMM launch");
+            m.scratch = e->mma_scratch;
+            m.scratch_floats = e->mma_scratch_floats;
+            if (m.ksplit > 1 && static_cast<long>(m.total_tiles) * m.ksplit * kMmaTileM * n_pad > m.scratch_floats) {
+                m.ksplit = 1;  // more partials than the scratch holds: one part per tile
+                m.bps = cols / 256;
+            }
+            ck(mma_gemm_launch(m, s, e->mma_pdl), "tensor-core GEMM launch");
             g_launches += 2;
         }
         return;
@@ -494,6 +503,10 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             // the 1B model took 0.98 ms with it and 0.79 ms without.
             const char *env = std::getenv("IJB_PDL");
             e->pdl = env && env[0] == '1';
+            // IJB_MMA_PDL=0 turns it off for the tensor-core path, where the next
+            // GEMM's weight loads and dequantisation overlap the previous kernel
+            const char *env2 = std::getenv("IJB_MMA_PDL");
+            e->mma_pdl = !(env2 && env2[0] == '0');
         }
         ck(attention_prepare(), "attention attributes");
         ck(cudaEventCreate(&e->ev_start), "event");
@@ -611,6 +624,9 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
             ck(cudaMemset(e->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
             e->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
+            // split launches have at most about two parts per SM
+            e->mma_scratch_floats = 2L * e->num_sms * kMmaTileM * kMmaMaxN;
+            e->mma_scratch = dev_alloc<float>(e->mma_scratch_floats, "split-K partials");
             const char *env = std::getenv("IJB_MMA_MIN_BATCH");  // diagnostic: path switch-over point
             if (env) e->mma_min_batch = std::max(1, std::atoi(env));
         }
@@ -709,6 +725,7 @@ void ijb_destroy(ijb_engine *e) {
     if (e->next_host) cudaFreeHost(e->next_host);
     cudaFree(e->x16);
     cudaFree(e->x_inv);
+    cudaFree(e->mma_scratch);
     cudaFree(e->attn_partial);
     cudaFree(e->attn_counters);
     cudaFree(e->status);

@@ -44,27 +44,26 @@
 namespace ijb {
 
 constexpr int kKChunk = 64;  // K per fp16 stage: one Q4_K group of 64 weights
-constexpr int kStages = 4;   // fp16 weight + activation stages: the 4 groups of one block column
-constexpr int kRawStages = 3;
+constexpr int kGroups = 4;   // 64-wide groups of a 256-wide block column
+constexpr int kStages = 8;   // fp16 weight + activation stages: two block columns in flight
+constexpr int kRawStages = 4;
 constexpr int kRawStageBytes = 128 * 208 + 128 * 16;  // Q6_K bodies + d (Q4_K uses 128 * 144)
 constexpr int kQ6DOff = 128 * 208;                    // d box within a Q6_K raw stage
-constexpr int kW16Bytes = kMmaTileM * kKChunk * 2;    // 16 KB
+constexpr uint32_t kTmemCols = 512;                   // accumulators [0, 128), fp16 weight stages [128, 384)
+constexpr uint32_t kTmemA = 128;                      // first column of the weight stages (32 per stage)
 constexpr int kX16Bytes = kMmaMaxN * kKChunk * 2;     // 8 KB
 constexpr int kCoreStride = 128;                      // bytes between 8-wide K cores
 constexpr int kGroupStride = (kKChunk / 8) * 128;     // bytes between 8-row groups (1 KB)
 constexpr int kMaxCluster = 8;
-// split K: a CTA receives [part][128 rows][slice tokens] fp32 partials (slice
-// = ceil(batch / parts) rounded up to 4, row stride padded to an odd number of
-// 16-byte units when that fits, for conflict-free vector access); the
-// unsplit epilogue uses the same buffer as [128 rows][kExch] floats
-constexpr int kRedBytes = 45 * 1024;
-constexpr int kExch = kMmaMaxN + 4;  // 68 floats: 17 x 16 B per row
+// the unsplit epilogue's copy of the accumulator, [128 rows][kExch] floats
+constexpr int kExch = kMmaMaxN + 4;  // 68 floats: 17 x 16 B per row (conflict-free vector access)
+constexpr int kRedBytes = kMmaTileM * kExch * 4;
 constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kXWarp = 6, kConvWarp0 = 7, kConvWarps = 16;
 constexpr int kMmaThreads = (kConvWarp0 + kConvWarps) * 32;
-constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 2;
+constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 1;
 
 struct MmaSmem {
-    int raw, w16, x16, red, tok, segs, bars, tmem, total;
+    int raw, x16, red, tok, segs, bars, tmem, total;
 };
 
 __host__ __device__ constexpr MmaSmem mma_smem() {
@@ -72,14 +71,12 @@ __host__ __device__ constexpr MmaSmem mma_smem() {
     int off = 0;
     L.raw = off;
     off += kRawStages * kRawStageBytes;
-    L.w16 = off;
-    off += kStages * kW16Bytes;
     L.x16 = off;
     off += kStages * kX16Bytes;
     L.red = off;
     off += kRedBytes;
-    L.tok = off;  // x_inv, positions and KV slots of the launch's tokens
-    off += 3 * kMmaMaxN * 4;
+    L.tok = off;  // x_inv, positions and KV slots of the launch's tokens, then argmax keys
+    off += 3 * kMmaMaxN * 4 + kMmaMaxN * 8;
     L.segs = off;  // the launch's segments and weight scale exponents
     off += kMaxSegs * static_cast<int>(sizeof(MmaSeg)) + 2 * kMaxSegs * 4;
     off = (off + 7) / 8 * 8;
@@ -93,14 +90,8 @@ __host__ __device__ constexpr MmaSmem mma_smem() {
 static_assert(mma_smem().total <= 227 * 1024, "shared memory of the tensor-core GEMM");
 static_assert(kMmaTileM * kExch * 4 <= kRedBytes, "the accumulator copy lives in the partial-sum buffer");
 
-// Tokens per part's slice and the row stride (floats) of the split-K buffer.
+// Tokens per part's epilogue slice (a multiple of 4).
 __host__ __device__ constexpr int split_per(int batch, int parts) { return ((batch + parts - 1) / parts + 3) / 4 * 4; }
-__host__ __device__ constexpr int split_stride(int per, int parts) {
-    return ((per / 4) % 2 == 0 && parts * kMmaTileM * (per + 4) * 4 <= kRedBytes) ? per + 4 : per;
-}
-__host__ __device__ constexpr bool split_fits(int parts) {
-    return parts * kMmaTileM * split_stride(split_per(kMmaMaxN, parts), parts) * 4 <= kRedBytes;
-}
 
 int mma_smem_bytes() { return mma_smem().total; }
 
@@ -138,6 +129,16 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
         : "memory");
 }
 
+// Same with A (M x K fp16, rows in TMEM lanes, two K elements per column) in TMEM.
+__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -154,6 +155,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Lane (warp quadrant + lane) of TMEM gets 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
@@ -195,9 +203,6 @@ __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
-}
-__device__ __forceinline__ void dsmem_st4(uint32_t addr, float a, float b, float c, float d) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 // Arrives on the mbarrier at `bar` in CTA `rank`, releasing this thread's
 // earlier writes (and those it has synchronised with) at cluster scope.
@@ -275,7 +280,7 @@ __device__ __forceinline__ int tile_row(const MmaSeg &s, int lt, int r, bool &va
 // (d*sc)*q - dmin*m as in q4_value (inferencer.cu:454-471), with the scale
 // products rounded to fp16 and one fp16 rounding of the result; q comes out
 // exact (1024 + q minus 1024, or (1024 + 16q) / 16 - 64).
-__device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int row, int g, float scale) {
+__device__ __forceinline__ void convert_q4(const uint8_t *raw, uint32_t tmem_row, int row, int g, float scale) {
     const uint8_t *bp = raw + row * 144;
     const uint4 hdr = *reinterpret_cast<const uint4 *>(bp);
     const uint4 qa = *reinterpret_cast<const uint4 *>(bp + 16 + g * 32);
@@ -303,20 +308,22 @@ __device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int
     const __half2 n2b = __float2half2_rn(-(dmin * static_cast<float>(m[1]) * scale));
     const __half2 k1024 = __float2half2_rn(1024.f), k16th = __float2half2_rn(0.0625f), km64 = __float2half2_rn(-64.f);
     const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    uint8_t *dst = w16 + (row >> 3) * kGroupStride + (row & 7) * 16;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const uint32_t w = words[j], w8 = w >> 8;
-        const __half2 qa02 = __hsub2(bits_h2((w & 0x000F000Fu) | 0x64006400u), k1024);
-        const __half2 qa13 = __hsub2(bits_h2((w8 & 0x000F000Fu) | 0x64006400u), k1024);
-        const __half2 qb02 = __hfma2(bits_h2((w & 0x00F000F0u) | 0x64006400u), k16th, km64);
-        const __half2 qb13 = __hfma2(bits_h2((w8 & 0x00F000F0u) | 0x64006400u), k16th, km64);
-        uint4 o;
-        o.x = h2_bits(__hfma2(qa02, s1a, n2a));
-        o.y = h2_bits(__hfma2(qa13, s1a, n2a));
-        o.z = h2_bits(__hfma2(qb02, s1b, n2b));
-        o.w = h2_bits(__hfma2(qb13, s1b, n2b));
-        *reinterpret_cast<uint4 *>(dst + j * kCoreStride) = o;
+    for (int j2 = 0; j2 < 8; j2 += 2) {  // two 8-wide cores = 8 TMEM columns per store
+        uint32_t o[8];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t w = words[j2 + h], w8 = w >> 8;
+            const __half2 qa02 = __hsub2(bits_h2((w & 0x000F000Fu) | 0x64006400u), k1024);
+            const __half2 qa13 = __hsub2(bits_h2((w8 & 0x000F000Fu) | 0x64006400u), k1024);
+            const __half2 qb02 = __hfma2(bits_h2((w & 0x00F000F0u) | 0x64006400u), k16th, km64);
+            const __half2 qb13 = __hfma2(bits_h2((w8 & 0x00F000F0u) | 0x64006400u), k16th, km64);
+            o[4 * h + 0] = h2_bits(__hfma2(qa02, s1a, n2a));
+            o[4 * h + 1] = h2_bits(__hfma2(qa13, s1a, n2a));
+            o[4 * h + 2] = h2_bits(__hfma2(qb02, s1b, n2b));
+            o[4 * h + 3] = h2_bits(__hfma2(qb13, s1b, n2b));
+        }
+        tmem_st8(tmem_row + static_cast<uint32_t>(j2 * 4), o);
     }
 }
 
@@ -327,7 +334,7 @@ __device__ __forceinline__ void convert_q4(const uint8_t *raw, uint8_t *w16, int
 // or 1024 + 16q for the high nibbles), q - 32 is exact, and one fp16 multiply
 // by d*scale (rounded to fp16) gives the weight of q6_value
 // (inferencer.cu:473-487) with two roundings.
-__device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int row, int g, int lb, float scale) {
+__device__ __forceinline__ void convert_q6(const uint8_t *raw, uint32_t tmem_row, int row, int g, int lb, float scale) {
     const uint8_t *body = raw + row * 208;
     const int h = g >> 1, hi = g & 1;
     const uint4 *A = reinterpret_cast<const uint4 *>(body) + 2 * h;
@@ -336,7 +343,6 @@ __device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int
     const uint2 scw = *reinterpret_cast<const uint2 *>(body + 192 + 8 * h);
     const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(raw + kQ6DOff + row * 16 + lb * 2)) * scale;
     const __half2 k1056 = __float2half2_rn(1056.f), k16th = __float2half2_rn(0.0625f), km96 = __float2half2_rn(-96.f);
-    uint8_t *dst = w16 + (row >> 3) * kGroupStride + (row & 7) * 16;
 #pragma unroll 1
     for (int l2 = 0; l2 < 2; ++l2) {
         const uint32_t s4 = l2 ? scw.y : scw.x;
@@ -345,6 +351,7 @@ __device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int
         const uint4 a4 = A[l2], b4 = B[l2], h4 = H[l2];
         const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w}, bw[4] = {b4.x, b4.y, b4.z, b4.w};
         const uint32_t hw[4] = {h4.x, h4.y, h4.z, h4.w};
+        uint32_t o[8];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const uint32_t a = aw[jj], b = bw[jj], q = hw[jj];
@@ -362,12 +369,11 @@ __device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int
                 v02b = __hfma2(bits_h2((b & 0x00F000F0u) | (qp2 & 0x03000300u) | 0x64006400u), k16th, km96);
                 v13b = __hfma2(bits_h2((b8 & 0x00F000F0u) | (qm6 & 0x03000300u) | 0x64006400u), k16th, km96);
             }
-            uint4 o;
-            o.x = h2_bits(__hmul2(v02a, sa));
-            o.y = h2_bits(__hmul2(v13a, sa));
-            o.z = h2_bits(__hmul2(v02b, sb));
-            o.w = h2_bits(__hmul2(v13b, sb));
-            *reinterpret_cast<uint4 *>(dst + (4 * l2 + jj) * kCoreStride) = o;
+            o[4 * (jj & 1) + 0] = h2_bits(__hmul2(v02a, sa));
+            o[4 * (jj & 1) + 1] = h2_bits(__hmul2(v13a, sa));
+            o[4 * (jj & 1) + 2] = h2_bits(__hmul2(v02b, sb));
+            o[4 * (jj & 1) + 3] = h2_bits(__hmul2(v13b, sb));
+            if (jj & 1) tmem_st8(tmem_row + static_cast<uint32_t>((4 * l2 + jj - 1) * 4), o);
         }
     }
 }
@@ -382,9 +388,10 @@ __device__ __forceinline__ void convert_q6(const uint8_t *raw, uint8_t *w16, int
 // writer per element, so the result is the plain fp32 sum).
 
 struct EpiTok {
-    const float *x_inv;  // [n_pad]
-    const int *pos;      // [n_pad]
-    const int *slot;     // [n_pad]
+    const float *x_inv;         // [n_pad]
+    const int *pos;             // [n_pad]
+    const int *slot;            // [n_pad]
+    unsigned long long *keys;   // [n_pad] this CTA's best logits key per token (shared memory)
 };
 
 // Per tile row: output pointer for token 0 and everything the operation needs.
@@ -487,7 +494,7 @@ __device__ __forceinline__ void epi_apply4(const MmaParams &p, const EpiRow &e, 
                     const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
                     key = other > key ? other : key;
                 }
-                if (lane == 0 && key) atomicMax(p.argmax_keys + n0 + k, key);
+                if (lane == 0 && key) atomicMax(tk.keys + n0 + k, key);  // flushed once at the end
             }
             break;
         default:
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
     uint64_t *full_raw = bars, *empty_raw = full_raw + kRawStages;
     uint64_t *full = empty_raw + kRawStages, *empty = full + kStages;  // fp16 weight + activation stage
     uint64_t *acc_full = empty + kStages, *acc_empty = acc_full + 2;
-    uint64_t *part_ready = acc_empty + 2, *part_free = part_ready + 1;
+    uint64_t *part_ready = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem);
     uint32_t *cta_abort = tmem_slot + 1;
     float *red = reinterpret_cast<float *>(smem + L.red);
@@ -516,7 +523,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
     const int rank = static_cast<int>(cluster_rank());
     const int tile_first = static_cast<int>(cluster_id()), tile_step = static_cast<int>(cluster_count());
     const int b0 = rank * p.bps, b1 = min(nb, b0 + p.bps);  // this part's block columns
-    const uint32_t tmem_cols = n_pad * 2 <= 32 ? 32 : (n_pad * 2 <= 64 ? 64 : 128);
+    const uint32_t tmem_cols = kTmemCols;
 
     MmaSeg *seg_s = reinterpret_cast<MmaSeg *>(smem + L.segs);
     int *wexp_s = reinterpret_cast<int *>(seg_s + kMaxSegs);
@@ -542,7 +549,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             mbar_init(empty_raw + i, kConvWarps);
         }
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(full + i, kConvWarps / kStages + 1);  // the group's warps + the activation copy
+            mbar_init(full + i, kConvWarps / kGroups + 1);  // the group's warps + the activation copy
             mbar_init(empty + i, 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -550,7 +557,6 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             mbar_init(acc_empty + i, 4);
         }
         mbar_init(part_ready, ksplit);
-        mbar_init(part_free, ksplit);
         fence_barrier_init();
     }
     if (warp == kMmaWarp) {
@@ -602,15 +608,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
     } else if (warp == kXWarp) {
         if (lane == 0) {
             pdl_wait();  // the activation is written by the previous kernel
-            uint32_t use = 0;  // block columns done: stage g's use count
+            // block column B (counted over this CTA's work) uses stages (B & 1) * 4 + g,
+            // each for the (B >> 1)-th time
+            uint32_t blk = 0;
             const uint32_t xbytes = static_cast<uint32_t>(n_pad) * kKChunk * 2;
             for (int t = tile_first; t < p.total_tiles; t += tile_step) {
-                for (int b = b0; b < b1; ++b, ++use) {
-                    for (int g = 0; g < kStages; ++g) {
-                        if (use) mbar_wait_bounded(empty + g, (use - 1) & 1, p.status, cta_abort);
-                        mbar_arrive_expect_tx(full + g, xbytes);
-                        bulk_g2s(smem + L.x16 + g * kX16Bytes, p.x16 + static_cast<long>(b * kStages + g) * xbytes,
-                                 xbytes, full + g);
+                for (int b = b0; b < b1; ++b, ++blk) {
+                    const uint32_t use = blk >> 1;
+                    for (int g = 0; g < kGroups; ++g) {
+                        const int st = (blk & 1) * kGroups + g;
+                        if (use) mbar_wait_bounded(empty + st, (use - 1) & 1, p.status, cta_abort);
+                        mbar_arrive_expect_tx(full + st, xbytes);
+                        bulk_g2s(smem + L.x16 + st * kX16Bytes, p.x16 + static_cast<long>(b * kGroups + g) * xbytes,
+                                 xbytes, full + st);
                     }
                 }
             }
@@ -619,29 +629,31 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
         if (lane == 0) {
             // D (fp32) [128 x n_pad] = A (fp16, K-major) * B (fp16, K-major)^T
             const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(n_pad >> 3) << 17) | (8u << 24);
-            const uint64_t a_desc0 = umma_desc(smem_u32(smem + L.w16), kCoreStride, kGroupStride);
             const uint64_t b_desc0 = umma_desc(smem_u32(smem + L.x16), kCoreStride, kGroupStride);
-            uint32_t use = 0, i = 0;
+            uint32_t blk = 0, i = 0;
             for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
                 const int a = i & 1;
                 if (i >= 2) mbar_wait_bounded(acc_empty + a, ((i >> 1) - 1) & 1, p.status, cta_abort);
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + static_cast<uint32_t>(a * n_pad);
                 uint32_t accumulate = 0;
-                for (int b = b0; b < b1; ++b, ++use) {
+                for (int b = b0; b < b1; ++b, ++blk) {
+                    const uint32_t ph = (blk >> 1) & 1;
 #pragma unroll
-                    for (int g = 0; g < kStages; ++g) {
-                        mbar_wait_bounded(full + g, use & 1, p.status, cta_abort);
+                    for (int g = 0; g < kGroups; ++g) {
+                        const int st = (blk & 1) * kGroups + g;
+                        mbar_wait_bounded(full + st, ph, p.status, cta_abort);
                         tc_fence_after();
-                        // descriptor address fields advance by 16 B units: stage g, then K=16 steps of 256 B
-                        const uint64_t ad = a_desc0 + static_cast<uint64_t>(g * (kW16Bytes >> 4));
-                        const uint64_t bd = b_desc0 + static_cast<uint64_t>(g * (kX16Bytes >> 4));
+                        // A: stage st's 32 TMEM columns, 8 per K=16 step; B: the descriptor's
+                        // address field advances by 16 B units (stage, then 256 B per K=16 step)
+                        const uint32_t ta = tmem_base + kTmemA + static_cast<uint32_t>(st * 32);
+                        const uint64_t bd = b_desc0 + static_cast<uint64_t>(st * (kX16Bytes >> 4));
 #pragma unroll
                         for (int kk = 0; kk < kKChunk / 16; ++kk) {
-                            umma_f16(dcol, ad + kk * 16, bd + kk * 16, idesc, accumulate);
+                            umma_f16_ta(dcol, ta + kk * 8, bd + kk * 16, idesc, accumulate);
                             accumulate = 1u;
                         }
-                        umma_commit(empty + g);
+                        umma_commit(empty + st);
                     }
                 }
                 umma_commit(acc_full + a);
@@ -654,15 +666,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
         pdl_wait();
         float *xinv_s = reinterpret_cast<float *>(smem + L.tok);
         int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxN), *slot_s = pos_s + kMmaMaxN;
+        unsigned long long *keys_s = reinterpret_cast<unsigned long long *>(slot_s + kMmaMaxN);
         if (r < n_pad) {
             xinv_s[r] = p.x_inv[r];
             pos_s[r] = p.tok_pos && r < p.batch ? p.tok_pos[r] : 0;
             slot_s[r] = p.tok_slot && r < p.batch ? p.tok_slot[r] : 0;
+            keys_s[r] = 0ull;
         }
         named_bar_sync(1, 128);
-        const EpiTok tk{xinv_s, pos_s, slot_s};
-        const int per = split_per(p.batch, ksplit), stride = split_stride(per, ksplit);  // split-K slices
-        const int chunks = n_pad / 16;
+        const EpiTok tk{xinv_s, pos_s, slot_s, keys_s};
+        bool any_logits = false;
+        const int per = split_per(p.batch, ksplit);  // tokens of each part's epilogue slice
         uint32_t i = 0;
         for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
             const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
@@ -674,28 +688,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             const int row = tile_row(sg, lt, r, valid);
             const EpiRow e = make_epi_row(p, sg, row, valid);
             const bool silu = sg.epi == kEpiSiluPair, pairs = sg.epi == kEpiRopeQ || sg.epi == kEpiRopeKCache;
+            any_logits |= sg.epi == kEpiLogitsArgmax;
             const float wscale = ldexpf(1.0f, -wexp_s[r >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * n_pad;
             if (ksplit > 1) {
-                // the owners have finished reading what this CTA pushed for the previous tile
-                bool ok = i == 0 || mbar_wait_cluster_bounded(part_free, (i - 1) & 1, p.status, cta_abort);
-                // push: tokens n..n+3 go to owner o = n / per, at red[rank][r][n - o * per] there;
-                // each part starts at a different chunk so the owners are written in turn
-                const uint32_t red_row = smem_u32(red) + static_cast<uint32_t>((rank * 128 + r) * stride * 4);
-                for (int cc = 0; cc < chunks && ok; ++cc) {
-                    const int c0 = ((cc + rank) % chunks) * 16;
-                    if (c0 >= p.batch) continue;
+                // this part's partial sums -> scratch[tile][part][row][token] (L2), then the
+                // parts signal each other; part s applies the epilogue to its token slice,
+                // summing the parts in part order (the result does not depend on timing)
+                float *dst = p.scratch + ((static_cast<long>(t) * ksplit + rank) * 128 + r) * n_pad;
+                for (int c0 = 0; c0 < n_pad; c0 += 16) {
                     float v[16];
                     tmem_ld16(taddr + c0, v);
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const int n = c0 + 4 * q;
-                        if (n < p.batch) {
-                            const int o = n / per;
-                            dsmem_st4(dsmem_addr(red_row + static_cast<uint32_t>((n - o * per) * 4), o),
-                                      v[4 * q] * wscale * xinv_s[n], v[4 * q + 1] * wscale * xinv_s[n + 1],
-                                      v[4 * q + 2] * wscale * xinv_s[n + 2], v[4 * q + 3] * wscale * xinv_s[n + 3]);
-                        }
+                        __stcg(reinterpret_cast<float4 *>(dst + n),
+                               make_float4(v[4 * q] * wscale * xinv_s[n], v[4 * q + 1] * wscale * xinv_s[n + 1],
+                                           v[4 * q + 2] * wscale * xinv_s[n + 2], v[4 * q + 3] * wscale * xinv_s[n + 3]));
                     }
                 }
                 tc_fence_before();
@@ -706,28 +715,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
                     asm volatile("fence.acq_rel.cluster;" ::: "memory");
                     for (int s = 0; s < ksplit; ++s) mbar_arrive_remote(part_ready, s);
                 }
-                ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort) && ok;
+                const bool ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort);
                 const int n_lo = min(p.batch, rank * per), n_end = min(p.batch, n_lo + per);
-                // this CTA's tokens, summed over the parts in part order
-                const float *mine = red + r * stride, *zrow = red + ((r + 64) & 127) * stride;
-                for (int t0 = 0; ok && n_lo + t0 < n_end; t0 += 4) {
+                const float *base = p.scratch + static_cast<long>(t) * ksplit * 128 * n_pad;
+                const float *mine = base + static_cast<long>(r) * n_pad, *zrow = base + static_cast<long>((r + 64) & 127) * n_pad;
+                for (int t0 = n_lo; ok && t0 < n_end; t0 += 4) {
                     float4 y = make_float4(0.f, 0.f, 0.f, 0.f), z = y;
                     for (int s = 0; s < ksplit; ++s) {
-                        const float4 v = *reinterpret_cast<const float4 *>(mine + s * 128 * stride + t0);
+                        const float4 v = __ldcg(reinterpret_cast<const float4 *>(mine + static_cast<long>(s) * 128 * n_pad + t0));
                         y.x += v.x; y.y += v.y; y.z += v.z; y.w += v.w;
                         if (silu && r < 64) {
-                            const float4 u = *reinterpret_cast<const float4 *>(zrow + s * 128 * stride + t0);
+                            const float4 u = __ldcg(reinterpret_cast<const float4 *>(zrow + static_cast<long>(s) * 128 * n_pad + t0));
                             z.x += u.x; z.y += u.y; z.z += u.z; z.w += u.w;
                         }
                     }
                     if (pairs)
                         z = make_float4(__shfl_xor_sync(0xffffffffu, y.x, 1), __shfl_xor_sync(0xffffffffu, y.y, 1),
                                         __shfl_xor_sync(0xffffffffu, y.z, 1), __shfl_xor_sync(0xffffffffu, y.w, 1));
-                    epi_apply4(p, e, tk, n_lo + t0, n_end, y, z, r < 64, lane);
+                    epi_apply4(p, e, tk, t0, n_end, y, z, r < 64, lane);
                 }
-                named_bar_sync(1, 128);  // this CTA's buffer has been read
-                if (threadIdx.x == kEpiWarp0 * 32)
-                    for (int s = 0; s < ksplit; ++s) mbar_arrive_remote(part_free, s);
                 continue;
             }
             // whole K range here: accumulator -> exch[row][token] (scaled), then 4 tokens at a time
@@ -755,28 +761,37 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             }
             named_bar_sync(1, 128);  // exch is rewritten by the next tile
         }
+        if (any_logits) {  // this CTA's best key per token, one global atomic each
+            named_bar_sync(1, 128);
+            if (r < p.batch && keys_s[r]) atomicMax(p.argmax_keys + r, keys_s[r]);
+        }
     } else {
         // ---------------------------------------------------------- dequant
         // four groups of four warps; group g converts group g of every block
         // column, warp w covers the rows of TMEM lane quadrant w % 4
         const int g = (warp - kConvWarp0) / 4;
         const int row = (warp & 3) * 32 + lane;
-        uint32_t use = 0;
+        const uint32_t tmem_lane = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + kTmemA;
+        uint32_t blk = 0;
         int r = 0;
         for (int t = tile_first; t < p.total_tiles; t += tile_step) {
             const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
             const float scale = ldexpf(1.0f, wexp_s[row >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
-            for (int b = b0; b < b1; ++b, ++use) {
-                mbar_wait_bounded(full_raw + r, (use / kRawStages) & 1, p.status, cta_abort);
-                if (use) mbar_wait_bounded(empty + g, (use - 1) & 1, p.status, cta_abort);
+            for (int b = b0; b < b1; ++b, ++blk) {
+                const int st = (blk & 1) * kGroups + g;
+                const uint32_t use = blk >> 1;
+                const uint32_t tmem_row = tmem_lane + static_cast<uint32_t>(st * 32);
+                mbar_wait_bounded(full_raw + r, (blk / kRawStages) & 1, p.status, cta_abort);
+                if (use) mbar_wait_bounded(empty + st, (use - 1) & 1, p.status, cta_abort);
+                tc_fence_after();
                 const uint8_t *raw = smem + L.raw + r * kRawStageBytes;
-                uint8_t *w16 = smem + L.w16 + g * kW16Bytes;
-                if (sg.type == kQ4K) convert_q4(raw, w16, row, g, scale);
-                else convert_q6(raw, w16, row, g, b % kUnitBlocks, scale);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                if (sg.type == kQ4K) convert_q4(raw, tmem_row, row, g, scale);
+                else convert_q6(raw, tmem_row, row, g, b % kUnitBlocks, scale);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(full + g);
+                    mbar_arrive(full + st);
                     mbar_arrive(empty_raw + r);
                 }
                 if (++r == kRawStages) r = 0;
@@ -929,10 +944,18 @@ __global__ void mma_scale_scan_kernel(int type, const uint8_t *w, long nblocks, 
 // ------------------------------------------------------------------- host --
 
 cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
-                            int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream) {
+                            int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl) {
     if (cols % 256 || cols > kMaxCols || batch < 1 || n_pad > kMmaMaxN || n_pad % 16) return cudaErrorInvalidValue;
-    mma_prep_kernel<<<n_pad, 256, 0, stream>>>(x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a, x16, x_inv);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_pad);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, mma_prep_kernel, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a, x16, x_inv);
 }
 
 cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks, int *out_max_bits, cudaStream_t stream) {
@@ -1029,7 +1052,6 @@ int mma_choose_split(int tiles, int nblocks, int *bps) {
     for (int k = 1; k <= kMaxCluster && k <= nblocks; ++k) {
         const int per = (nblocks + k - 1) / k;
         if ((nblocks + per - 1) / per != k) continue;  // every part non-empty
-        if (k > 1 && !split_fits(k)) continue;
         const int cap = g_cluster_cap[k];
         if (cap < 1) continue;
         const int waves = (tiles + cap - 1) / cap;
@@ -1043,10 +1065,11 @@ int mma_choose_split(int tiles, int nblocks, int *bps) {
     return best_k;
 }
 
-cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream) {
+cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl) {
     if (p.n_pad < 16 || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.cols % 256 || p.total_tiles < 1 || p.ksplit < 1 ||
         p.ksplit > kMaxCluster || p.bps < 1 || (p.ksplit - 1) * p.bps >= p.cols / 256 ||
-        p.ksplit * p.bps < p.cols / 256 || g_cluster_cap[p.ksplit] < 1 || (p.ksplit > 1 && !split_fits(p.ksplit)))
+        p.ksplit * p.bps < p.cols / 256 || g_cluster_cap[p.ksplit] < 1 ||
+        (p.ksplit > 1 && (!p.scratch || static_cast<long>(p.total_tiles) * p.ksplit * kMmaTileM * p.n_pad > p.scratch_floats)))
         return cudaErrorInvalidValue;
     const int clusters = p.total_tiles < g_cluster_cap[p.ksplit] ? p.total_tiles : g_cluster_cap[p.ksplit];
     cudaLaunchConfig_t cfg = {};
@@ -1056,7 +1079,7 @@ cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream) {
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 0;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = p.ksplit;
     attr[1].val.clusterDim.y = 1;

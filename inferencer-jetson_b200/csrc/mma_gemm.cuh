@@ -41,9 +41,12 @@ struct MmaParams {
     int nseg;
     int total_tiles;
     // split K: each tile's K range is cut into ksplit parts of bps block
-    // columns, run by the ksplit CTAs of one cluster (mma_choose_split)
+    // columns, run by the ksplit CTAs of one cluster (mma_choose_split); the
+    // parts exchange fp32 partial sums through scratch [tiles][ksplit][128][n_pad]
     int ksplit;
     int bps;
+    float *scratch;
+    long scratch_floats;
     int cols;             // K
     int batch;            // tokens in this launch (<= kMmaMaxN)
     int n_pad;            // MMA N: batch rounded up to 16
@@ -71,7 +74,7 @@ struct MmaParams {
 // plain fp32 values, times a per-token power of two, in the tensor cores'
 // K-major layout.  Padding tokens up to n_pad are zero.
 cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
-                            int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream);
+                            int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl);
 
 // Exponent e with max|w| * 2^e <= 2^15 for a quantised matrix (one reduction
 // over its block scales); written to *out_exp on the device.
@@ -82,7 +85,10 @@ cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks_gguf_
 int mma_make_weight(int type, const void *data, int rows, long row_bytes, int rows_per_box, MmaWeight *out,
                     char *err, int err_len);
 
-cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream);
+// pdl: launch with programmatic stream serialisation; the kernel loads and
+// dequantises weights before waiting for the previous kernel, and reads the
+// activation and writes outputs only after the wait.
+cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl);
 // Parts per tile (the cluster size) for a launch of `tiles` tiles of
 // `nblocks` 256-wide block columns, from how many clusters of each size fit
 // on the GPU at once; *bps receives block columns per part.  Needs
