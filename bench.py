@@ -11,6 +11,9 @@ Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
             step is one packed decode step over the 64 live sequences.
   decode1   same model, one sequence: 512-token prompt (ids U[0,128000),
             seed 1), then greedy decode steps.
+  gemm_q6k_b64  the dominant kernel of ragged64 alone: the tensor-core
+            quantised GEMM (+ its activation prep) on the 1B vocab
+            projection, Q6_K 128256x2048, 64 tokens, through ijb_matvec.
 `value` is whole-job decode tokens/s: tokens generated in the K timed steps
 on all ranks / max over ranks of the device time of those steps (CUDA events
 around each step's graph).  Replacement prefills run between timed steps and
@@ -53,11 +56,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=48)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["ragged64", "decode1", "gemv_q4k", "gemv_q6k"], default="ragged64")
+    ap.add_argument("--workload", choices=["ragged64", "decode1", "gemv_q4k", "gemv_q6k", "gemm_q6k_b64"],
+                    default="ragged64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=512, help="decode1 prompt length")
     ap.add_argument("--prompt-max", type=int, default=1024,
                     help="ragged64 longest prompt (1024 in the BASELINE config; smaller for profiling captures)")
+    ap.add_argument("--nvtx-step", action="store_true",
+                    help="wrap the last timed step in an NVTX range 'step' (ncu --nvtx-include step/)")
     return ap.parse_args()
 
 
@@ -249,6 +255,73 @@ def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
     return out
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one mma_gemm_kernel launch of
+# the gemm_q6k_b64 workload, from the ncu capture summarised in
+# profiles/mma_gemm_q6k_vocab_b64.md (None until captured)
+MMA_VOCAB_TRAFFIC = None
+
+
+def mma_roofline(eng, cuda, peak, iters=20, batch=64):
+    """The tensor-core GEMM timed alone with CUDA events on its stream: the
+    vocab projection (Q6_K 128256x2048, the largest launch of a decode step)
+    for `batch` tokens through ijb_matvec, each launch = activation prep +
+    mma_gemm_kernel.  Algorithmic bytes: the Q6_K weights as stored (unit
+    layout), the fp32 activations read and the fp32 logits written."""
+    import torch
+    L = ijblib.load()
+    cfg = eng.cfg
+    idx = eng.tensor_index("token_embd.weight")
+    cols, rows = cfg.dim, cfg.vocab
+    x = torch.randn(batch, cols, device=cuda)
+    y = torch.empty(batch, rows, device=cuda)
+    side = torch.cuda.Stream(device=cuda)  # a real stream handle (0 would mean the engine's own stream)
+    stream = side.cuda_stream
+    def launch():
+        ijblib.check(L.ijb_matvec(eng.h, idx, x.data_ptr(), y.data_ptr(), cols, rows, batch, ctypes.c_void_p(stream)),
+                     eng.h)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            launch()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(side)
+        for _ in range(iters):
+            launch()
+        b.record(side)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    w_bytes = rows * L.ijb_q6k_planar_row_bytes(cols)
+    algo = w_bytes + batch * cols * 4 + batch * rows * 4
+    gbs = algo / (ms * 1e-3) / 1e9
+    return {"us_per_launch": ms * 1e3, "algorithmic_bytes": algo, "gbs": gbs, "frac": gbs / peak,
+            "kernel": f"mma_gemm_kernel + activation prep (Q6_K {rows}x{cols} vocab projection, {batch} tokens)",
+            "traffic": MMA_VOCAB_TRAFFIC}
+
+
+def run_gemm(args):
+    """The dominant kernel of ragged64 alone (see mma_roofline)."""
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    cuda = torch.device(f"cuda:{local}")
+    peak, src = hbm_peak()
+    full = synth.LLAMA_1B
+    cfg = synth.ModelConfig("llama-3.2-1b-1layer", dim=full.dim, layers=1, heads=full.heads,
+                            kv_heads=full.kv_heads, hidden=full.hidden, vocab=full.vocab)
+    from ijb200.engine import Engine
+    eng = Engine(cfg, synth.make_model(cfg, seed=0), context=32, max_batch=64, device=local)
+    r = mma_roofline(eng, cuda, peak, iters=max(args.steps, 5))
+    eng.close()
+    if rank != 0:
+        return None
+    return {"metric": "GEMM HBM GB/s (Q6_K 128256x2048 vocab projection, 64 tokens)", "value": r["gbs"],
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 3, "ms_per_step": r["us_per_launch"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 x fp16 (exact dequant, int8-path activations), fp32 accumulate",
+            "data": "synthetic (seeded)", "config": {"workload": "gemm_q6k_b64", "l2": "weights 216 MB > L2"},
+            "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peak, "unit": "GB/s", "frac": r["frac"],
+                         "traffic": r["traffic"], "kernel": r["kernel"], "peak_source": src}}
+
+
 def cpu_baseline(cfg, weights, contexts, threads, budget_s=20.0):
     """The oracle's FastRunner::forward on the host cores: decode one token at
     each sampled context length; returns tokens/s and the sample used."""
@@ -294,6 +367,8 @@ def run_ours(args):
     import torch
     if args.workload.startswith("gemv"):
         return run_gemv(args)
+    if args.workload == "gemm_q6k_b64":
+        return run_gemm(args)
     world, rank, local = dist_setup(args.gpus)
     cuda = torch.device(f"cuda:{local}")
     peak, peak_src = hbm_peak()
@@ -334,8 +409,12 @@ def run_ours(args):
     launches0 = ijblib.load().ijb_kernel_launches()
     tokens, dev_ms, wall_s, kv_tokens, replaced_s = 0, 0.0, 0.0, 0, 0.0
     t_region = time.perf_counter()
-    for _ in range(args.steps):
+    for k in range(args.steps):
+        if args.nvtx_step and k == args.steps - 1:
+            torch.cuda.nvtx.range_push("step")
         n, ms, wall, ctx = one_step()
+        if args.nvtx_step and k == args.steps - 1:
+            torch.cuda.nvtx.range_pop()
         tokens += n
         dev_ms += ms
         wall_s += wall
@@ -364,7 +443,8 @@ def run_ours(args):
     result = None
     if rank == 0:
         kern = gemv_roofline(cuda, peak)
-        dom = kern["q6k_lm_head_128256x2048"]
+        dom = mma_roofline(eng, cuda, peak) if args.workload == "ragged64" else dict(
+            kern["q6k_lm_head_128256x2048"], kernel="gemv_kernel (Q6_K lm_head 128256x2048, B=1)", traffic=None)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             ctxs = ([int(c) for c in server.contexts()[:8]] if args.workload == "ragged64" else [pos] * 4)
@@ -389,8 +469,8 @@ def run_ours(args):
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * batch},
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
-                         "frac": dom["frac"], "traffic": None, "kernel": "gemv_kernel (Q6_K lm_head 128256x2048, B=1)",
-                         "peak_source": peak_src},
+                         "frac": dom["frac"], "traffic": dom["traffic"], "kernel": dom["kernel"],
+                         "us_per_launch": dom["us_per_launch"], "peak_source": peak_src},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak},
             "gemv": kern,
             "cpu_baseline": cpu,

@@ -55,9 +55,10 @@ constexpr int kX16Bytes = kMmaMaxN * kKChunk * 2;     // 8 KB
 constexpr int kCoreStride = 128;                      // bytes between 8-wide K cores
 constexpr int kGroupStride = (kKChunk / 8) * 128;     // bytes between 8-row groups (1 KB)
 constexpr int kMaxCluster = 8;
-// the unsplit epilogue's copy of the accumulator, [128 rows][kExch] floats
-constexpr int kExch = kMmaMaxN + 4;  // 68 floats: 17 x 16 B per row (conflict-free vector access)
-constexpr int kRedBytes = kMmaTileM * kExch * 4;
+// the epilogue's output tile, [token][kStage] floats (a token's 128 rows contiguous,
+// 16-byte aligned rows for bulk stores)
+constexpr int kStage = kMmaTileM + 4;
+constexpr int kRedBytes = kMmaMaxN * kStage * 4;
 constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kXWarp = 6, kConvWarp0 = 7, kConvWarps = 16;
 constexpr int kMmaThreads = (kConvWarp0 + kConvWarps) * 32;
 constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 1;
@@ -88,7 +89,7 @@ __host__ __device__ constexpr MmaSmem mma_smem() {
     return L;
 }
 static_assert(mma_smem().total <= 227 * 1024, "shared memory of the tensor-core GEMM");
-static_assert(kMmaTileM * kExch * 4 <= kRedBytes, "the accumulator copy lives in the partial-sum buffer");
+static_assert((kStage * 4) % 16 == 0, "bulk-store rows");
 
 // Tokens per part's epilogue slice (a multiple of 4).
 __host__ __device__ constexpr int split_per(int batch, int parts) { return ((batch + parts - 1) / parts + 3) / 4 * 4; }
@@ -163,6 +164,22 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                  "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                  : "memory");
 }
+
+// Bulk (TMA engine) stores of shared-memory rows: plain copy or fp32 add into
+// global memory; bytes and both addresses multiples of 16.
+__device__ __forceinline__ void bulk_s2g(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_s2g_add(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
@@ -416,89 +433,112 @@ __device__ __forceinline__ EpiRow make_epi_row(const MmaParams &p, const MmaSeg 
     return e;
 }
 
-// Tokens n0 .. n0+3 (those below n_end) of one tile row: values y, and z =
-// the value of row ^ 1 (RoPE pairs) or of the matching up row (SiLU pairs,
-// gate rows only).  One switch per four tokens; every lane of the warp calls
-// this with the same n0 (the logits key is a warp reduction).
-__device__ __forceinline__ void epi_apply4(const MmaParams &p, const EpiRow &e, const EpiTok &tk, int n0, int n_end,
-                                           float4 y4, float4 z4, bool gate, int lane) {
-    const float y[4] = {y4.x, y4.y, y4.z, y4.w}, z[4] = {z4.x, z4.y, z4.z, z4.w};
+// KV cache element of (token n, tile row) for a K or V write.
+__device__ __forceinline__ long kv_offset(const MmaParams &p, const EpiRow &e, const EpiTok &tk, int n) {
+    const int slot = tk.slot[n];
+    return static_cast<long>(slot / p.page_size) * p.page_stride +
+           (static_cast<long>(e.head) * p.page_size + slot % p.page_size) * p.head_dim + e.dd;
+}
+
+// Phase B of the epilogue: stage[n][r] holds the finished GEMM value of tile
+// lane r for tokens [t_lo, t_hi); apply the row operation in place (SiLU pairs,
+// RoPE), write the KV cache, or (no bulk path) store the outputs directly.
+// Every thread of the 128 calls this; per-token loops are warp-uniform.
+__device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, float *stage, int r, int t_lo, int t_hi,
+                         bool bulk) {
+    float *col = stage + r;  // token n at col[n * kStage]
     switch (e.epi) {
-        case kEpiStore:
-            if (e.valid)
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (n0 + k < n_end) e.out[(n0 + k) * e.stride] = y[k];
-            break;
-        case kEpiAdd:
-            if (e.valid)
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (n0 + k < n_end)
-                        asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + (n0 + k) * e.stride), "f"(y[k])
-                                     : "memory");
-            break;
         case kEpiSiluPair:
-            if (e.valid && gate)
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (n0 + k < n_end) e.out[(n0 + k) * e.stride] = y[k] / (1.f + __expf(-y[k])) * z[k];
+            if (r < 64)
+                for (int n = t_lo; n < t_hi; ++n) {
+                    const float g = col[n * kStage], u = col[n * kStage + 64];
+                    const float v = g / (1.f + __expf(-g)) * u;
+                    if (bulk) col[n * kStage] = v;
+                    else if (e.valid) e.out[n * e.stride] = v;
+                }
             break;
         case kEpiRopeQ:
         case kEpiRopeKCache: {
-            if (!e.valid) break;
-            // rope_cuda (inferencer.cu:906-917)
-            float c[4], sn[4];
+            // rope_cuda (inferencer.cu:906-917); the partner row r ^ 1 is the neighbouring lane
+            const float *pc = p.rope_cos + e.f, *ps = p.rope_sin + e.f;
+            for (int n0 = t_lo; n0 < t_hi; n0 += 8) {
+                float y[8], z[8], c[8], sn[8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int pos = n0 + k < n_end ? tk.pos[n0 + k] : 0;
-                c[k] = __ldg(p.rope_cos + pos * p.half_head + e.f);
-                sn[k] = __ldg(p.rope_sin + pos * p.half_head + e.f);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (n0 + k >= n_end) continue;
-                const float a = e.even ? y[k] : z[k], b = e.even ? z[k] : y[k];
-                const float r = e.even ? a * c[k] - b * sn[k] : a * sn[k] + b * c[k];
-                if (e.epi == kEpiRopeQ) {
-                    e.out[(n0 + k) * e.stride] = r;
-                } else {
-                    const int slot = tk.slot[n0 + k];
-                    const long off = static_cast<long>(slot / p.page_size) * p.page_stride +
-                                     (static_cast<long>(e.head) * p.page_size + slot % p.page_size) * p.head_dim + e.dd;
-                    if (p.kv_f32) static_cast<float *>(p.k_cache)[off] = r;
-                    else static_cast<__half *>(p.k_cache)[off] = __float2half_rn(r);
+                for (int k = 0; k < 8; ++k) {
+                    const int n = min(n0 + k, t_hi - 1);
+                    y[k] = col[n * kStage];
+                    z[k] = stage[n * kStage + (r ^ 1)];
+                    const int pos = tk.pos[n] * p.half_head;
+                    c[k] = __ldg(pc + pos);
+                    sn[k] = __ldg(ps + pos);
                 }
+                __syncwarp();
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (n0 + k >= t_hi) break;
+                    const float a = e.even ? y[k] : z[k], b = e.even ? z[k] : y[k];
+                    const float v = e.even ? a * c[k] - b * sn[k] : a * sn[k] + b * c[k];
+                    if (e.epi == kEpiRopeQ) {
+                        if (bulk) col[(n0 + k) * kStage] = v;
+                        else if (e.valid) e.out[(n0 + k) * e.stride] = v;
+                    } else if (e.valid) {
+                        const long off = kv_offset(p, e, tk, n0 + k);
+                        if (p.kv_f32) static_cast<float *>(p.k_cache)[off] = v;
+                        else static_cast<__half *>(p.k_cache)[off] = __float2half_rn(v);
+                    }
+                }
+                __syncwarp();
             }
             break;
         }
         case kEpiVCache:
             if (e.valid)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    if (n0 + k >= n_end) continue;
-                    const int slot = tk.slot[n0 + k];
-                    const long off = static_cast<long>(slot / p.page_size) * p.page_stride +
-                                     (static_cast<long>(e.head) * p.page_size + slot % p.page_size) * p.head_dim + e.dd;
-                    if (p.kv_f32) static_cast<float *>(p.v_cache)[off] = y[k];
-                    else static_cast<__half *>(p.v_cache)[off] = __float2half_rn(y[k]);
+                for (int n = t_lo; n < t_hi; ++n) {
+                    const long off = kv_offset(p, e, tk, n);
+                    if (p.kv_f32) static_cast<float *>(p.v_cache)[off] = col[n * kStage];
+                    else static_cast<__half *>(p.v_cache)[off] = __float2half_rn(col[n * kStage]);
                 }
             break;
+        case kEpiStore:
+            if (!bulk && e.valid)
+                for (int n = t_lo; n < t_hi; ++n) e.out[n * e.stride] = col[n * kStage];
+            break;
+        case kEpiAdd:
+            if (!bulk && e.valid)
+                for (int n = t_lo; n < t_hi; ++n)
+                    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + n * e.stride), "f"(col[n * kStage])
+                                 : "memory");
+            break;
         case kEpiLogitsArgmax:
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (n0 + k >= n_end) break;
-                if (e.valid) e.out[(n0 + k) * e.stride] = y[k];
-                unsigned long long key = e.valid ? argmax_key(y[k], e.row) : 0ull;
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-                    key = other > key ? other : key;
-                }
-                if (lane == 0 && key) atomicMax(tk.keys + n0 + k, key);  // flushed once at the end
-            }
+            if (!bulk && e.valid)
+                for (int n = t_lo; n < t_hi; ++n) e.out[n * e.stride] = col[n * kStage];
             break;
         default:
             break;
+    }
+}
+
+// Logits: the best (value, row) key of each token over the tile's `count`
+// rows, two threads per token scanning 64 rows each; kept in the CTA's
+// shared key array (flushed to global once at the end of the kernel).
+__device__ void epi_argmax(const float *stage, const EpiTok &tk, int row_base, int count, int t_lo, int t_hi) {
+    const int tid = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    for (int n0 = t_lo; n0 < t_hi; n0 += 64) {
+        const int n = n0 + (tid >> 1), h = tid & 1;
+        unsigned long long best = 0ull;
+        if (n < t_hi) {
+            const float *v = stage + n * kStage;
+            for (int i = 0; i < 64; ++i) {
+                const int rr = h * 64 + ((i + n) & 63);  // staggered so the pair's lanes hit different banks
+                if (rr < count) {
+                    const unsigned long long key = argmax_key(v[rr], row_base + rr);
+                    best = key > best ? key : best;
+                }
+            }
+        }
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, 1);
+        best = other > best ? other : best;
+        if (h == 0 && n < t_hi && best) atomicMax(tk.keys + n, best);
     }
 }
 
@@ -687,14 +727,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             bool valid;
             const int row = tile_row(sg, lt, r, valid);
             const EpiRow e = make_epi_row(p, sg, row, valid);
-            const bool silu = sg.epi == kEpiSiluPair, pairs = sg.epi == kEpiRopeQ || sg.epi == kEpiRopeKCache;
             any_logits |= sg.epi == kEpiLogitsArgmax;
             const float wscale = ldexpf(1.0f, -wexp_s[r >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * n_pad;
+            // the bulk stores of the previous tile have finished reading the staging tile
+            if (i > 0) {
+                if (threadIdx.x == kEpiWarp0 * 32) bulk_wait_read();
+                named_bar_sync(1, 128);
+            }
+            float *stage = red;
+            int t_lo = 0, t_hi = p.batch;
             if (ksplit > 1) {
                 // this part's partial sums -> scratch[tile][part][row][token] (L2), then the
-                // parts signal each other; part s applies the epilogue to its token slice,
-                // summing the parts in part order (the result does not depend on timing)
+                // parts signal each other; part s finishes its token slice, summing the parts
+                // in part order (the result does not depend on timing)
                 float *dst = p.scratch + ((static_cast<long>(t) * ksplit + rank) * 128 + r) * n_pad;
                 for (int c0 = 0; c0 < n_pad; c0 += 16) {
                     float v[16];
@@ -716,51 +762,59 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
                     for (int s = 0; s < ksplit; ++s) mbar_arrive_remote(part_ready, s);
                 }
                 const bool ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort);
-                const int n_lo = min(p.batch, rank * per), n_end = min(p.batch, n_lo + per);
-                const float *base = p.scratch + static_cast<long>(t) * ksplit * 128 * n_pad;
-                const float *mine = base + static_cast<long>(r) * n_pad, *zrow = base + static_cast<long>((r + 64) & 127) * n_pad;
-                for (int t0 = n_lo; ok && t0 < n_end; t0 += 4) {
-                    float4 y = make_float4(0.f, 0.f, 0.f, 0.f), z = y;
+                t_lo = min(p.batch, rank * per);
+                t_hi = ok ? min(p.batch, t_lo + per) : t_lo;
+                const float *mine = p.scratch + static_cast<long>(t) * ksplit * 128 * n_pad + static_cast<long>(r) * n_pad;
+                for (int t0 = t_lo; t0 < t_hi; t0 += 4) {
+                    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (int s = 0; s < ksplit; ++s) {
                         const float4 v = __ldcg(reinterpret_cast<const float4 *>(mine + static_cast<long>(s) * 128 * n_pad + t0));
                         y.x += v.x; y.y += v.y; y.z += v.z; y.w += v.w;
-                        if (silu && r < 64) {
-                            const float4 u = __ldcg(reinterpret_cast<const float4 *>(zrow + static_cast<long>(s) * 128 * n_pad + t0));
-                            z.x += u.x; z.y += u.y; z.z += u.z; z.w += u.w;
-                        }
                     }
-                    if (pairs)
-                        z = make_float4(__shfl_xor_sync(0xffffffffu, y.x, 1), __shfl_xor_sync(0xffffffffu, y.y, 1),
-                                        __shfl_xor_sync(0xffffffffu, y.z, 1), __shfl_xor_sync(0xffffffffu, y.w, 1));
-                    epi_apply4(p, e, tk, t0, n_end, y, z, r < 64, lane);
+                    stage[t0 * kStage + r] = y.x;
+                    stage[(t0 + 1) * kStage + r] = y.y;
+                    stage[(t0 + 2) * kStage + r] = y.z;
+                    stage[(t0 + 3) * kStage + r] = y.w;
                 }
-                continue;
-            }
-            // whole K range here: accumulator -> exch[row][token] (scaled), then 4 tokens at a time
-            float *exch = red;
-            for (int c0 = 0; c0 < n_pad; c0 += 16) {
-                float v[16];
-                tmem_ld16(taddr + c0, v);
+            } else {
+                // whole K range here: accumulator -> stage[token][row], scaled
+                for (int c0 = 0; c0 < n_pad; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + c0, v);
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<float4 *>(exch + r * kExch + c0 + 4 * q) =
-                        make_float4(v[4 * q] * wscale * xinv_s[c0 + 4 * q], v[4 * q + 1] * wscale * xinv_s[c0 + 4 * q + 1],
-                                    v[4 * q + 2] * wscale * xinv_s[c0 + 4 * q + 2],
-                                    v[4 * q + 3] * wscale * xinv_s[c0 + 4 * q + 3]);
+                    for (int k = 0; k < 16; ++k) stage[(c0 + k) * kStage + r] = v[k] * wscale * xinv_s[c0 + k];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty + a);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty + a);
             named_bar_sync(1, 128);
-            const float *mine = exch + r * kExch;
-            const float *other = exch + (silu ? (r + 64) & 127 : r ^ 1) * kExch;
-            for (int n0 = 0; n0 < p.batch; n0 += 4) {
-                const float4 y = *reinterpret_cast<const float4 *>(mine + n0);
-                const float4 z = (silu || pairs) ? *reinterpret_cast<const float4 *>(other + n0) : y;
-                epi_apply4(p, e, tk, n0, p.batch, y, z, r < 64, lane);
+            // rows this tile writes and whether whole token rows can go out as bulk stores
+            const int row0 = sg.w1 >= 0 ? lt * 64 : lt * 128;
+            const int count = min(sg.w1 >= 0 ? 64 : 128, sg.rows - row0);
+            float *gbase = sg.out + sg.row_offset + row0;
+            const bool bulk_kind = sg.epi == kEpiStore || sg.epi == kEpiAdd || sg.epi == kEpiSiluPair ||
+                                   sg.epi == kEpiRopeQ || sg.epi == kEpiLogitsArgmax;
+            const bool bulk = bulk_kind && count > 0 && (count & 3) == 0 && (sg.out_stride & 3) == 0 &&
+                              (reinterpret_cast<uintptr_t>(gbase) & 15) == 0;
+            epi_rows(p, e, tk, stage, r, t_lo, t_hi, bulk);
+            if (sg.epi == kEpiLogitsArgmax) {
+                named_bar_sync(1, 128);
+                epi_argmax(stage, tk, sg.row_offset + row0, count, t_lo, t_hi);
             }
-            named_bar_sync(1, 128);  // exch is rewritten by the next tile
+            if (bulk) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                named_bar_sync(1, 128);
+                if (threadIdx.x == kEpiWarp0 * 32) {
+                    for (int n = t_lo; n < t_hi; ++n) {
+                        if (sg.epi == kEpiAdd) bulk_s2g_add(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
+                        else bulk_s2g(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
+                    }
+                    bulk_commit();
+                }
+            }
         }
+        if (threadIdx.x == kEpiWarp0 * 32) bulk_wait_all();
         if (any_logits) {  // this CTA's best key per token, one global atomic each
             named_bar_sync(1, 128);
             if (r < p.batch && keys_s[r]) atomicMax(p.argmax_keys + r, keys_s[r]);
