@@ -20,7 +20,17 @@ namespace ijb {
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
-constexpr int kAttnSplit = kAttnWarps * 32;  // positions per split: one 32-position group per warp
+constexpr int kAttnChunk = 32;   // positions a warp scores at once (one per lane)
+constexpr int kAttnSplit = 512;  // positions per CTA: each warp walks every 4th chunk of 32
+
+// K/V tile stages per warp: two (the next chunk loads while this one is used)
+// when a 32-row K+V tile pair is at most 8 KB, else one.
+template <int HD, typename KT>
+__host__ __device__ constexpr int attn_stages() { return HD * static_cast<int>(sizeof(KT)) <= 128 ? 2 : 1; }
+template <int HD, typename KT>
+__host__ __device__ constexpr int attn_smem() {
+    return kAttnWarps * attn_stages<HD, KT>() * 2 * kAttnChunk * HD * static_cast<int>(sizeof(KT));
+}
 
 // Loads of cached K/V elements as fp32 from either storage format.
 __device__ __forceinline__ void load8(const __half *p, float (&f)[8]) {
@@ -63,26 +73,27 @@ __device__ __forceinline__ void loadn(const float *p, float (&f)[N]) {
     }
 }
 
-// One CTA = one (token, kv head, split of kAttnSplit positions); warp w owns
-// positions [p0 + 32w, p0 + 32w + 32): lane 0 copies the two K pages and two V
-// pages that hold them into the warp's shared-memory tiles with cp.async.bulk,
-// lanes then score one position each (rows read in a lane-rotated chunk order,
-// so the 128-bit shared loads do not collide in banks), and accumulate V with
-// lanes owning head-dim elements.
+// One CTA = one (token, kv head, split of up to kAttnSplit positions).  Warp
+// w takes chunks w, w+4, w+8, ... of 32 positions: lane 0 copies the K and V
+// page rows of a chunk into one of the warp's tile stages with cp.async.bulk
+// (the next chunk loads while this one is used), lanes score one position
+// each (rows read in a lane-rotated chunk order, so the 128-bit shared loads do
+// not collide in banks), and the warp keeps an online-softmax state per query
+// head across its chunks, accumulating V with lanes owning head-dim elements.
 template <int HD, int G, typename KT>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnParams p) {
     constexpr int DPL = HD / 32;  // head-dim elements per lane in the V phase
     constexpr int CH = HD / 8;    // 8-element chunks per row
+    constexpr int ST = attn_stages<HD, KT>();
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     extern __shared__ __align__(128) uint8_t smem[];
-    KT *ktile = reinterpret_cast<KT *>(smem) + warp * 2 * 32 * HD;  // [32][HD]
-    KT *vtile = ktile + 32 * HD;                                      // [32][HD]
+    KT *tiles = reinterpret_cast<KT *>(smem) + warp * ST * 2 * kAttnChunk * HD;  // [ST][K, V][32][HD]
     __shared__ __align__(16) float qs[G][HD];
     __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
     __shared__ __align__(16) float wo[kAttnWarps][G][HD];
-    __shared__ __align__(8) uint64_t bar[kAttnWarps];
+    __shared__ __align__(8) uint64_t bar[kAttnWarps][ST];
     __shared__ int is_last;
     __shared__ uint32_t cta_abort;
 
@@ -96,30 +107,36 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const int nsplit = (n_pos + p.split_len - 1) / p.split_len;
     if (p0 >= n_pos) return;  // this token has fewer splits (uniform across the CTA)
     const int p1 = min(n_pos, p0 + p.split_len);
+    const int nchunks = (p1 - p0 + kAttnChunk - 1) / kAttnChunk;
+    const int mine = warp < nchunks ? (nchunks - warp + kAttnWarps - 1) / kAttnWarps : 0;
     const int *pages = p.page_table + static_cast<long>(seq) * p.max_pages_per_seq;
-    const int t0 = p0 + warp * 32;
-    const bool has = t0 < p1;
     const long head_off = static_cast<long>(kvh) * p.page_size * HD;
 
     if (threadIdx.x == 0) cta_abort = 0u;  // read only after the __syncthreads below
     if (lane == 0) {
-        mbar_init(&bar[warp], 1);
+        for (int st = 0; st < ST; ++st) mbar_init(&bar[warp][st], 1);
         fence_barrier_init();
     }
     __syncwarp();
-    if (has && lane == 0) {
-        // 32 positions = 32 / page_size pages, each a contiguous run of rows
+    // chunk k of this warp -> stage k % ST: the pages holding its valid rows
+    auto issue = [&](int k) {
+        const int t0 = p0 + (warp + kAttnWarps * k) * kAttnChunk;
+        const int cnt = min(kAttnChunk, p1 - t0);
+        const int npg = (cnt + p.page_size - 1) / p.page_size;
         const uint32_t row_bytes = HD * sizeof(KT);
-        const int npg = 32 / p.page_size;
-        mbar_arrive_expect_tx(&bar[warp], 2u * npg * p.page_size * row_bytes);
+        KT *kt = tiles + (k % ST) * 2 * kAttnChunk * HD, *vt = kt + kAttnChunk * HD;
+        uint64_t *bb = &bar[warp][k % ST];
+        mbar_arrive_expect_tx(bb, 2u * npg * p.page_size * row_bytes);
         for (int j = 0; j < npg; ++j) {
             const long page = pages[(t0 + j * p.page_size) / p.page_size];
             const KT *ks = static_cast<const KT *>(p.k_cache) + page * p.page_stride + head_off;
             const KT *vs = static_cast<const KT *>(p.v_cache) + page * p.page_stride + head_off;
-            bulk_g2s(ktile + j * p.page_size * HD, ks, p.page_size * row_bytes, &bar[warp]);
-            bulk_g2s(vtile + j * p.page_size * HD, vs, p.page_size * row_bytes, &bar[warp]);
+            bulk_g2s(kt + j * p.page_size * HD, ks, p.page_size * row_bytes, bb);
+            bulk_g2s(vt + j * p.page_size * HD, vs, p.page_size * row_bytes, bb);
         }
-    }
+    };
+    if (lane == 0)
+        for (int k = 0; k < ST && k < mine; ++k) issue(k);
     const float *q = p.q + static_cast<long>(b) * p.q_stride + static_cast<long>(kvh) * G * HD;
     for (int i = threadIdx.x; i < G * HD; i += kAttnThreads) qs[i / HD][i % HD] = q[i];
     __syncthreads();
@@ -132,10 +149,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
 #pragma unroll
         for (int j = 0; j < DPL; ++j) o[g][j] = 0.f;
     }
-    if (has) {
-        mbar_wait_bounded(&bar[warp], 0, p.status, &cta_abort);
+    for (int k = 0; k < mine; ++k) {
+        mbar_wait_bounded(&bar[warp][k % ST], (k / ST) & 1, p.status, &cta_abort);
+        const KT *ktile = tiles + (k % ST) * 2 * kAttnChunk * HD, *vtile = ktile + kAttnChunk * HD;
+        const int t0 = p0 + (warp + kAttnWarps * k) * kAttnChunk;
+        const int cnt = min(kAttnChunk, p1 - t0);
         // ---- scores: lane -> position t0 + lane
-        const int t = t0 + lane;
         float s[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) s[g] = 0.f;
@@ -159,18 +178,20 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
                 s[g] = fmaf(qb.w, kf[7], s[g]);
             }
         }
-#pragma unroll
-        for (int g = 0; g < G; ++g) s[g] = t < p1 ? s[g] * p.scale : -INFINITY;
-        // ---- softmax over this group of (up to) 32 positions
+        // ---- online softmax: rescale the running state to the new maximum
         float pr[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            m[g] = warp_max(s[g]);
-            pr[g] = __expf(s[g] - m[g]);
-            l[g] = warp_sum(pr[g]);
+            const float sg = lane < cnt ? s[g] * p.scale : -INFINITY;
+            const float mn = fmaxf(m[g], warp_max(sg));
+            const float alpha = m[g] == -INFINITY ? 0.f : __expf(m[g] - mn);
+            pr[g] = lane < cnt ? __expf(sg - mn) : 0.f;
+            l[g] = fmaf(l[g], alpha, warp_sum(pr[g]));
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) o[g][j] *= alpha;
+            m[g] = mn;
         }
         // ---- V: lane -> head-dim elements [lane*DPL, lane*DPL+DPL)
-        const int cnt = min(32, p1 - t0);
 #pragma unroll 4
         for (int tt = 0; tt < cnt; ++tt) {
             float vf[DPL];
@@ -181,6 +202,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
 #pragma unroll
                 for (int j = 0; j < DPL; ++j) o[g][j] = fmaf(pg, vf[j], o[g][j]);
             }
+        }
+        __syncwarp();  // every lane is done with this stage
+        if (lane == 0 && k + ST < mine) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(k + ST);
         }
     }
 
@@ -262,7 +288,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
 
 template <int HD, int G, typename KT>
 static cudaError_t launch_attn(const AttnParams &p, dim3 grid, cudaStream_t stream, bool pdl) {
-    const int smem = kAttnWarps * 2 * 32 * HD * static_cast<int>(sizeof(KT));
+    const int smem = attn_smem<HD, KT>();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kAttnThreads);
@@ -299,7 +325,7 @@ int attention_split_len() { return kAttnSplit; }
 // (done once per device at engine creation, outside any graph capture).
 template <int HD, int G, typename KT>
 static cudaError_t set_attr() {
-    const int smem = kAttnWarps * 2 * 32 * HD * static_cast<int>(sizeof(KT));
+    const int smem = attn_smem<HD, KT>();
     return cudaFuncSetAttribute(attention_kernel<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
