@@ -1,5 +1,6 @@
 // Host-visible parameters of the paged decode-attention launch.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -7,6 +8,11 @@
 namespace ijb {
 
 struct AttnParams {
+    // fp16 cache with head_dim 64: 3-D TMA map over this layer's pool, box =
+    // one (page, kv head) run of page_size rows, 128-byte swizzled (see
+    // attention_make_kv_map); the tensor-core kernel is used when has_map
+    CUtensorMap kv_map;
+    int has_map;
     const float *q;        // [batch][q_stride], RoPE already applied
     long q_stride;
     float *out;            // [batch][out_stride]
@@ -30,6 +36,11 @@ struct AttnParams {
 };
 
 cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl);
+// Encodes the TMA map of one layer's fp16 KV pool for the tensor-core
+// kernel: dims {head_dim, 2 * kv_heads * page_size rows, num_pages}; returns
+// 0 on success, -1 where the tensor-core kernel does not apply (head_dim != 64).
+int attention_make_kv_map(CUtensorMap *map, const void *layer_base, int head_dim, int kv_heads, int page_size,
+                          long page_stride_elems, long num_pages);
 int attention_split_len();  // positions per split the kernel is built for
 cudaError_t attention_prepare();  // once per device, before any launch
 

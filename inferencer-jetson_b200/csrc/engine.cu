@@ -94,6 +94,7 @@ struct ijb_engine {
     std::vector<int> free_pages;
     int max_pages_per_seq = 0;
     int *page_table_dev = nullptr;
+    std::vector<CUtensorMap> kv_maps;  // per layer, for the tensor-core attention (fp16 cache, head_dim 64)
     int *page_table_host = nullptr;  // pinned mirror [max_seqs][max_pages_per_seq]
     std::vector<std::vector<int>> seq_pages;
     std::vector<int> seq_len;
@@ -351,6 +352,10 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
         a.partial = e->attn_partial;
         a.counters = e->attn_counters;
         a.status = e->status;
+        if (!e->kv_maps.empty()) {
+            a.kv_map = e->kv_maps[l];
+            a.has_map = 1;
+        }
         ck(attention_launch(a, s, e->pdl), "attention launch");
         ++g_launches;
         {
@@ -656,6 +661,14 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         const size_t kv_bytes = static_cast<size_t>(d.layers) * e->num_pages * e->page_stride * e->kv_elem;
         e->kv = dev_alloc<char>(kv_bytes, "KV pool");
         ck(cudaMemset(e->kv, 0, kv_bytes), "KV clear");
+        if (!e->kv_f32 && e->head_dim == 64) {
+            const long layer_pool = e->num_pages * e->page_stride;
+            e->kv_maps.resize(d.layers);
+            for (int l = 0; l < d.layers && !e->kv_maps.empty(); ++l)
+                if (attention_make_kv_map(&e->kv_maps[l], static_cast<char *>(e->kv) + l * layer_pool * e->kv_elem,
+                                          e->head_dim, d.kv_heads, d.page_size, e->page_stride, e->num_pages) != 0)
+                    e->kv_maps.clear();  // the CUDA-core attention serves every layer then
+        }
         for (long p = e->num_pages - 1; p >= 0; --p) e->free_pages.push_back(static_cast<int>(p));
         const size_t pt = static_cast<size_t>(d.max_seqs) * e->max_pages_per_seq;
         e->page_table_dev = dev_alloc<int>(pt, "page table");
