@@ -114,6 +114,7 @@ struct ijb_engine {
     int *attn_counters = nullptr;
     uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
     float *x_inv = nullptr;
+    int mma_max_split = 8, mma_split_cost = 1;
     float *mma_scratch = nullptr;  // split-K partial sums of the tensor-core path
     long mma_scratch_floats = 0;
     int mma_min_batch = kMmaMinBatch;
@@ -278,7 +279,7 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.page_stride = e->page_stride;
             m.argmax_keys = e->keys + g0 + t0;
             m.status = e->status;
-            m.ksplit = mma_choose_split(m.total_tiles, cols / 256, &m.bps);
+            m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->mma_max_split, e->mma_split_cost, &m.bps);
             m.scratch = e->mma_scratch;
             m.scratch_floats = e->mma_scratch_floats;
             if (m.ksplit > 1 && static_cast<long>(m.total_tiles) * m.ksplit * kMmaTileM * n_pad > m.scratch_floats) {
@@ -634,6 +635,9 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->mma_scratch = dev_alloc<float>(e->mma_scratch_floats, "split-K partials");
             const char *env = std::getenv("IJB_MMA_MIN_BATCH");  // diagnostic: path switch-over point
             if (env) e->mma_min_batch = std::max(1, std::atoi(env));
+            // split-K tuning: most parts per tile, and the exchange's cost in block columns
+            if ((env = std::getenv("IJB_MMA_MAX_SPLIT"))) e->mma_max_split = std::max(1, std::atoi(env));
+            if ((env = std::getenv("IJB_MMA_SPLIT_COST"))) e->mma_split_cost = std::max(0, std::atoi(env));
         }
 
         // RoPE tables, computed on the host the way FastRunner's constructor

@@ -413,15 +413,18 @@ struct EpiTok {
 
 // Per tile row: output pointer for token 0 and everything the operation needs.
 struct EpiRow {
-    float *out;  // segment output + row offset + row; token n at out[n * stride]
+    float *out;       // segment output + row offset + row; token n at out[n * stride]
+    float *out_pair;  // gate/up tiles: the output of gate row (lane & 63)
     long stride;
     int epi, f, head, dd, row;
-    bool valid, even;
+    bool valid, even, valid_pair;
 };
 
 __device__ __forceinline__ EpiRow make_epi_row(const MmaParams &p, const MmaSeg &sg, int row, bool valid) {
     EpiRow e;
     e.out = sg.out + sg.row_offset + row;
+    e.out_pair = e.out;
+    e.valid_pair = valid;
     e.stride = sg.out_stride;
     e.epi = sg.epi;
     e.row = sg.row_offset + row;
@@ -448,15 +451,20 @@ __device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, 
                          bool bulk) {
     float *col = stage + r;  // token n at col[n * kStage]
     switch (e.epi) {
-        case kEpiSiluPair:
-            if (r < 64)
-                for (int n = t_lo; n < t_hi; ++n) {
-                    const float g = col[n * kStage], u = col[n * kStage + 64];
-                    const float v = g / (1.f + __expf(-g)) * u;
-                    if (bulk) col[n * kStage] = v;
-                    else if (e.valid) e.out[n * e.stride] = v;
-                }
+        case kEpiSiluPair: {
+            // gate row r & 63 of every other token (both halves of the 128 threads
+            // work); silu(g) * u with the fast division (2 ulp)
+            float *gcol = stage + (r & 63);
+            const bool valid = r < 64 ? e.valid : e.valid_pair;
+#pragma unroll 4
+            for (int n = t_lo + (r >> 6); n < t_hi; n += 2) {
+                const float g = gcol[n * kStage], u = gcol[n * kStage + 64];
+                const float v = __fdividef(g, 1.f + __expf(-g)) * u;
+                if (bulk) gcol[n * kStage] = v;
+                else if (valid) e.out_pair[n * e.stride] = v;
+            }
             break;
+        }
         case kEpiRopeQ:
         case kEpiRopeKCache: {
             // rope_cuda (inferencer.cu:906-917); the partner row r ^ 1 is the neighbouring lane
@@ -528,13 +536,17 @@ __device__ void epi_argmax(const float *stage, const EpiTok &tk, int row_base, i
         unsigned long long best = 0ull;
         if (n < t_hi) {
             const float *v = stage + n * kStage;
-            for (int i = 0; i < 64; ++i) {
-                const int rr = h * 64 + ((i + n) & 63);  // staggered so the pair's lanes hit different banks
-                if (rr < count) {
-                    const unsigned long long key = argmax_key(v[rr], row_base + rr);
-                    best = key > best ? key : best;
+            unsigned long long b8[8] = {0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull, 0ull};
+            for (int i = 0; i < 64; i += 8) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int rr = h * 64 + ((i + u + n) & 63);  // staggered so the pair's lanes hit different banks
+                    const unsigned long long key = rr < count ? argmax_key(v[rr], row_base + rr) : 0ull;
+                    b8[u] = key > b8[u] ? key : b8[u];
                 }
             }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) best = b8[u] > best ? b8[u] : best;
         }
         const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, 1);
         best = other > best ? other : best;
@@ -726,7 +738,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             tc_fence_after();
             bool valid;
             const int row = tile_row(sg, lt, r, valid);
-            const EpiRow e = make_epi_row(p, sg, row, valid);
+            EpiRow e = make_epi_row(p, sg, row, valid);
+            if (sg.w1 >= 0 && r >= 64) {  // up-row threads also finish gate row r - 64 (SiLU pass)
+                bool v2;
+                const int row2 = tile_row(sg, lt, r - 64, v2);
+                e.out_pair = sg.out + sg.row_offset + row2;
+                e.valid_pair = v2;
+            }
             any_logits |= sg.epi == kEpiLogitsArgmax;
             const float wscale = ldexpf(1.0f, -wexp_s[r >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * n_pad;
@@ -1099,17 +1117,17 @@ cudaError_t mma_prepare() {
     return cudaSuccess;
 }
 
-int mma_choose_split(int tiles, int nblocks, int *bps) {
-    // cost ~ waves of clusters x block columns per part, plus about one block
-    // column's time for the cluster reduction when the K range is split
+int mma_choose_split(int tiles, int nblocks, int max_split, int split_cost, int *bps) {
+    // cost ~ waves of clusters x block columns per part, plus split_cost block
+    // columns' time for the exchange of partial sums when the K range is split
     int best_k = 1, best_cost = 0;
-    for (int k = 1; k <= kMaxCluster && k <= nblocks; ++k) {
+    for (int k = 1; k <= kMaxCluster && k <= nblocks && k <= max_split; ++k) {
         const int per = (nblocks + k - 1) / k;
         if ((nblocks + per - 1) / per != k) continue;  // every part non-empty
         const int cap = g_cluster_cap[k];
         if (cap < 1) continue;
         const int waves = (tiles + cap - 1) / cap;
-        const int cost = waves * per + (k > 1 ? 1 : 0);
+        const int cost = waves * per + (k > 1 ? split_cost : 0);
         if (k == 1 || cost < best_cost) {
             best_k = k;
             best_cost = cost;

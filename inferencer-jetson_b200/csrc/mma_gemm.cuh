@@ -91,9 +91,10 @@ int mma_make_weight(int type, const void *data, int rows, long row_bytes, int ro
 cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl);
 // Parts per tile (the cluster size) for a launch of `tiles` tiles of
 // `nblocks` 256-wide block columns, from how many clusters of each size fit
-// on the GPU at once; *bps receives block columns per part.  Needs
+// on the GPU at once (at most max_split parts; a split costs split_cost block
+// columns of time); *bps receives block columns per part.  Needs
 // mma_prepare() first.
-int mma_choose_split(int tiles, int nblocks, int *bps);
+int mma_choose_split(int tiles, int nblocks, int max_split, int split_cost, int *bps);
 // Sets the kernel's shared-memory limit and measures cluster occupancy for
 // the current device.
 cudaError_t mma_prepare();
