@@ -889,13 +889,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
 // with core j holding 64c + 4j + {0,2,1,3} and 64c + 32 + 4j + {0,2,1,3}.
 // Each thread owns cores; the 8 cores of a chunk sit on 8 adjacent lanes, so
 // a 32-wide quantisation group is an 8-lane shuffle reduction.
-__global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
-                                int n_pad, int use_dp4a, uint8_t *x16, float *x_inv) {
+__global__ void __launch_bounds__(256) mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
+                                                       int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
+                                                       float *x_inv) {
     pdl_trigger();
     pdl_wait();
-    const int n = blockIdx.x, tid = threadIdx.x;
-    __shared__ float red[256];
-    __shared__ float amax_s[8];
+    const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float part_s[8], amax_s[8];
     const long chunk_bytes = static_cast<long>(n_pad) * kKChunk * 2;
     const int cores = cols / 8;
     auto dst_of = [&](int core) -> uint8_t * {
@@ -907,32 +907,40 @@ __global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm
         return;
     }
     const float *xr = x + n * x_stride;
-    float r = 1.f;
-    if (norm_w) {
-        float s = 0.f;
-        for (int i = tid; i < cols; i += 256) s = fmaf(xr[i], xr[i], s);
-        red[tid] = s;
-        __syncthreads();
-        for (int st = 128; st > 0; st >>= 1) {
-            if (tid < st) red[tid] += red[tid + st];
-            __syncthreads();
-        }
-        r = rsqrtf(red[0] / static_cast<float>(cols) + eps);
-    }
-    // pass 1: values and the token's max |x^|
-    float local_max = 0.f;
+    // every value this thread needs, loaded once (activation and norm weight together)
     constexpr int kPer = kMaxCols / (256 * 8);
     float vals[kPer][8];
+    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const int core = tid + 256 * j;
         if (core >= cores) continue;
         const int k0 = (core >> 3) * 64 + (core & 7) * 4;  // first of the low four; +32 for the high four
-        float v[8];
         const float4 a = *reinterpret_cast<const float4 *>(xr + k0);
         const float4 b = *reinterpret_cast<const float4 *>(xr + k0 + 32);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        vals[j][0] = a.x; vals[j][1] = a.y; vals[j][2] = a.z; vals[j][3] = a.w;
+        vals[j][4] = b.x; vals[j][5] = b.y; vals[j][6] = b.z; vals[j][7] = b.w;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(vals[j][e], vals[j][e], ss);
+    }
+    float r = 1.f;
+    if (norm_w) {  // RMSNorm: warp sums, then the 8 warp partials in a fixed order
+        ss = warp_sum(ss);
+        if (lane == 0) part_s[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += part_s[w];
+        r = rsqrtf(tot / static_cast<float>(cols) + eps);
+    }
+    float local_max = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int core = tid + 256 * j;
+        if (core >= cores) continue;  // warp-uniform: cores is a multiple of 32
+        float *v = vals[j];
         if (norm_w) {
+            const int k0 = (core >> 3) * 64 + (core & 7) * 4;
             const float4 wa = *reinterpret_cast<const float4 *>(norm_w + k0);
             const float4 wb = *reinterpret_cast<const float4 *>(norm_w + k0 + 32);
             const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
@@ -963,15 +971,13 @@ __global__ void mma_prep_kernel(const float *x, long x_stride, const float *norm
             }
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            vals[j][e] = v[e];
-            local_max = fmaxf(local_max, fabsf(v[e]));
-        }
+        for (int e = 0; e < 8; ++e) local_max = fmaxf(local_max, fabsf(v[e]));
     }
     local_max = warp_max(local_max);
-    if ((tid & 31) == 0) amax_s[tid >> 5] = local_max;
+    if (lane == 0) amax_s[warp] = local_max;
     __syncthreads();
     float amax = 0.f;
+#pragma unroll
     for (int w = 0; w < 8; ++w) amax = fmaxf(amax, amax_s[w]);
     int e2 = 0;
     if (amax > 0.f) frexpf(amax, &e2);
