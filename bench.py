@@ -121,6 +121,8 @@ class ClockSampler:
 
 
 def dist_setup(n_gpus):
+    """One process per GPU under torchrun: NCCL when CUDA is present (the bench),
+    gloo otherwise (the CPU tests of the multi-rank bookkeeping)."""
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -128,9 +130,12 @@ def dist_setup(n_gpus):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device(f"cuda:{local}"))
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device(f"cuda:{local}"))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
     return world, rank, local
@@ -142,8 +147,9 @@ def reduce_max_sum(world, values_max, values_sum):
         return values_max, values_sum
     import torch
     import torch.distributed as dist
-    a = torch.tensor(values_max, dtype=torch.float64, device="cuda")
-    b = torch.tensor(values_sum, dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    a = torch.tensor(values_max, dtype=torch.float64, device=dev)
+    b = torch.tensor(values_sum, dtype=torch.float64, device=dev)
     dist.all_reduce(a, op=dist.ReduceOp.MAX)
     dist.all_reduce(b, op=dist.ReduceOp.SUM)
     return a.tolist(), b.tolist()
@@ -154,7 +160,15 @@ def barrier(world):
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+
+
+def job_throughput(world, tokens, dev_ms, wall_s):
+    """Whole-job tokens/s: all ranks' tokens over the slowest rank's device time
+    (`value`) and over the slowest rank's wall time (`e2e`)."""
+    (max_dev_ms, max_wall), (sum_tokens,) = reduce_max_sum(world, [dev_ms, wall_s], [float(tokens)])
+    return sum_tokens / (max_dev_ms / 1e3), sum_tokens / max_wall, max_dev_ms
 
 
 # ------------------------------------------------------------ workloads --
@@ -428,9 +442,7 @@ def run_ours(args):
     launches = ijblib.load().ijb_kernel_launches() - launches0
     clocks = sampler.stop()
 
-    (max_dev_ms, max_wall), (sum_tokens,) = reduce_max_sum(world, [dev_ms, wall_s], [float(tokens)])
-    value = sum_tokens / (max_dev_ms / 1e3)
-    e2e = sum_tokens / max_wall
+    value, e2e, max_dev_ms = job_throughput(world, tokens, dev_ms, wall_s)
     ms_per_step = max_dev_ms / args.steps
 
     # step roofline: quantised weights + norms, KV read for every live context
