@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     __shared__ __align__(8) uint64_t bar[kAttnWarps][ST];
     __shared__ int is_last;
     __shared__ uint32_t cta_abort;
+    __shared__ int pg_s[kAttnSplit / 8];  // this split's page ids (page_size >= 8)
 
     pdl_trigger();
     pdl_wait();
@@ -109,7 +110,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const int p1 = min(n_pos, p0 + p.split_len);
     const int nchunks = (p1 - p0 + kAttnChunk - 1) / kAttnChunk;
     const int mine = warp < nchunks ? (nchunks - warp + kAttnWarps - 1) / kAttnWarps : 0;
-    const int *pages = p.page_table + static_cast<long>(seq) * p.max_pages_per_seq;
+    {
+        const int *pt = p.page_table + static_cast<long>(seq) * p.max_pages_per_seq + p0 / p.page_size;
+        for (int i = threadIdx.x; i < (p1 - p0 + p.page_size - 1) / p.page_size; i += kAttnThreads) pg_s[i] = pt[i];
+        __syncthreads();
+    }
     const long head_off = static_cast<long>(kvh) * p.page_size * HD;
 
     if (threadIdx.x == 0) cta_abort = 0u;  // read only after the __syncthreads below
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         uint64_t *bb = &bar[warp][k % ST];
         mbar_arrive_expect_tx(bb, 2u * npg * p.page_size * row_bytes);
         for (int j = 0; j < npg; ++j) {
-            const long page = pages[(t0 + j * p.page_size) / p.page_size];
+            const long page = pg_s[(t0 - p0) / p.page_size + j];
             const KT *ks = static_cast<const KT *>(p.k_cache) + page * p.page_stride + head_off;
             const KT *vs = static_cast<const KT *>(p.v_cache) + page * p.page_stride + head_off;
             bulk_g2s(kt + j * p.page_size * HD, ks, p.page_size * row_bytes, bb);
@@ -350,6 +355,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(const __gri
     __shared__ __align__(8) uint64_t bar[kAttnWarps][ST];
     __shared__ int is_last;
     __shared__ uint32_t cta_abort;
+    __shared__ int pg_s[kAttnSplit / 8];  // this split's page ids (page_size >= 8)
 
     pdl_trigger();
     pdl_wait();
@@ -363,7 +369,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(const __gri
     const int p1 = min(n_pos, p0 + p.split_len);
     const int nchunks = (p1 - p0 + kAttnChunk - 1) / kAttnChunk;
     const int mine = warp < nchunks ? (nchunks - warp + kAttnWarps - 1) / kAttnWarps : 0;
-    const int *pages = p.page_table + static_cast<long>(seq) * p.max_pages_per_seq;
+    {
+        const int *pt = p.page_table + static_cast<long>(seq) * p.max_pages_per_seq + p0 / p.page_size;
+        for (int i = threadIdx.x; i < (p1 - p0 + p.page_size - 1) / p.page_size; i += kAttnThreads) pg_s[i] = pt[i];
+        __syncthreads();
+    }
     const int ps = p.page_size;
 
     if (threadIdx.x == 0) cta_abort = 0u;
@@ -380,7 +390,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(const __gri
         uint64_t *bb = &bar[warp][k % ST];
         mbar_arrive_expect_tx(bb, 2u * npg * ps * 128u);
         for (int j = 0; j < npg; ++j) {
-            const int page = pages[(t0 + j * ps) / ps];
+            const int page = pg_s[(t0 - p0) / ps + j];
             tma_load_3d(kt + j * ps * 128, &p.kv_map, 0, kvh * ps, page, bb);
             tma_load_3d(vt + j * ps * 128, &p.kv_map, 0, (p.kv_heads + kvh) * ps, page, bb);
         }
@@ -682,7 +692,8 @@ cudaError_t attention_prepare() {
 }
 
 cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl) {
-    if (p.split_len != kAttnSplit || p.page_size > 32 || 32 % p.page_size) return cudaErrorInvalidValue;
+    if (p.split_len != kAttnSplit || p.page_size < 8 || p.page_size > 32 || 32 % p.page_size)
+        return cudaErrorInvalidValue;
     dim3 grid(p.max_splits, p.kv_heads, p.batch);
     if (p.has_map && p.head_dim == 64 && !p.kv_f32) {
         const int G = p.heads / p.kv_heads;
