@@ -115,8 +115,7 @@ struct ijb_engine {
     uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
     float *x_inv = nullptr;
     int mma_max_split = 8, mma_split_cost = 1;
-    float *mma_scratch = nullptr;  // split-K partial sums of the tensor-core path
-    long mma_scratch_floats = 0;
+    int mma_bulk_out = 1;
     int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
     uint32_t *status = nullptr;
@@ -280,12 +279,7 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.argmax_keys = e->keys + g0 + t0;
             m.status = e->status;
             m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->mma_max_split, e->mma_split_cost, &m.bps);
-            m.scratch = e->mma_scratch;
-            m.scratch_floats = e->mma_scratch_floats;
-            if (m.ksplit > 1 && static_cast<long>(m.total_tiles) * m.ksplit * kMmaTileM * n_pad > m.scratch_floats) {
-                m.ksplit = 1;  // more partials than the scratch holds: one part per tile
-                m.bps = cols / 256;
-            }
+            m.bulk_out = e->mma_bulk_out;
             ck(mma_gemm_launch(m, s, e->mma_pdl), "tensor-core GEMM launch");
             g_launches += 2;
         }
@@ -630,14 +624,12 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
             ck(cudaMemset(e->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
             e->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
-            // split launches have at most about two parts per SM
-            e->mma_scratch_floats = 2L * e->num_sms * kMmaTileM * kMmaMaxN;
-            e->mma_scratch = dev_alloc<float>(e->mma_scratch_floats, "split-K partials");
             const char *env = std::getenv("IJB_MMA_MIN_BATCH");  // diagnostic: path switch-over point
             if (env) e->mma_min_batch = std::max(1, std::atoi(env));
             // split-K tuning: most parts per tile, and the exchange's cost in block columns
             if ((env = std::getenv("IJB_MMA_MAX_SPLIT"))) e->mma_max_split = std::max(1, std::atoi(env));
             if ((env = std::getenv("IJB_MMA_SPLIT_COST"))) e->mma_split_cost = std::max(0, std::atoi(env));
+            if ((env = std::getenv("IJB_MMA_BULK_OUT"))) e->mma_bulk_out = std::atoi(env) != 0;
         }
 
         // RoPE tables, computed on the host the way FastRunner's constructor
@@ -742,7 +734,6 @@ void ijb_destroy(ijb_engine *e) {
     if (e->next_host) cudaFreeHost(e->next_host);
     cudaFree(e->x16);
     cudaFree(e->x_inv);
-    cudaFree(e->mma_scratch);
     cudaFree(e->attn_partial);
     cudaFree(e->attn_counters);
     cudaFree(e->status);

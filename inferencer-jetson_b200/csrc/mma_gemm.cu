@@ -61,7 +61,7 @@ constexpr int kStage = kMmaTileM + 4;
 constexpr int kRedBytes = kMmaMaxN * kStage * 4;
 constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kXWarp = 6, kConvWarp0 = 7, kConvWarps = 16;
 constexpr int kMmaThreads = (kConvWarp0 + kConvWarps) * 32;
-constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 1;
+constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 2;
 
 struct MmaSmem {
     int raw, x16, red, tok, segs, bars, tmem, total;
@@ -145,19 +145,23 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
+// 16 columns without waiting; tmem_wait16 completes every earlier load and
+// makes the 16 values it is given depend on the wait.
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t *r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-
+__device__ __forceinline__ void tmem_wait16(uint32_t *r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
 // Lane (warp quadrant + lane) of TMEM gets 8 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
@@ -216,9 +220,12 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
     return v;
 }
 // Arrives on the mbarrier at `bar` in CTA `rank`, releasing this thread's
@@ -563,7 +570,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
     uint64_t *full_raw = bars, *empty_raw = full_raw + kRawStages;
     uint64_t *full = empty_raw + kRawStages, *empty = full + kStages;  // fp16 weight + activation stage
     uint64_t *acc_full = empty + kStages, *acc_empty = acc_full + 2;
-    uint64_t *part_ready = acc_empty + 2;
+    uint64_t *part_ready = acc_empty + 2, *part_free = part_ready + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem);
     uint32_t *cta_abort = tmem_slot + 1;
     float *red = reinterpret_cast<float *>(smem + L.red);
@@ -609,6 +616,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             mbar_init(acc_empty + i, 4);
         }
         mbar_init(part_ready, ksplit);
+        mbar_init(part_free, ksplit);
         fence_barrier_init();
     }
     if (warp == kMmaWarp) {
@@ -734,8 +742,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
             const int lt = t - sg.tile0;
             const int a = i & 1;
-            mbar_wait_bounded(acc_full + a, (i >> 1) & 1, p.status, cta_abort);
-            tc_fence_after();
+            // the tile's row bookkeeping, done while its accumulator is still being summed
             bool valid;
             const int row = tile_row(sg, lt, r, valid);
             EpiRow e = make_epi_row(p, sg, row, valid);
@@ -750,61 +757,67 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * n_pad;
             // the bulk stores of the previous tile have finished reading the staging tile
             if (i > 0) {
-                if (threadIdx.x == kEpiWarp0 * 32) bulk_wait_read();
+                if (warp == kEpiWarp0) bulk_wait_read();
                 named_bar_sync(1, 128);
             }
+            // ... and (split K) every part has read its slice of this CTA's previous tile
+            if (ksplit > 1 && i > 0) mbar_wait_cluster_bounded(part_free, (i - 1) & 1, p.status, cta_abort);
+            mbar_wait_bounded(acc_full + a, (i >> 1) & 1, p.status, cta_abort);
+            tc_fence_after();
+            // accumulator -> stage[token][row], scaled; 32 columns per TMEM wait
             float *stage = red;
+            for (int c0 = 0; c0 < n_pad; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16_nw(taddr + c0, v);
+                tmem_wait16(v);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) stage[(c0 + k) * kStage + r] = __uint_as_float(v[k]) * wscale * xinv_s[c0 + k];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + a);
             int t_lo = 0, t_hi = p.batch;
             if (ksplit > 1) {
-                // this part's partial sums -> scratch[tile][part][row][token] (L2), then the
-                // parts signal each other; part s finishes its token slice, summing the parts
-                // in part order (the result does not depend on timing)
-                float *dst = p.scratch + ((static_cast<long>(t) * ksplit + rank) * 128 + r) * n_pad;
-                for (int c0 = 0; c0 < n_pad; c0 += 16) {
-                    float v[16];
-                    tmem_ld16(taddr + c0, v);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int n = c0 + 4 * q;
-                        __stcg(reinterpret_cast<float4 *>(dst + n),
-                               make_float4(v[4 * q] * wscale * xinv_s[n], v[4 * q + 1] * wscale * xinv_s[n + 1],
-                                           v[4 * q + 2] * wscale * xinv_s[n + 2], v[4 * q + 3] * wscale * xinv_s[n + 3]));
-                    }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(acc_empty + a);
+                // the parts signal each other that their partial tiles are staged, then
+                // part s sums its token slice of every part's tile over the cluster's
+                // shared memory (DSMEM), in part order, so the result does not depend on
+                // timing; the sums overwrite the slice in this CTA's own tile
                 named_bar_sync(1, 128);
-                if (threadIdx.x == kEpiWarp0 * 32) {
+                if (warp == kEpiWarp0 && lane < ksplit) {
                     asm volatile("fence.acq_rel.cluster;" ::: "memory");
-                    for (int s = 0; s < ksplit; ++s) mbar_arrive_remote(part_ready, s);
+                    mbar_arrive_remote(part_ready, lane);
                 }
                 const bool ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort);
                 t_lo = min(p.batch, rank * per);
                 t_hi = ok ? min(p.batch, t_lo + per) : t_lo;
-                const float *mine = p.scratch + static_cast<long>(t) * ksplit * 128 * n_pad + static_cast<long>(r) * n_pad;
-                for (int t0 = t_lo; t0 < t_hi; t0 += 4) {
+                // items of four rows x one token, a warp covering one token's 128 rows
+                const int items = (t_hi - t_lo) * 32;
+                const uint32_t base = smem_u32(stage);
+                for (int it = threadIdx.x - kEpiWarp0 * 32; it < items; it += 128) {
+                    const uint32_t off = static_cast<uint32_t>(((t_lo + (it >> 5)) * kStage + (it & 31) * 4) * 4);
                     float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int s = 0; s < ksplit; ++s) {
-                        const float4 v = __ldcg(reinterpret_cast<const float4 *>(mine + static_cast<long>(s) * 128 * n_pad + t0));
-                        y.x += v.x; y.y += v.y; y.z += v.z; y.w += v.w;
-                    }
-                    stage[t0 * kStage + r] = y.x;
-                    stage[(t0 + 1) * kStage + r] = y.y;
-                    stage[(t0 + 2) * kStage + r] = y.z;
-                    stage[(t0 + 3) * kStage + r] = y.w;
-                }
-            } else {
-                // whole K range here: accumulator -> stage[token][row], scaled
-                for (int c0 = 0; c0 < n_pad; c0 += 16) {
-                    float v[16];
-                    tmem_ld16(taddr + c0, v);
+                    for (int q0 = 0; q0 < ksplit; q0 += 4) {  // four loads in flight, summed in part order
+                        float4 v[4];
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) stage[(c0 + k) * kStage + r] = v[k] * wscale * xinv_s[c0 + k];
+                        for (int q = 0; q < 4; ++q)
+                            if (q0 + q < ksplit) v[q] = dsmem_ld4(dsmem_addr(base + off, q0 + q));
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            if (q0 + q < ksplit) {
+                                y.x += v[q].x; y.y += v[q].y; y.z += v[q].z; y.w += v[q].w;
+                            }
+                        }
+                    }
+                    *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(stage) + off) = y;
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(acc_empty + a);
+                // the peers may refill their tiles once every part has read its slice
+                if (t + tile_step < p.total_tiles) {
+                    named_bar_sync(1, 128);
+                    if (warp == kEpiWarp0 && lane < ksplit) {
+                        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                        mbar_arrive_remote(part_free, lane);
+                    }
+                }
             }
             named_bar_sync(1, 128);
             // rows this tile writes and whether whole token rows can go out as bulk stores
@@ -813,7 +826,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             float *gbase = sg.out + sg.row_offset + row0;
             const bool bulk_kind = sg.epi == kEpiStore || sg.epi == kEpiAdd || sg.epi == kEpiSiluPair ||
                                    sg.epi == kEpiRopeQ || sg.epi == kEpiLogitsArgmax;
-            const bool bulk = bulk_kind && count > 0 && (count & 3) == 0 && (sg.out_stride & 3) == 0 &&
+            const bool bulk = p.bulk_out && bulk_kind && count > 0 && (count & 3) == 0 && (sg.out_stride & 3) == 0 &&
                               (reinterpret_cast<uintptr_t>(gbase) & 15) == 0;
             epi_rows(p, e, tk, stage, r, t_lo, t_hi, bulk);
             if (sg.epi == kEpiLogitsArgmax) {
@@ -823,8 +836,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             if (bulk) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 named_bar_sync(1, 128);
-                if (threadIdx.x == kEpiWarp0 * 32) {
-                    for (int n = t_lo; n < t_hi; ++n) {
+                if (warp == kEpiWarp0) {  // one token row per lane at a time
+                    for (int n = t_lo + lane; n < t_hi; n += 32) {
                         if (sg.epi == kEpiAdd) bulk_s2g_add(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
                         else bulk_s2g(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
                     }
@@ -832,7 +845,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
                 }
             }
         }
-        if (threadIdx.x == kEpiWarp0 * 32) bulk_wait_all();
+        if (warp == kEpiWarp0) bulk_wait_read();  // the writes complete with the grid
         if (any_logits) {  // this CTA's best key per token, one global atomic each
             named_bar_sync(1, 128);
             if (r < p.batch && keys_s[r]) atomicMax(p.argmax_keys + r, keys_s[r]);
@@ -1146,8 +1159,7 @@ int mma_choose_split(int tiles, int nblocks, int max_split, int split_cost, int 
 cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl) {
     if (p.n_pad < 16 || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.cols % 256 || p.total_tiles < 1 || p.ksplit < 1 ||
         p.ksplit > kMaxCluster || p.bps < 1 || (p.ksplit - 1) * p.bps >= p.cols / 256 ||
-        p.ksplit * p.bps < p.cols / 256 || g_cluster_cap[p.ksplit] < 1 ||
-        (p.ksplit > 1 && (!p.scratch || static_cast<long>(p.total_tiles) * p.ksplit * kMmaTileM * p.n_pad > p.scratch_floats)))
+        p.ksplit * p.bps < p.cols / 256 || g_cluster_cap[p.ksplit] < 1)
         return cudaErrorInvalidValue;
     const int clusters = p.total_tiles < g_cluster_cap[p.ksplit] ? p.total_tiles : g_cluster_cap[p.ksplit];
     cudaLaunchConfig_t cfg = {};

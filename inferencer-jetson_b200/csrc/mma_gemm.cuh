@@ -42,11 +42,10 @@ struct MmaParams {
     int total_tiles;
     // split K: each tile's K range is cut into ksplit parts of bps block
     // columns, run by the ksplit CTAs of one cluster (mma_choose_split); the
-    // parts exchange fp32 partial sums through scratch [tiles][ksplit][128][n_pad]
+    // parts exchange fp32 partial sums through the cluster's shared memory
     int ksplit;
     int bps;
-    float *scratch;
-    long scratch_floats;
+    int bulk_out;  // finished token rows leave as bulk (TMA engine) copies, else as coalesced thread stores
     int cols;             // K
     int batch;            // tokens in this launch (<= kMmaMaxN)
     int n_pad;            // MMA N: batch rounded up to 16
