@@ -303,13 +303,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
 // fp16 hi + lo pairs (two MMAs each), so only the cache's own fp16 rounding
 // remains; softmax stays fp32 with __expf as above.
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -336,268 +329,448 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 // Byte offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile
 // (1024-byte aligned): the chunk index is XORed with the row's low 3 bits.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
+// mma.m16n8k16 with all four A registers (rows 8-15 in use).
+__device__ __forceinline__ void mma16816_a4(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Transpose of the 8x8 fp16 matrix whose fragment (row lane/4, columns
+// 2(lane%4) and +1) this warp holds.
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
 
-constexpr int kMmaAttnStages = 2;
 constexpr int kMmaAttnTile = kAttnChunk * 128;  // one K or V tile: 32 rows of 64 fp16
-constexpr int kMmaAttnSmem = kAttnWarps * kMmaAttnStages * 2 * kMmaAttnTile + 1024;  // + alignment slack
+
+// One chunk of up to 32 positions on the tensor cores with positions as the
+// MMA rows and the group's query heads as its 8 columns (G <= 8):
+//   S^T[pos][head] = K[pos][:] . Q^T           (2 tiles of 16 positions)
+//   O^T[dim][head] += V^T[dim][pos] . P^T      (4 tiles of 16 dims)
+// The lane holds heads 2(lane%4) and 2(lane%4)+1: its online-softmax state
+// m[2], l[2]; the max and sum run over the 8 lanes of equal lane%4.  P^T
+// comes from the score accumulators through movmatrix transposes.  Q and P
+// enter as fp16 hi + lo pairs (two MMAs each), so only the cache's own fp16
+// rounding remains; softmax is fp32 with __expf.  kt / vt: the chunk's
+// 128-byte-swizzled K and V tiles (V rows past cnt are zeroed here).
+__device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, float scale, const uint32_t (&qb)[4][2][2],
+                                             float (&o)[4][4], float (&m)[2], float (&l)[2], int lane) {
+    const int gid = lane >> 2, mi = lane >> 3;
+    if (cnt < kAttnChunk) {  // V rows past the last position: zero (their weights are zero, keep them finite)
+        for (int r = cnt + (lane >> 3); r < kAttnChunk; r += 4)
+            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vt + r * 128 + (lane & 7) * 16), "r"(0u)
+                         : "memory");
+        __syncwarp();
+    }
+    // ---- scores: sc[mt] = S^T rows 16mt + gid (+8), heads 2(lane%4) (+1)
+    float sc[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+        sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t ka[4];
+            ldsm_x4(kt + swz(16 * mt + 8 * (mi & 1) + (lane & 7), 2 * kk + (mi >> 1)), ka);
+            mma16816_a4(sc[mt], ka, qb[kk][0][0], qb[kk][0][1]);
+            mma16816_a4(sc[mt], ka, qb[kk][1][0], qb[kk][1][1]);
+        }
+    }
+    // ---- online softmax per head
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float v = 16 * mt + gid + 8 * (i >> 1) < cnt ? sc[mt][i] * scale : -INFINITY;
+            sc[mt][i] = v;
+            mx[i & 1] = fmaxf(mx[i & 1], v);
+        }
+    float alpha[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+        const float mn = fmaxf(m[e], mx[e]);
+        alpha[e] = m[e] == -INFINITY ? 0.f : __expf(m[e] - mn);
+        m[e] = mn;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float pr = sc[mt][i] == -INFINITY ? 0.f : __expf(sc[mt][i] - m[i & 1]);
+            sc[mt][i] = pr;
+            rs[i & 1] += pr;
+        }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        rs[e] += __shfl_xor_sync(0xffffffffu, rs[e], 4);
+        rs[e] += __shfl_xor_sync(0xffffffffu, rs[e], 8);
+        rs[e] += __shfl_xor_sync(0xffffffffu, rs[e], 16);
+        l[e] = fmaf(l[e], alpha[e], rs[e]);
+    }
+#pragma unroll
+    for (int md = 0; md < 4; ++md) {
+        o[md][0] *= alpha[0];
+        o[md][1] *= alpha[1];
+        o[md][2] *= alpha[0];
+        o[md][3] *= alpha[1];
+    }
+    // ---- O^T += V^T P^T, 16 positions per k-step
+#pragma unroll
+    for (int kp = 0; kp < 2; ++kp) {
+        const __half2 ht = __floats2half2_rn(sc[kp][0], sc[kp][1]), hb = __floats2half2_rn(sc[kp][2], sc[kp][3]);
+        const float2 ft = __half22float2(ht), fb = __half22float2(hb);
+        const uint32_t bt = movm_t(*reinterpret_cast<const uint32_t *>(&ht));
+        const uint32_t bb = movm_t(*reinterpret_cast<const uint32_t *>(&hb));
+        const uint32_t lt = movm_t(pack_h2(sc[kp][0] - ft.x, sc[kp][1] - ft.y));
+        const uint32_t lb = movm_t(pack_h2(sc[kp][2] - fb.x, sc[kp][3] - fb.y));
+#pragma unroll
+        for (int md = 0; md < 4; ++md) {
+            uint32_t va[4];
+            ldsm_x4_t(vt + swz(16 * kp + 8 * (mi >> 1) + (lane & 7), 2 * md + (mi & 1)), va);
+            mma16816_a4(o[md], va, bt, bb);
+            mma16816_a4(o[md], va, lt, lb);
+        }
+    }
+}
+
+// ------------------------------------------------ streaming variant --
+//
+// fp16 cache, head_dim 64, tensor-core chunks as above, as a persistent
+// kernel: one CTA of kStreamWarps independent warps per SM.  The work is cut
+// into items of up to kAttnItem positions of one (token, kv head): a warp's
+// first item is fixed by its index, the next ones come from a device-wide
+// counter (the request for the following item is in flight while the current
+// one is set up).  Each warp keeps kStreamStages chunks of K/V in flight
+// through the 3-D TMA map, across item boundaries (a warp's queue holds the
+// items its in-flight chunks belong to), refilling a stage as soon as it is
+// used, so a warp's copies never drain between items and no CTA waits for
+// another wave.  A finished item leaves its softmax state (max, sum,
+// unnormalised output) per head for attention_merge_kernel, or the output
+// itself when it covers the whole sequence.  The last CTA to finish resets the
+// item counter.
+
+constexpr int kStreamWarps = 8;
+constexpr int kStreamStages = 3;
+constexpr int kStreamQueue = kStreamStages + 1;  // items a warp's in-flight chunks can span, plus the one in use
+constexpr int kAttnItem = 128;                   // positions per work item
+constexpr int kItemPages = kAttnItem / 8;        // page ids of an item (page_size >= 8)
+constexpr int kStreamMaxBatch = 256;
+constexpr int kStreamSmem = kStreamWarps * kStreamStages * 2 * kMmaAttnTile + 1024;  // + alignment slack
+
+struct StreamItem {
+    int b, h, j, p0, p1, nch, pad0, pad1;
+    int pg[kItemPages];
+};
 
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(const __grid_constant__ AttnParams p) {
-    constexpr int HD = 64, ST = kMmaAttnStages;
-    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int HD = 64, ST = kStreamStages, QN = kStreamQueue;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;  // swizzled TMA tiles need 1024-byte alignment
     const uint32_t wtiles = base + static_cast<uint32_t>(warp * ST * 2 * kMmaAttnTile);  // [ST][K, V]
-    __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
-    __shared__ __align__(16) float wo[kAttnWarps][G][HD];
-    __shared__ __align__(8) uint64_t bar[kAttnWarps][ST];
-    __shared__ int is_last;
+    __shared__ int first_s[kStreamMaxBatch + 1];  // first work item of each token (prefix sums)
+    __shared__ int nj_s[kStreamMaxBatch];         // items per kv head of each token
+    __shared__ int seq_s[kStreamMaxBatch];
+    __shared__ int npos_s[kStreamMaxBatch];
+    __shared__ StreamItem q_s[kStreamWarps][QN];
+    __shared__ __align__(8) uint64_t bar[kStreamWarps][ST];
     __shared__ uint32_t cta_abort;
-    __shared__ int pg_s[kAttnSplit / 8];  // this split's page ids (page_size >= 8)
-
-    pdl_trigger();
-    pdl_wait();
-
-    const int pos = p.tok_pos[b];
-    const int seq = p.tok_seq[b];
-    const int n_pos = pos + 1;
-    const int p0 = split * p.split_len;
-    const int nsplit = (n_pos + p.split_len - 1) / p.split_len;
-    if (p0 >= n_pos) return;
-    const int p1 = min(n_pos, p0 + p.split_len);
-    const int nchunks = (p1 - p0 + kAttnChunk - 1) / kAttnChunk;
-    const int mine = warp < nchunks ? (nchunks - warp + kAttnWarps - 1) / kAttnWarps : 0;
-    {
-        const int *pt = p.page_table + static_cast<long>(seq) * p.max_pages_per_seq + p0 / p.page_size;
-        for (int i = threadIdx.x; i < (p1 - p0 + p.page_size - 1) / p.page_size; i += kAttnThreads) pg_s[i] = pt[i];
-        __syncthreads();
-    }
-    const int ps = p.page_size;
 
     if (threadIdx.x == 0) cta_abort = 0u;
     if (lane == 0) {
         for (int st = 0; st < ST; ++st) mbar_init(&bar[warp][st], 1);
         fence_barrier_init();
     }
-    __syncwarp();
-    auto issue = [&](int k) {
-        const int t0 = p0 + (warp + kAttnWarps * k) * kAttnChunk;
-        const int cnt = min(kAttnChunk, p1 - t0);
-        const int npg = (cnt + ps - 1) / ps;
-        const uint32_t kt = wtiles + static_cast<uint32_t>((k % ST) * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
-        uint64_t *bb = &bar[warp][k % ST];
-        mbar_arrive_expect_tx(bb, 2u * npg * ps * 128u);
-        for (int j = 0; j < npg; ++j) {
-            const int page = pg_s[(t0 - p0) / ps + j];
-            tma_load_3d(kt + j * ps * 128, &p.kv_map, 0, kvh * ps, page, bb);
-            tma_load_3d(vt + j * ps * 128, &p.kv_map, 0, (p.kv_heads + kvh) * ps, page, bb);
+    pdl_trigger();
+    pdl_wait();
+    if (warp == 0) {
+        int run = 0;
+        for (int b0 = 0; b0 < p.batch; b0 += 32) {
+            const int b = b0 + lane;
+            int nj = 0;
+            if (b < p.batch) {
+                const int n_pos = p.tok_pos[b] + 1;
+                nj = (n_pos + kAttnItem - 1) / kAttnItem;
+                nj_s[b] = nj;
+                npos_s[b] = n_pos;
+                seq_s[b] = p.tok_seq[b];
+            }
+            int v = nj * p.kv_heads;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += n;
+            }
+            if (b < p.batch) first_s[b + 1] = run + v;
+            run += __shfl_sync(0xffffffffu, v, 31);
+        }
+        if (lane == 0) first_s[0] = 0;
+    }
+    __syncthreads();
+    const int total = first_s[p.batch];
+    const int ps = p.page_size;
+
+    // this warp's next item into queue slot `slot` (warp-uniform)
+    const int nwarps = static_cast<int>(gridDim.x) * kStreamWarps;
+    bool first = true;
+    int pending = 0;  // lane 0: the counter value for the following item (request in flight)
+    auto grab = [&](int slot) -> bool {
+        int id;
+        if (first) {
+            id = static_cast<int>(blockIdx.x) * kStreamWarps + warp;
+            first = false;
+        } else {
+            id = __shfl_sync(0xffffffffu, pending, 0) + nwarps;
+        }
+        if (id >= total) return false;
+        if (lane == 0) pending = atomicAdd(p.work, 1);
+        int lo = 0, hi = p.batch - 1;  // last token whose first item is <= id
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (first_s[mid] <= id) lo = mid;
+            else hi = mid - 1;
+        }
+        const int b = lo, r = id - first_s[b], nj = nj_s[b];
+        const int p0 = (r % nj) * kAttnItem, p1 = min(npos_s[b], p0 + kAttnItem);
+        StreamItem &it = q_s[warp][slot];
+        if (lane < (p1 - p0 + ps - 1) / ps)
+            it.pg[lane] = p.page_table[static_cast<long>(seq_s[b]) * p.max_pages_per_seq + p0 / ps + lane];
+        if (lane == 0) {
+            it.b = b;
+            it.h = r / nj;
+            it.j = r % nj;
+            it.p0 = p0;
+            it.p1 = p1;
+            it.nch = (p1 - p0 + kAttnChunk - 1) / kAttnChunk;
+        }
+        __syncwarp();
+        return true;
+    };
+    // chunk c of item `it` into stage `stage` (warp-uniform)
+    auto issue = [&](const StreamItem &it, int c, int stage) {
+        const int t0 = it.p0 + c * kAttnChunk;
+        const int npg = (min(kAttnChunk, it.p1 - t0) + ps - 1) / ps;
+        const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
+        uint64_t *bb = &bar[warp][stage];
+        if (lane == 0) mbar_arrive_expect_tx(bb, 2u * npg * ps * 128u);
+        __syncwarp();
+        if (lane < 2 * npg) {  // one copy per lane: page lane/2, K (even lanes) or V (odd)
+            const int j = lane >> 1, page = it.pg[(t0 - it.p0) / ps + j];
+            if (lane & 1) tma_load_3d(vt + j * ps * 128, &p.kv_map, 0, (p.kv_heads + it.h) * ps, page, bb);
+            else tma_load_3d(kt + j * ps * 128, &p.kv_map, 0, it.h * ps, page, bb);
         }
     };
-    if (lane == 0)
-        for (int k = 0; k < ST && k < mine; ++k) issue(k);
 
-    // query fragments (rows = the group's heads, 16 wide: rows >= G are zero),
-    // [k-step][hi, lo][a0, a2]
+    int q_head = 0, q_tail = 0;  // queue: items in use / grabbed (running counts)
+    int is_item = 0, is_ch = 0;  // issue cursor
+    int issued = 0, done = 0, cc = 0;
+    bool exhausted = false;
     uint32_t qa[4][2][2];
-    {
-        const float *q = p.q + static_cast<long>(b) * p.q_stride + static_cast<long>(kvh) * G * HD;
+    float o[4][4];  // O^T: dims 16md + gid (+8), heads 2tig (+1)
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    // keep ST chunks of the warp's stream in flight (warp-uniform)
+    auto refill = [&]() {
+        while (issued - done < ST) {
+            if (is_item == q_tail) {
+                if (exhausted) break;
+                if (!grab(q_tail % QN)) {
+                    exhausted = true;
+                    break;
+                }
+                ++q_tail;
+            }
+            const StreamItem &it = q_s[warp][is_item % QN];
+            if (is_ch == it.nch) {
+                ++is_item;
+                is_ch = 0;
+                continue;
+            }
+            issue(it, is_ch, issued % ST);
+            ++is_ch;
+            ++issued;
+        }
+    };
+    // the query of queued item k, raw (the MMA fragments are built when it starts)
+    float qv[4][4];
+    int qv_item = -1;
+    auto load_q = [&](int k) {
+        const StreamItem &it = q_s[warp][k % QN];
+        const float *q = p.q + static_cast<long>(it.b) * p.q_stride + static_cast<long>(it.h) * G * HD;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
+            float2 v0 = make_float2(0.f, 0.f), v1 = v0;
             if (gid < G) {
-                const float2 v0 = *reinterpret_cast<const float2 *>(q + gid * HD + 16 * kk + 2 * tig);
-                const float2 v1 = *reinterpret_cast<const float2 *>(q + gid * HD + 16 * kk + 8 + 2 * tig);
-                const __half2 h0 = __floats2half2_rn(v0.x, v0.y), h1 = __floats2half2_rn(v1.x, v1.y);
+                v0 = *reinterpret_cast<const float2 *>(q + gid * HD + 16 * kk + 2 * tig);
+                v1 = *reinterpret_cast<const float2 *>(q + gid * HD + 16 * kk + 8 + 2 * tig);
+            }
+            qv[kk][0] = v0.x;
+            qv[kk][1] = v0.y;
+            qv[kk][2] = v1.x;
+            qv[kk][3] = v1.y;
+        }
+        qv_item = k;
+    };
+    refill();
+    while (done < issued) {
+        const StreamItem &it = q_s[warp][q_head % QN];
+        if (cc == 0) {
+            // query fragments of the item's (token, kv head), the MMA's B operand:
+            // column gid = head gid (zero for gid >= G), [k-step][hi, lo][b0, b1]
+            if (qv_item != q_head) load_q(q_head);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const __half2 h0 = __floats2half2_rn(qv[kk][0], qv[kk][1]), h1 = __floats2half2_rn(qv[kk][2], qv[kk][3]);
                 const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
                 qa[kk][0][0] = *reinterpret_cast<const uint32_t *>(&h0);
                 qa[kk][0][1] = *reinterpret_cast<const uint32_t *>(&h1);
-                qa[kk][1][0] = pack_h2(v0.x - f0.x, v0.y - f0.y);
-                qa[kk][1][1] = pack_h2(v1.x - f1.x, v1.y - f1.y);
-            } else {
-                qa[kk][0][0] = qa[kk][0][1] = qa[kk][1][0] = qa[kk][1][1] = 0u;
+                qa[kk][1][0] = pack_h2(qv[kk][0] - f0.x, qv[kk][1] - f0.y);
+                qa[kk][1][1] = pack_h2(qv[kk][2] - f1.x, qv[kk][3] - f1.y);
             }
+#pragma unroll
+            for (int md = 0; md < 4; ++md) o[md][0] = o[md][1] = o[md][2] = o[md][3] = 0.f;
+            m[0] = m[1] = -INFINITY;
+            l[0] = l[1] = 0.f;
         }
-    }
-    __syncthreads();  // barriers initialised, cta_abort cleared
+        const int stage = done % ST;
+        mbar_wait_bounded(&bar[warp][stage], (done / ST) & 1, p.status, &cta_abort);
+        const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
+        const int t0 = it.p0 + cc * kAttnChunk;
+        attn_chunk_t(kt, vt, min(kAttnChunk, it.p1 - t0), p.scale, qa, o, m, l, lane);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic accesses before TMA refills the stage
+        __syncwarp();
+        ++done;
+        refill();  // the used stage goes back into flight before anything else
+        if (++cc < it.nch) continue;
 
-    float o[8][4];
+        // ---- the item is finished: output, or its state for the merge
+        cc = 0;
+        const int b = it.b, h = it.h, j = it.j, nsplit = nj_s[b];
+        ++q_head;
+        if (q_head < q_tail) load_q(q_head);  // the next item's query loads during what follows
+        if (nsplit == 1) {
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-    float m = -INFINITY, l = 0.f;  // this lane's head row gid
-    for (int k = 0; k < mine; ++k) {
-        mbar_wait_bounded(&bar[warp][k % ST], (k / ST) & 1, p.status, &cta_abort);
-        const uint32_t kt = wtiles + static_cast<uint32_t>((k % ST) * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
-        const int t0 = p0 + (warp + kAttnWarps * k) * kAttnChunk;
-        const int cnt = min(kAttnChunk, p1 - t0);
-        if (cnt < kAttnChunk) {  // V rows past the last position: zero (their weights are zero, keep them finite)
-            for (int r = cnt + (lane >> 3); r < kAttnChunk; r += 4)
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vt + r * 128 + (lane & 7) * 16), "r"(0u)
-                             : "memory");
-            __syncwarp();
-        }
-        // ---- scores S[head][position] = Q . K^T, 4 tiles of 8 positions
-        float sc[4][4];
+            for (int e = 0; e < 2; ++e) {
+                if (2 * tig + e >= G) continue;
+                float *out = p.out + static_cast<long>(b) * p.out_stride + (static_cast<long>(h) * G + 2 * tig + e) * HD;
+                const float inv = 1.f / l[e];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-#pragma unroll
-            for (int kk2 = 0; kk2 < 2; ++kk2) {
-                uint32_t kb[4];
-                ldsm_x4(kt + swz(8 * j + (lane & 7), 4 * kk2 + (lane >> 3)), kb);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    mma16816(sc[j], qa[2 * kk2][h][0], qa[2 * kk2][h][1], kb[0], kb[1]);
-                    mma16816(sc[j], qa[2 * kk2 + 1][h][0], qa[2 * kk2 + 1][h][1], kb[2], kb[3]);
+                for (int md = 0; md < 4; ++md) {
+                    out[16 * md + gid] = o[md][e] * inv;
+                    out[16 * md + gid + 8] = o[md][2 + e] * inv;
                 }
             }
+            continue;
         }
-        // ---- online softmax for row gid (the lane quad holds its 32 positions)
-        float mx = -INFINITY;
+        float *part = p.partial + ((static_cast<long>(b) * p.heads + h * G) * p.max_splits) * (HD + 2);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const float v = 8 * j + 2 * tig + e < cnt ? sc[j][e] * p.scale : -INFINITY;
-                sc[j][e] = v;
-                mx = fmaxf(mx, v);
+        for (int e = 0; e < 2; ++e) {
+            if (2 * tig + e >= G) continue;
+            float *rec = part + (static_cast<long>(2 * tig + e) * p.max_splits + j) * (HD + 2);
+            if (gid == 0) {
+                rec[0] = m[e];
+                rec[1] = l[e];
             }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float mn = fmaxf(m, mx);
-        const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-        float rs = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const float pr = sc[j][e] == -INFINITY ? 0.f : __expf(sc[j][e] - mn);
-                sc[j][e] = pr;
-                rs += pr;
-            }
-        rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-        l = fmaf(l, alpha, rs);
-        m = mn;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            o[nt][0] *= alpha;
-            o[nt][1] *= alpha;
-        }
-        // ---- O += P V: P from the score registers, V tiles through ldmatrix.trans
-#pragma unroll
-        for (int kp = 0; kp < 2; ++kp) {
-            const __half2 h0 = __floats2half2_rn(sc[2 * kp][0], sc[2 * kp][1]);
-            const __half2 h2 = __floats2half2_rn(sc[2 * kp + 1][0], sc[2 * kp + 1][1]);
-            const float2 f0 = __half22float2(h0), f2 = __half22float2(h2);
-            const uint32_t pa0 = *reinterpret_cast<const uint32_t *>(&h0), pa2 = *reinterpret_cast<const uint32_t *>(&h2);
-            const uint32_t pl0 = pack_h2(sc[2 * kp][0] - f0.x, sc[2 * kp][1] - f0.y);
-            const uint32_t pl2 = pack_h2(sc[2 * kp + 1][0] - f2.x, sc[2 * kp + 1][1] - f2.y);
-#pragma unroll
-            for (int nt2 = 0; nt2 < 4; ++nt2) {
-                uint32_t vb[4];
-                const int mi = lane >> 3;
-                ldsm_x4_t(vt + swz(16 * kp + (mi & 1) * 8 + (lane & 7), 2 * nt2 + (mi >> 1)), vb);
-                mma16816(o[2 * nt2], pa0, pa2, vb[0], vb[1]);
-                mma16816(o[2 * nt2 + 1], pa0, pa2, vb[2], vb[3]);
-                mma16816(o[2 * nt2], pl0, pl2, vb[0], vb[1]);
-                mma16816(o[2 * nt2 + 1], pl0, pl2, vb[2], vb[3]);
+            for (int md = 0; md < 4; ++md) {
+                rec[2 + 16 * md + gid] = o[md][e];
+                rec[2 + 16 * md + gid + 8] = o[md][2 + e];
             }
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // this stage's generic accesses before TMA refills it
-        __syncwarp();
-        if (lane == 0 && k + ST < mine) issue(k + ST);
     }
-
-    // ---- merge the warps of this CTA, then the splits (as in attention_kernel)
-    if (gid < G) {
-        if (tig == 0) {
-            wm[warp][gid] = m;
-            wl[warp][gid] = l;
-        }
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            wo[warp][gid][8 * nt + 2 * tig] = o[nt][0];
-            wo[warp][gid][8 * nt + 2 * tig + 1] = o[nt][1];
-        }
-    }
-    __syncthreads();
-    if (nsplit == 1) {
-        for (int i = threadIdx.x; i < G * HD; i += kAttnThreads) {
-            const int g = i / HD, d = i % HD;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][g]);
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (int w = 0; w < kAttnWarps; ++w) {
-                const float f = wm[w][g] == -INFINITY ? 0.f : __expf(wm[w][g] - M);
-                L = fmaf(wl[w][g], f, L);
-                O = fmaf(wo[w][g][d], f, O);
-            }
-            p.out[static_cast<long>(b) * p.out_stride + (static_cast<long>(kvh) * G + g) * HD + d] = O / L;
-        }
-        return;
-    }
-    float *part = p.partial + ((static_cast<long>(b) * p.heads + kvh * G) * p.max_splits) * (HD + 2);
-    for (int i = threadIdx.x; i < G * HD; i += kAttnThreads) {
-        const int g = i / HD, d = i % HD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][g]);
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
-            const float f = wm[w][g] == -INFINITY ? 0.f : __expf(wm[w][g] - M);
-            L = fmaf(wl[w][g], f, L);
-            O = fmaf(wo[w][g][d], f, O);
-        }
-        float *rec = part + (static_cast<long>(g) * p.max_splits + split) * (HD + 2);
-        rec[2 + d] = O;
-        if (d == 0) {
-            rec[0] = M;
-            rec[1] = L;
-        }
-    }
-    __threadfence();
+    // every warp of the grid has taken its last item once all CTAs get here:
+    // the last CTA resets the item counter for the next launch
     __syncthreads();
     if (threadIdx.x == 0) {
-        int *ctr = p.counters + b * p.kv_heads + kvh;
-        const int prev = atomicAdd(ctr, 1);
-        is_last = (prev == nsplit - 1);
-        if (is_last) *ctr = 0;
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    for (int i = threadIdx.x; i < G * HD; i += kAttnThreads) {
-        const int g = i / HD, d = i % HD;
-        const volatile float *recs = part + static_cast<long>(g) * p.max_splits * (HD + 2);
-        float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, recs[sp * (HD + 2)]);
-        float L = 0.f, O = 0.f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float f = __expf(recs[sp * (HD + 2)] - M);
-            L = fmaf(recs[sp * (HD + 2) + 1], f, L);
-            O = fmaf(recs[sp * (HD + 2) + 2 + d], f, O);
+        __threadfence();
+        if (atomicAdd(p.work + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+            p.work[0] = 0;
+            p.work[1] = 0;
+            __threadfence();
         }
-        p.out[static_cast<long>(b) * p.out_stride + (static_cast<long>(kvh) * G + g) * HD + d] = O / L;
+    }
+}
+
+// One warp per (token, kv head) of more than one item: lane s holds item s's
+// max and sum (at most 32 items), the weights exp(m_s - M) come from a warp
+// max, then each lane sums two output dims over the items, KB items of every
+// head per round of loads.
+template <int G>
+__global__ void __launch_bounds__(256) attention_merge_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int HD = 64, KB = G >= 8 ? 4 : 8;
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int wid = static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int b = wid / p.kv_heads, h = wid % p.kv_heads;
+    if (b >= p.batch) return;
+    const int nsplit = (p.tok_pos[b] + kAttnItem) / kAttnItem;
+    if (nsplit <= 1) return;
+    const float *part = p.partial + ((static_cast<long>(b) * p.heads + h * G) * p.max_splits) * (HD + 2);
+    float fg[G], Lg[G];
+    float2 O[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float *recs = part + static_cast<long>(g) * p.max_splits * (HD + 2);
+        const float ms = lane < nsplit ? recs[lane * (HD + 2)] : -INFINITY;
+        const float ls = lane < nsplit ? recs[lane * (HD + 2) + 1] : 0.f;
+        const float M = warp_max(ms);
+        fg[g] = lane < nsplit ? __expf(ms - M) : 0.f;
+        Lg[g] = warp_sum(fg[g] * ls);
+        O[g] = make_float2(0.f, 0.f);
+    }
+    for (int k0 = 0; k0 < nsplit; k0 += KB) {
+        float2 v[G][KB];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int k = 0; k < KB; ++k)
+                v[g][k] = k0 + k < nsplit
+                              ? reinterpret_cast<const float2 *>(part + (static_cast<long>(g) * p.max_splits + k0 + k) * (HD + 2) + 2)[lane]
+                              : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int k = 0; k < KB; ++k) {
+                const float fk = __shfl_sync(0xffffffffu, fg[g], (k0 + k) & 31);
+                O[g].x = fmaf(v[g][k].x, fk, O[g].x);
+                O[g].y = fmaf(v[g][k].y, fk, O[g].y);
+            }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float *out = p.out + static_cast<long>(b) * p.out_stride + (static_cast<long>(h) * G + g) * HD;
+        *reinterpret_cast<float2 *>(out + 2 * lane) = make_float2(O[g].x / Lg[g], O[g].y / Lg[g]);
     }
 }
 
 template <int G>
-static cudaError_t launch_attn_mma(const AttnParams &p, dim3 grid, cudaStream_t stream, bool pdl) {
+static cudaError_t launch_attn_stream(const AttnParams &p, cudaStream_t stream, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = kMmaAttnSmem;
+    cfg.gridDim = dim3(p.num_ctas);
+    cfg.blockDim = dim3(kStreamWarps * 32);
+    cfg.dynamicSmemBytes = kStreamSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attention_mma_kernel<G>, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attention_stream_kernel<G>, p);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3((p.batch * p.kv_heads + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, attention_merge_kernel<G>, p);
 }
 
 typedef CUresult (*EncodeTiledFnA)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -661,6 +834,8 @@ static cudaError_t attention_launch_t(const AttnParams &p, dim3 grid, cudaStream
 }
 
 int attention_split_len() { return kAttnSplit; }
+int attention_kernels(const AttnParams &p) { return p.has_map && p.head_dim == 64 && !p.kv_f32 ? 2 : 1; }
+int attention_item_len() { return kAttnItem; }
 
 // Opts every instance in to its K/V tile shared memory on the current device
 // (done once per device at engine creation, outside any graph capture).
@@ -682,10 +857,10 @@ static cudaError_t set_attrs_t() {
 
 cudaError_t attention_prepare() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(attention_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmem)) ||
-        (e = cudaFuncSetAttribute(attention_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmem)) ||
-        (e = cudaFuncSetAttribute(attention_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmem)) ||
-        (e = cudaFuncSetAttribute(attention_mma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaAttnSmem)))
+    if ((e = cudaFuncSetAttribute(attention_stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(attention_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(attention_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)))
         return e;
     e = set_attrs_t<__half>();
     return e != cudaSuccess ? e : set_attrs_t<float>();
@@ -694,14 +869,18 @@ cudaError_t attention_prepare() {
 cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl) {
     if (p.split_len != kAttnSplit || p.page_size < 8 || p.page_size > 32 || 32 % p.page_size)
         return cudaErrorInvalidValue;
-    dim3 grid(p.max_splits, p.kv_heads, p.batch);
+    if (p.max_splits * kAttnItem < 1) return cudaErrorInvalidValue;
     if (p.has_map && p.head_dim == 64 && !p.kv_f32) {
+        if (!p.work || p.num_ctas < 1 || p.batch > kStreamMaxBatch || p.max_splits > 32) return cudaErrorInvalidValue;
         const int G = p.heads / p.kv_heads;
-        if (G == 4) return launch_attn_mma<4>(p, grid, stream, pdl);
-        if (G == 8) return launch_attn_mma<8>(p, grid, stream, pdl);
-        if (G == 2) return launch_attn_mma<2>(p, grid, stream, pdl);
-        if (G == 1) return launch_attn_mma<1>(p, grid, stream, pdl);
+        if (G == 4) return launch_attn_stream<4>(p, stream, pdl);
+        if (G == 8) return launch_attn_stream<8>(p, stream, pdl);
+        if (G == 2) return launch_attn_stream<2>(p, stream, pdl);
+        if (G == 1) return launch_attn_stream<1>(p, stream, pdl);
     }
+    // one CTA per split of kAttnSplit positions (the partial records are kept
+    // at kAttnItem granularity, so max_splits counts items)
+    dim3 grid((p.max_splits * kAttnItem + kAttnSplit - 1) / kAttnSplit, p.kv_heads, p.batch);
     return p.kv_f32 ? attention_launch_t<float>(p, grid, stream, pdl) : attention_launch_t<__half>(p, grid, stream, pdl);
 }
 

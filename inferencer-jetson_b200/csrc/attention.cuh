@@ -29,19 +29,23 @@ struct AttnParams {
     int batch, heads, kv_heads, head_dim;
     float scale;           // 1/sqrt(head_dim)
     int split_len;         // positions per split (attention_split_len())
-    int max_splits;        // grid.x; >= ceil(context / split_len)
+    int max_splits;        // partial records per (token, head); >= ceil(context / attention_item_len())
     float *partial;        // [batch][heads][max_splits][head_dim + 2] scratch
     int *counters;         // [batch][kv_heads], zero between launches
+    int *work;             // [2] streaming kernel's item counter and finished-CTA counter, zero between launches
+    int num_ctas;          // streaming kernel grid (one CTA per SM)
     uint32_t *status;      // device error word (bounded waits)
 };
 
 cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl);
+int attention_kernels(const AttnParams &p);  // kernels attention_launch launches for p
 // Encodes the TMA map of one layer's fp16 KV pool for the tensor-core
 // kernel: dims {head_dim, 2 * kv_heads * page_size rows, num_pages}; returns
 // 0 on success, -1 where the tensor-core kernel does not apply (head_dim != 64).
 int attention_make_kv_map(CUtensorMap *map, const void *layer_base, int head_dim, int kv_heads, int page_size,
                           long page_stride_elems, long num_pages);
 int attention_split_len();  // positions per split the kernel is built for
+int attention_item_len();   // positions per work item of the streaming kernel (finest split)
 cudaError_t attention_prepare();  // once per device, before any launch
 
 }  // namespace ijb

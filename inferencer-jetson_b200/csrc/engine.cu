@@ -57,8 +57,9 @@ struct Weight {
     const uint8_t *data = nullptr;  // usable layout (Q4_K GGUF, Q6_K unit layout, F32)
     int row_bytes = 0;
     void *owned = nullptr;
-    bool has_mma = false;  // TMA descriptors for the tensor-core path
+    bool has_mma = false;  // chunked copy for the tensor-core path
     MmaWeight mma;
+    void *mma_owned = nullptr;
 };
 
 struct StepGraph {
@@ -115,7 +116,7 @@ struct ijb_engine {
     uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
     float *x_inv = nullptr;
     int mma_max_split = 8, mma_split_cost = 1;
-    int mma_bulk_out = 1;
+    int mma_bulk_out = 0;  // thread stores measured faster than per-row bulk copies
     int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
     uint32_t *status = nullptr;
@@ -223,10 +224,7 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
         const Weight &w = e->w[segs[i].w0];
         const int sdp = w.type == kQ4K ? d.use_dp4a : d.use_q6_dp4a;
         if (dp < 0) dp = sdp;
-        // a weight's TMA boxes are 64 rows when it is half of a gate/up tile
-        const int want_rows = segs[i].w1 >= 0 ? 64 : 128;
-        mma_ok = w.has_mma && w.mma.rows_per_box == want_rows && sdp == dp &&
-                 (segs[i].w1 < 0 || (e->w[segs[i].w1].has_mma && e->w[segs[i].w1].mma.rows_per_box == 64));
+        mma_ok = w.has_mma && sdp == dp && (segs[i].w1 < 0 || e->w[segs[i].w1].has_mma);
     }
     const int cols = e->w[segs[0].w0].cols;
     if (mma_ok) {
@@ -346,13 +344,15 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
         a.max_splits = e->attn_max_splits;
         a.partial = e->attn_partial;
         a.counters = e->attn_counters;
+        a.work = e->attn_counters + d.max_batch * d.kv_heads;
+        a.num_ctas = e->num_sms;
         a.status = e->status;
         if (!e->kv_maps.empty()) {
             a.kv_map = e->kv_maps[l];
             a.has_map = 1;
         }
         ck(attention_launch(a, s, e->pdl), "attention launch");
-        ++g_launches;
+        g_launches += attention_kernels(a);
         {
             const ProjSeg segs[1] = {{L.o, -1, kEpiAdd, e->x, d.dim}};
             launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, segs, 1, nullptr, 0);
@@ -604,23 +604,23 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         }
         require(e->w[e->output_norm].type == IJB_TYPE_F32 && e->w[e->output_norm].cols == d.dim, "bad output_norm");
 
-        // TMA descriptors of the tensor-core path (64-row boxes for gate/up,
-        // whose tiles hold 64 rows of each)
+        // chunked weight copies of the tensor-core path ([64-row group][block
+        // column] chunks, so that each stage of a tile is a few plain bulk copies)
         if (d.max_batch >= kMmaMinBatch) {
             ck(mma_prepare(), "tensor-core GEMM attributes");
-            std::vector<int> paired(e->w.size(), 0);
-            for (auto &L : e->layers) paired[L.gate] = paired[L.up] = 1;
             for (size_t i = 0; i < e->w.size(); ++i) {
                 Weight &w = e->w[i];
                 if (w.type != kQ4K && w.type != kQ6K) continue;
-                char msg[128];
-                const int scale_exp = w.mma.scale_exp;  // mma_make_weight clears the struct
-                if (mma_make_weight(w.type, w.data, w.rows, w.row_bytes, paired[i] ? 64 : 128, &w.mma, msg,
-                                    sizeof(msg)) == 0) {
-                    w.has_mma = true;
-                }
-                w.mma.scale_exp = scale_exp;
+                uint8_t *c = dev_alloc<uint8_t>(static_cast<size_t>(mma_tile_bytes(w.type, w.rows, w.cols)),
+                                                "tensor-core weight copy");
+                ck(mma_tile_repack_launch(w.type, w.data, w.row_bytes, w.rows, w.cols, c, e->stream),
+                   "tensor-core weight copy");
+                w.mma.chunks = c;
+                w.mma.nblocks = w.cols / 256;
+                w.mma_owned = c;
+                w.has_mma = true;
             }
+            ck(cudaStreamSynchronize(e->stream), "tensor-core weight copy");
             e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
             ck(cudaMemset(e->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
             e->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
@@ -690,12 +690,12 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         ck(cudaMallocHost(&e->meta_host, 4 * B * sizeof(int)), "meta staging");
         ck(cudaMallocHost(&e->next_host, B * sizeof(int)), "next staging");
         std::memset(e->meta_host, 0, 4 * B * sizeof(int));
-        // attention splits: short splits when few tokens share the GPU
+        // attention: partial softmax records per (token, head) at work-item granularity
         e->attn_split_len = attention_split_len();
-        e->attn_max_splits = (d.context + e->attn_split_len - 1) / e->attn_split_len;
+        e->attn_max_splits = (d.context + attention_item_len() - 1) / attention_item_len();
         e->attn_partial = dev_alloc<float>(B * d.heads * e->attn_max_splits * (e->head_dim + 2), "attention partials");
-        e->attn_counters = dev_alloc<int>(B * d.kv_heads, "attention counters");
-        ck(cudaMemset(e->attn_counters, 0, B * d.kv_heads * sizeof(int)), "counters clear");
+        e->attn_counters = dev_alloc<int>(B * d.kv_heads + 2, "attention counters");
+        ck(cudaMemset(e->attn_counters, 0, (B * d.kv_heads + 2) * sizeof(int)), "counters clear");
         e->status = dev_alloc<uint32_t>(1, "status");
         ck(cudaMemset(e->status, 0, sizeof(uint32_t)), "status clear");
         e->scratch_key = dev_alloc<unsigned long long>(1, "argmax scratch");
@@ -715,8 +715,10 @@ void ijb_destroy(ijb_engine *e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     for (auto &kv : e->graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    for (auto &w : e->w)
+    for (auto &w : e->w) {
         if (w.owned) cudaFree(w.owned);
+        if (w.mma_owned) cudaFree(w.mma_owned);
+    }
     cudaFree(e->kv);
     cudaFree(e->page_table_dev);
     if (e->page_table_host) cudaFreeHost(e->page_table_host);

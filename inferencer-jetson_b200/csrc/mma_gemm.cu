@@ -9,9 +9,10 @@
 // fill the GPU, each tile's K range into `ksplit` parts run by the CTAs of one
 // thread-block cluster.  Warp roles of a CTA:
 //   * warp 0, lane 0: weight producer.  Per 256-wide block column of a tile it
-//     loads the raw quantised bytes as 2-D TMA boxes (Q4_K: [128 rows][144 B];
-//     Q6_K: the 208-byte block bodies and the unit's 16 bytes of d) into a
-//     4-stage ring.
+//     copies the raw quantised bytes of the tile's two 64-row groups, each a
+//     contiguous chunk of the weight's chunked copy (Q4_K: [64 rows][144 B];
+//     Q6_K: [64][208 B] block bodies and [64] fp16 d), with plain bulk copies
+//     into a 4-stage ring.
 //   * warp 6, lane 0: activation producer: per 64-wide K stage, one bulk copy
 //     of the prepared fp16 activation chunk into a 4-stage ring.
 //   * warps 7..14: dequantise.  Warps 7-10 convert the even 64-wide groups of
@@ -47,10 +48,11 @@ constexpr int kKChunk = 64;  // K per fp16 stage: one Q4_K group of 64 weights
 constexpr int kGroups = 4;   // 64-wide groups of a 256-wide block column
 constexpr int kStages = 8;   // fp16 weight + activation stages: two block columns in flight
 constexpr int kRawStages = 4;
-constexpr int kRawStageBytes = 128 * 208 + 128 * 16;  // Q6_K bodies + d (Q4_K uses 128 * 144)
+constexpr int kRawStageBytes = 128 * 208 + 128 * 2;  // Q6_K bodies + d (Q4_K uses 128 * 144)
 constexpr int kQ6DOff = 128 * 208;                    // d box within a Q6_K raw stage
-constexpr uint32_t kTmemCols = 512;                   // accumulators [0, 128), fp16 weight stages [128, 384)
-constexpr uint32_t kTmemA = 128;                      // first column of the weight stages (32 per stage)
+constexpr uint32_t kTmemCols = 512;  // accumulator chain 0 [0, 128), fp16 weight stages [128, 384), chain 1 [384, 512)
+constexpr uint32_t kTmemA = 128;     // first column of the weight stages (32 per stage)
+constexpr uint32_t kTmemAcc1 = 384;  // chain 1 of the accumulators
 constexpr int kX16Bytes = kMmaMaxN * kKChunk * 2;     // 8 KB
 constexpr int kCoreStride = 128;                      // bytes between 8-wide K cores
 constexpr int kGroupStride = (kKChunk / 8) * 128;     // bytes between 8-row groups (1 KB)
@@ -98,13 +100,6 @@ int mma_smem_bytes() { return mma_smem().total; }
 
 // ------------------------------------------------------------ PTX helpers --
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -351,21 +346,21 @@ __device__ __forceinline__ void convert_q4(const uint8_t *raw, uint32_t tmem_row
     }
 }
 
-// Q6_K group g of a raw block column (unit layout, gemv.cuh) -> fp16 stage.
+// Q6_K group g of a raw block column (unit layout body, gemv.cuh) -> fp16 stage.
 // Weights 64g .. 64g+63 are, in Q6_K terms, parts 2(g&1) and 2(g&1)+1 of the
 // 128-half g>>1, positions l = 0..31 (lanes 2(g>>1) and 2(g>>1)+1 of the
 // unit layout).  The 6-bit code is assembled in an fp16 mantissa (1024 + q,
 // or 1024 + 16q for the high nibbles), q - 32 is exact, and one fp16 multiply
 // by d*scale (rounded to fp16) gives the weight of q6_value
 // (inferencer.cu:473-487) with two roundings.
-__device__ __forceinline__ void convert_q6(const uint8_t *raw, uint32_t tmem_row, int row, int g, int lb, float scale) {
+__device__ __forceinline__ void convert_q6(const uint8_t *raw, uint32_t tmem_row, int row, int g, float scale) {
     const uint8_t *body = raw + row * 208;
     const int h = g >> 1, hi = g & 1;
     const uint4 *A = reinterpret_cast<const uint4 *>(body) + 2 * h;
     const uint4 *B = reinterpret_cast<const uint4 *>(body + 64) + 2 * h;
     const uint4 *H = reinterpret_cast<const uint4 *>(body + 128) + 2 * h;
     const uint2 scw = *reinterpret_cast<const uint2 *>(body + 192 + 8 * h);
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(raw + kQ6DOff + row * 16 + lb * 2)) * scale;
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(raw + kQ6DOff + row * 2)) * scale;
     const __half2 k1056 = __float2half2_rn(1056.f), k16th = __float2half2_rn(0.0625f), km96 = __float2half2_rn(-96.f);
 #pragma unroll 1
     for (int l2 = 0; l2 < 2; ++l2) {
@@ -583,21 +578,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
     const int tile_first = static_cast<int>(cluster_id()), tile_step = static_cast<int>(cluster_count());
     const int b0 = rank * p.bps, b1 = min(nb, b0 + p.bps);  // this part's block columns
     const uint32_t tmem_cols = kTmemCols;
+    const bool single = tile_first + tile_step >= p.total_tiles;  // this CTA has one tile
 
     MmaSeg *seg_s = reinterpret_cast<MmaSeg *>(smem + L.segs);
     int *wexp_s = reinterpret_cast<int *>(seg_s + kMaxSegs);
     if (warp == kProducerWarp) {
-        // the launch's segments into shared memory, TMA descriptors fetched early
+        // the launch's segments into shared memory
         if (lane < p.nseg) {
             const MmaSeg sg = p.seg[lane];
             seg_s[lane] = sg;
             for (int h = 0; h < 2; ++h) {
                 const int wi = h ? sg.w1 : sg.w0;
-                if (wi < 0) continue;
-                wexp_s[wi] = p.w[wi].scale_exp;
-                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.w[wi].body)) : "memory");
-                if (sg.type == kQ6K)
-                    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.w[wi].dvec)) : "memory");
+                if (wi >= 0) wexp_s[wi] = p.w[wi].scale_exp;
             }
         }
     }
@@ -612,7 +604,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             mbar_init(empty + i, 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(acc_full + i, 1);
+            mbar_init(acc_full + i, single ? 2 : 1);  // a commit from each issuing thread
             mbar_init(acc_empty + i, 4);
         }
         mbar_init(part_ready, ksplit);
@@ -631,35 +623,81 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
     const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
 
+    // MMA issue for the 64-wide groups in `mask` of every block column: D (fp32)
+    // [128 x n_pad] = A (fp16 weights in TMEM) * B (fp16 activation, K-major)^T.
+    // Even groups accumulate into chain 0, odd groups into chain 1 (summed by the
+    // epilogue).  One thread issues a tcgen05.mma about every 100 cycles
+    // whatever N, so a CTA with a single tile lets two epilogue warps, idle
+    // until then, issue one chain each; otherwise warp 1 issues both and the
+    // accumulators are double-buffered across tiles.
+    auto mma_loop = [&](uint32_t mask) {
+        const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(n_pad >> 3) << 17) | (8u << 24);
+        const uint64_t b_desc0 = umma_desc(smem_u32(smem + L.x16), kCoreStride, kGroupStride);
+        uint32_t blk = 0, i = 0;
+        for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
+            const int a = i & 1;
+            if (i >= 2) mbar_wait_bounded(acc_empty + a, ((i >> 1) - 1) & 1, p.status, cta_abort);
+            tc_fence_after();
+            const uint32_t dcol0 = tmem_base + static_cast<uint32_t>(a * n_pad), dcol1 = dcol0 + kTmemAcc1;
+            uint32_t acc0 = 0, acc1 = 0;
+            for (int b = b0; b < b1; ++b, ++blk) {
+                const uint32_t ph = (blk >> 1) & 1;
+#pragma unroll
+                for (int g = 0; g < kGroups; ++g) {
+                    if (!((mask >> g) & 1u)) continue;
+                    const int st = (blk & 1) * kGroups + g;
+                    mbar_wait_bounded(full + st, ph, p.status, cta_abort);
+                    tc_fence_after();
+                    // A: stage st's 32 TMEM columns, 8 per K=16 step; B: the descriptor's
+                    // address field advances by 16 B units (stage, then 256 B per K=16 step)
+                    const uint32_t ta = tmem_base + kTmemA + static_cast<uint32_t>(st * 32);
+                    const uint64_t bd = b_desc0 + static_cast<uint64_t>(st * (kX16Bytes >> 4));
+#pragma unroll
+                    for (int kk = 0; kk < kKChunk / 16; ++kk) {
+                        if (g & 1) {
+                            umma_f16_ta(dcol1, ta + kk * 8, bd + kk * 16, idesc, acc1);
+                            acc1 = 1u;
+                        } else {
+                            umma_f16_ta(dcol0, ta + kk * 8, bd + kk * 16, idesc, acc0);
+                            acc0 = 1u;
+                        }
+                    }
+                    umma_commit(empty + st);
+                }
+            }
+            umma_commit(acc_full + a);
+        }
+    };
+
     if (warp == kProducerWarp) {
         if (lane == 0) {
+            const uint64_t pol = policy_evict_first();  // weights are read once per step
             uint32_t rc = 0;
             int r = 0;
             for (int t = tile_first; t < p.total_tiles; t += tile_step) {
                 const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
                 const int lt = t - sg.tile0;
                 const bool pair = sg.w1 >= 0;
-                const int y0 = pair ? lt * 64 : lt * 128;
+                // the tile's two row groups: rows 0-63 and 64-127 of a plain tile, or
+                // row group lt of the gate and of the up matrix
+                const MmaWeight &wa = p.w[sg.w0], &wb = pair ? p.w[sg.w1] : p.w[sg.w0];
+                const long ga = pair ? lt : 2L * lt, gb = pair ? lt : 2L * lt + 1;
                 for (int b = b0; b < b1; ++b, ++rc) {
                     if (rc >= kRawStages)
                         mbar_wait_bounded(empty_raw + r, ((rc / kRawStages) - 1) & 1, p.status, cta_abort);
                     uint8_t *dst = smem + L.raw + r * kRawStageBytes;
                     if (sg.type == kQ4K) {
-                        mbar_arrive_expect_tx(full_raw + r, 128 * 144);
-                        tma_load_2d(dst, &p.w[sg.w0].body, b * 144, y0, full_raw + r);
-                        if (pair) tma_load_2d(dst + 64 * 144, &p.w[sg.w1].body, b * 144, y0, full_raw + r);
+                        mbar_arrive_expect_tx(full_raw + r, 2 * kMmaChunkQ4);
+                        bulk_g2s_evict_first(dst, wa.chunks + (ga * nb + b) * kMmaChunkQ4, kMmaChunkQ4, full_raw + r, pol);
+                        bulk_g2s_evict_first(dst + kMmaChunkQ4, wb.chunks + (gb * nb + b) * kMmaChunkQ4, kMmaChunkQ4, full_raw + r, pol);
                     } else {
-                        const int u = b / kUnitBlocks, lb = b % kUnitBlocks;
-                        const int n_u = min(kUnitBlocks, nb - u * kUnitBlocks);
-                        const int xb = u * q6_unit_bytes(kUnitBlocks) + lb * 208;
-                        const int xd = u * q6_unit_bytes(kUnitBlocks) + n_u * 208;
-                        mbar_arrive_expect_tx(full_raw + r, kRawStageBytes);
-                        tma_load_2d(dst, &p.w[sg.w0].body, xb, y0, full_raw + r);
-                        tma_load_2d(dst + kQ6DOff, &p.w[sg.w0].dvec, xd, y0, full_raw + r);
-                        if (pair) {
-                            tma_load_2d(dst + 64 * 208, &p.w[sg.w1].body, xb, y0, full_raw + r);
-                            tma_load_2d(dst + kQ6DOff + 64 * 16, &p.w[sg.w1].dvec, xd, y0, full_raw + r);
-                        }
+                        const uint8_t *ca = wa.chunks + (ga * nb + b) * kMmaChunkQ6;
+                        const uint8_t *cb = wb.chunks + (gb * nb + b) * kMmaChunkQ6;
+                        mbar_arrive_expect_tx(full_raw + r, 2 * kMmaChunkQ6);
+                        bulk_g2s_evict_first(dst, ca, kMmaChunkQ6Body, full_raw + r, pol);
+                        bulk_g2s_evict_first(dst + kMmaChunkQ6Body, cb, kMmaChunkQ6Body, full_raw + r, pol);
+                        bulk_g2s_evict_first(dst + kQ6DOff, ca + kMmaChunkQ6Body, kMmaRowGroup * 2, full_raw + r, pol);
+                        bulk_g2s_evict_first(dst + kQ6DOff + kMmaRowGroup * 2, cb + kMmaChunkQ6Body, kMmaRowGroup * 2, full_raw + r, pol);
                     }
                     if (++r == kRawStages) r = 0;
                 }
@@ -686,43 +724,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
-            // D (fp32) [128 x n_pad] = A (fp16, K-major) * B (fp16, K-major)^T
-            const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(n_pad >> 3) << 17) | (8u << 24);
-            const uint64_t b_desc0 = umma_desc(smem_u32(smem + L.x16), kCoreStride, kGroupStride);
-            uint32_t blk = 0, i = 0;
-            for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
-                const int a = i & 1;
-                if (i >= 2) mbar_wait_bounded(acc_empty + a, ((i >> 1) - 1) & 1, p.status, cta_abort);
-                tc_fence_after();
-                const uint32_t dcol = tmem_base + static_cast<uint32_t>(a * n_pad);
-                uint32_t accumulate = 0;
-                for (int b = b0; b < b1; ++b, ++blk) {
-                    const uint32_t ph = (blk >> 1) & 1;
-#pragma unroll
-                    for (int g = 0; g < kGroups; ++g) {
-                        const int st = (blk & 1) * kGroups + g;
-                        mbar_wait_bounded(full + st, ph, p.status, cta_abort);
-                        tc_fence_after();
-                        // A: stage st's 32 TMEM columns, 8 per K=16 step; B: the descriptor's
-                        // address field advances by 16 B units (stage, then 256 B per K=16 step)
-                        const uint32_t ta = tmem_base + kTmemA + static_cast<uint32_t>(st * 32);
-                        const uint64_t bd = b_desc0 + static_cast<uint64_t>(st * (kX16Bytes >> 4));
-#pragma unroll
-                        for (int kk = 0; kk < kKChunk / 16; ++kk) {
-                            umma_f16_ta(dcol, ta + kk * 8, bd + kk * 16, idesc, accumulate);
-                            accumulate = 1u;
-                        }
-                        umma_commit(empty + st);
-                    }
-                }
-                umma_commit(acc_full + a);
-            }
-        }
+        if (lane == 0 && !single) mma_loop(0xFu);
     } else if (warp < kXWarp) {
         // ---------------------------------------------------------- epilogue
         const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
         const int r = quad * 32 + lane;
+        if (single && warp < kEpiWarp0 + 2) {  // first issue one accumulation chain's MMAs
+            if (lane == 0) mma_loop(warp == kEpiWarp0 ? 0x5u : 0xAu);
+            __syncwarp();
+        }
         pdl_wait();
         float *xinv_s = reinterpret_cast<float *>(smem + L.tok);
         int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxN), *slot_s = pos_s + kMmaMaxN;
@@ -764,14 +774,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
             if (ksplit > 1 && i > 0) mbar_wait_cluster_bounded(part_free, (i - 1) & 1, p.status, cta_abort);
             mbar_wait_bounded(acc_full + a, (i >> 1) & 1, p.status, cta_abort);
             tc_fence_after();
-            // accumulator -> stage[token][row], scaled; 32 columns per TMEM wait
+            // accumulator (chain 0 + chain 1) -> stage[token][row], scaled
             float *stage = red;
             for (int c0 = 0; c0 < n_pad; c0 += 16) {
-                uint32_t v[16];
+                uint32_t v[16], w[16];
                 tmem_ld16_nw(taddr + c0, v);
+                tmem_ld16_nw(taddr + kTmemAcc1 + c0, w);
                 tmem_wait16(v);
+                tmem_wait16(w);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) stage[(c0 + k) * kStage + r] = __uint_as_float(v[k]) * wscale * xinv_s[c0 + k];
+                for (int k = 0; k < 16; ++k)
+                    stage[(c0 + k) * kStage + r] = (__uint_as_float(v[k]) + __uint_as_float(w[k])) * wscale * xinv_s[c0 + k];
             }
             tc_fence_before();
             __syncwarp();
@@ -871,7 +884,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
                 tc_fence_after();
                 const uint8_t *raw = smem + L.raw + r * kRawStageBytes;
                 if (sg.type == kQ4K) convert_q4(raw, tmem_row, row, g, scale);
-                else convert_q6(raw, tmem_row, row, g, b % kUnitBlocks, scale);
+                else convert_q6(raw, tmem_row, row, g, scale);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
@@ -1056,48 +1069,45 @@ cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks, int 
     return cudaGetLastError();
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+// ------------------------------------------------------- chunked weights --
 
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
+long mma_tile_bytes(int type, int rows, int cols) {
+    const long groups = ((rows + kMmaRowGroup - 1) / kMmaRowGroup + 1) / 2 * 2;
+    return groups * (cols / 256) * (type == kQ4K ? kMmaChunkQ4 : kMmaChunkQ6);
 }
 
-static int encode_box(CUtensorMap *m, const void *data, int rows, long row_bytes, int box_bytes, int box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return -1;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes), static_cast<cuuint32_t>(box_rows)};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(data), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+// One CTA per (row group, block column), one thread per row of the group.
+__global__ void mma_tile_repack_kernel(int type, const uint8_t *src, long row_bytes, int rows, int nb, uint8_t *dst) {
+    const long g = blockIdx.x / nb;
+    const int b = blockIdx.x % nb, i = threadIdx.x;
+    const long row = g * kMmaRowGroup + i;
+    uint8_t *chunk = dst + static_cast<long>(blockIdx.x) * (type == kQ4K ? kMmaChunkQ4 : kMmaChunkQ6);
+    if (type == kQ4K) {
+        uint4 *o = reinterpret_cast<uint4 *>(chunk + i * 144);
+        const uint4 *in = reinterpret_cast<const uint4 *>(src + row * row_bytes + b * 144L);
+        for (int k = 0; k < 9; ++k) o[k] = row < rows ? in[k] : make_uint4(0, 0, 0, 0);
+    } else {
+        // unit layout (gemv.cuh): unit u of kUnitBlocks blocks holds their bodies, then their d values
+        const int u = b / kUnitBlocks, lb = b % kUnitBlocks, n_u = min(kUnitBlocks, nb - u * kUnitBlocks);
+        const uint8_t *unit = src + row * row_bytes + static_cast<long>(u) * q6_unit_bytes(kUnitBlocks);
+        uint4 *o = reinterpret_cast<uint4 *>(chunk + i * 208);
+        const uint4 *in = reinterpret_cast<const uint4 *>(unit + lb * 208);
+        for (int k = 0; k < 13; ++k) o[k] = row < rows ? in[k] : make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint16_t *>(chunk + kMmaChunkQ6Body)[i] =
+            row < rows ? *reinterpret_cast<const uint16_t *>(unit + n_u * 208 + lb * 2) : 0;
+    }
 }
 
-int mma_make_weight(int type, const void *data, int rows, long row_bytes, int rows_per_box, MmaWeight *out, char *err,
-                    int err_len) {
-    std::memset(out, 0, sizeof(*out));
-    if ((reinterpret_cast<uintptr_t>(data) & 15) || (row_bytes & 15)) {
-        std::snprintf(err, err_len, "tensor-core path needs 16-byte aligned rows");
-        return -1;
-    }
-    const int body = type == kQ4K ? 144 : 208;
-    out->rows_per_box = rows_per_box;
-    int r = encode_box(&out->body, data, rows, row_bytes, body, rows_per_box);
-    if (r == 0 && type == kQ6K) r = encode_box(&out->dvec, data, rows, row_bytes, 16, rows_per_box);
-    if (r != 0) std::snprintf(err, err_len, "cuTensorMapEncodeTiled failed (%d)", r);
-    return r;
+cudaError_t mma_tile_repack_launch(int type, const uint8_t *src, long row_bytes, int rows, int cols, uint8_t *dst,
+                                   cudaStream_t stream) {
+    if ((type != kQ4K && type != kQ6K) || cols % 256 || rows < 1 || (row_bytes & 15) ||
+        (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+        return cudaErrorInvalidValue;
+    const int nb = cols / 256;
+    const long groups = mma_tile_bytes(type, rows, cols) / (static_cast<long>(nb) * (type == kQ4K ? kMmaChunkQ4 : kMmaChunkQ6));
+    mma_tile_repack_kernel<<<static_cast<unsigned>(groups * nb), kMmaRowGroup, 0, stream>>>(type, src, row_bytes, rows,
+                                                                                            nb, dst);
+    return cudaGetLastError();
 }
 
 // Clusters of k CTAs (one CTA per SM) that can be resident at once, k = 1..8.

@@ -13,16 +13,32 @@ constexpr int kMmaTileM = 128;    // weight rows per tile (TMEM lanes)
 constexpr int kMmaMaxN = 64;      // tokens per launch (MMA N, padded to 16)
 constexpr int kMmaMinBatch = 16;  // below this the CUDA-core GEMV is used
 
-// One weight matrix as the tensor-core path reads it: TMA descriptors over
-// its rows (Q4_K: one box per 144-byte block; Q6_K: one box per 208-byte
-// block body and one for the unit's 16 bytes of d), and a power-of-two scale
+// Row groups of the tensor-core path's weight layout.
+constexpr int kMmaRowGroup = 64;
+// Bytes of one (row group, block column) chunk: Q4_K 64 GGUF blocks of 144
+// bytes; Q6_K 64 block bodies of 208 bytes (unit layout order) then their 64
+// fp16 d values.
+constexpr int kMmaChunkQ4 = kMmaRowGroup * 144;
+constexpr int kMmaChunkQ6Body = kMmaRowGroup * 208;
+constexpr int kMmaChunkQ6 = kMmaChunkQ6Body + kMmaRowGroup * 2;
+
+// One weight matrix as the tensor-core path reads it: chunks [row group][block
+// column] of contiguous bytes (mma_tile_repack_launch), so that a stage of a
+// 128-row tile is two or four plain bulk copies, and a power-of-two scale
 // 2^scale_exp that keeps every dequantised weight in fp16's normal range.
 struct MmaWeight {
-    CUtensorMap body;   // box [rows_per_box][144 or 208 bytes]
-    CUtensorMap dvec;   // Q6_K only: box [rows_per_box][16 bytes]
+    const uint8_t *chunks;
     int scale_exp;
-    int rows_per_box;   // 128, or 64 for the two halves of a gate/up tile
+    int nblocks;  // block columns (cols / 256)
 };
+
+// Bytes of the chunked copy of a rows x cols matrix (row groups rounded up to
+// an even count, so that any 128-row tile reads inside the buffer).
+long mma_tile_bytes(int type, int rows, int cols);
+// Writes the chunked copy: src is the Q4_K GGUF layout or the Q6_K unit
+// layout (row_bytes per row); rows past `rows` are zero.
+cudaError_t mma_tile_repack_launch(int type, const uint8_t *src, long row_bytes, int rows, int cols, uint8_t *dst,
+                                   cudaStream_t stream);
 
 struct MmaSeg {
     int w0, w1;        // indexes into MmaParams::w (w1 < 0 unless a gate/up pair)
@@ -79,10 +95,6 @@ cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, 
 // over its block scales); written to *out_exp on the device.
 cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks_gguf_layout, int *out_max_bits,
                                   cudaStream_t stream);
-
-// Encodes the TMA descriptors of a weight (row_bytes per row, rows rows).
-int mma_make_weight(int type, const void *data, int rows, long row_bytes, int rows_per_box, MmaWeight *out,
-                    char *err, int err_len);
 
 // pdl: launch with programmatic stream serialisation; the kernel loads and
 // dequantises weights before waiting for the previous kernel, and reads the
