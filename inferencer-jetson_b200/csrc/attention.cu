@@ -15,6 +15,7 @@
 // engine's cache format).
 #include "attention.cuh"
 #include "common.cuh"
+#include "mma_gemm.cuh"
 
 namespace ijb {
 
@@ -453,7 +454,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 // items its in-flight chunks belong to), refilling a stage as soon as it is
 // used, so a warp's copies never drain between items and no CTA waits for
 // another wave.  A finished item leaves its softmax state (max, sum,
-// unnormalised output) per head for attention_merge_kernel, or the output
+// unnormalised output) per head for attention_finish_kernel, or the output
 // itself when it covers the whole sequence.  The last CTA to finish resets the
 // item counter.
 
@@ -700,56 +701,62 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(
     }
 }
 
-// One warp per (token, kv head) of more than one item: lane s holds item s's
-// max and sum (at most 32 items), the weights exp(m_s - M) come from a warp
-// max, then each lane sums two output dims over the items, KB items of every
-// head per round of loads.
+// One CTA per token.  Each warp merges the items of one kv head of a token
+// whose sequence spans more than one item: lane s holds item s's max and sum
+// (at most 32 items), the weights exp(m_s - M) come from a warp max, then each
+// lane sums two output dims over the items, KB items of every head per round
+// of loads.  When the O projection runs on the tensor cores (x16 set), the CTA
+// then builds the token's fp16 activation row for it (mma_prep_token), which
+// takes the place of the projection's own prep launch.
 template <int G>
-__global__ void __launch_bounds__(256) attention_merge_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(256) attention_finish_kernel(const __grid_constant__ AttnParams p) {
     constexpr int HD = 64, KB = G >= 8 ? 4 : 8;
     pdl_trigger();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int wid = static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-    const int b = wid / p.kv_heads, h = wid % p.kv_heads;
-    if (b >= p.batch) return;
-    const int nsplit = (p.tok_pos[b] + kAttnItem) / kAttnItem;
-    if (nsplit <= 1) return;
-    const float *part = p.partial + ((static_cast<long>(b) * p.heads + h * G) * p.max_splits) * (HD + 2);
-    float fg[G], Lg[G];
-    float2 O[G];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int b = blockIdx.x;
+    const int nsplit = b < p.batch ? (p.tok_pos[b] + kAttnItem) / kAttnItem : 0;
+    for (int h = warp; nsplit > 1 && h < p.kv_heads; h += 8) {
+        const float *part = p.partial + ((static_cast<long>(b) * p.heads + h * G) * p.max_splits) * (HD + 2);
+        float fg[G], Lg[G];
+        float2 O[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float *recs = part + static_cast<long>(g) * p.max_splits * (HD + 2);
-        const float ms = lane < nsplit ? recs[lane * (HD + 2)] : -INFINITY;
-        const float ls = lane < nsplit ? recs[lane * (HD + 2) + 1] : 0.f;
-        const float M = warp_max(ms);
-        fg[g] = lane < nsplit ? __expf(ms - M) : 0.f;
-        Lg[g] = warp_sum(fg[g] * ls);
-        O[g] = make_float2(0.f, 0.f);
+        for (int g = 0; g < G; ++g) {
+            const float *recs = part + static_cast<long>(g) * p.max_splits * (HD + 2);
+            const float ms = lane < nsplit ? recs[lane * (HD + 2)] : -INFINITY;
+            const float ls = lane < nsplit ? recs[lane * (HD + 2) + 1] : 0.f;
+            const float M = warp_max(ms);
+            fg[g] = lane < nsplit ? __expf(ms - M) : 0.f;
+            Lg[g] = warp_sum(fg[g] * ls);
+            O[g] = make_float2(0.f, 0.f);
+        }
+        for (int k0 = 0; k0 < nsplit; k0 += KB) {
+            float2 v[G][KB];
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int k = 0; k < KB; ++k)
+                    v[g][k] = k0 + k < nsplit ? reinterpret_cast<const float2 *>(
+                                                    part + (static_cast<long>(g) * p.max_splits + k0 + k) * (HD + 2) + 2)[lane]
+                                              : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int k = 0; k < KB; ++k) {
+                    const float fk = __shfl_sync(0xffffffffu, fg[g], (k0 + k) & 31);
+                    O[g].x = fmaf(v[g][k].x, fk, O[g].x);
+                    O[g].y = fmaf(v[g][k].y, fk, O[g].y);
+                }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float *out = p.out + static_cast<long>(b) * p.out_stride + (static_cast<long>(h) * G + g) * HD;
+            *reinterpret_cast<float2 *>(out + 2 * lane) = make_float2(O[g].x / Lg[g], O[g].y / Lg[g]);
+        }
     }
-    for (int k0 = 0; k0 < nsplit; k0 += KB) {
-        float2 v[G][KB];
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int k = 0; k < KB; ++k)
-                v[g][k] = k0 + k < nsplit
-                              ? reinterpret_cast<const float2 *>(part + (static_cast<long>(g) * p.max_splits + k0 + k) * (HD + 2) + 2)[lane]
-                              : make_float2(0.f, 0.f);
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int k = 0; k < KB; ++k) {
-                const float fk = __shfl_sync(0xffffffffu, fg[g], (k0 + k) & 31);
-                O[g].x = fmaf(v[g][k].x, fk, O[g].x);
-                O[g].y = fmaf(v[g][k].y, fk, O[g].y);
-            }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        float *out = p.out + static_cast<long>(b) * p.out_stride + (static_cast<long>(h) * G + g) * HD;
-        *reinterpret_cast<float2 *>(out + 2 * lane) = make_float2(O[g].x / Lg[g], O[g].y / Lg[g]);
+    if (p.x16) {
+        __syncthreads();  // the merged rows are read back below
+        mma_prep_token(p.out, p.out_stride, nullptr, 0.f, p.heads * HD, p.batch, b, p.n_pad, p.use_dp4a, p.x16, p.x_inv);
     }
 }
 
@@ -767,10 +774,10 @@ static cudaError_t launch_attn_stream(const AttnParams &p, cudaStream_t stream, 
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, attention_stream_kernel<G>, p);
     if (e != cudaSuccess) return e;
-    cfg.gridDim = dim3((p.batch * p.kv_heads + 7) / 8);
+    cfg.gridDim = dim3(p.x16 ? p.n_pad : p.batch);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&cfg, attention_merge_kernel<G>, p);
+    return cudaLaunchKernelEx(&cfg, attention_finish_kernel<G>, p);
 }
 
 typedef CUresult (*EncodeTiledFnA)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -871,7 +878,9 @@ cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
         return cudaErrorInvalidValue;
     if (p.max_splits * kAttnItem < 1) return cudaErrorInvalidValue;
     if (p.has_map && p.head_dim == 64 && !p.kv_f32) {
-        if (!p.work || p.num_ctas < 1 || p.batch > kStreamMaxBatch || p.max_splits > 32) return cudaErrorInvalidValue;
+        if (!p.work || p.num_ctas < 1 || p.batch > kStreamMaxBatch || p.max_splits > 32 ||
+            (p.x16 && (p.n_pad < p.batch || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.heads * 64 > kMaxCols)))
+            return cudaErrorInvalidValue;
         const int G = p.heads / p.kv_heads;
         if (G == 4) return launch_attn_stream<4>(p, stream, pdl);
         if (G == 8) return launch_attn_stream<8>(p, stream, pdl);

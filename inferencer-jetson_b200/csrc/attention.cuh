@@ -34,6 +34,12 @@ struct AttnParams {
     int *counters;         // [batch][kv_heads], zero between launches
     int *work;             // [2] streaming kernel's item counter and finished-CTA counter, zero between launches
     int num_ctas;          // streaming kernel grid (one CTA per SM)
+    // optional: the O projection's fp16 activation tile (mma_prep_launch layout),
+    // built by the streaming path's finish kernel instead of a separate prep
+    uint8_t *x16;
+    float *x_inv;
+    int n_pad;
+    int use_dp4a;
     uint32_t *status;      // device error word (bounded waits)
 };
 

@@ -213,11 +213,10 @@ struct ProjSeg {
     long out_stride;
 };
 
-void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const float *x, long x_stride,
-                       const float *norm_w, const ProjSeg *segs, int nsegs, char *kbase, long v_off) {
+// Whether a projection of gn tokens over `segs` runs on the tensor cores, and
+// the activation path (*dp: 1 = the reference's int8 quantisation) it uses.
+bool proj_uses_mma(const ijb_engine *e, int gn, const ProjSeg *segs, int nsegs, int *dp_out) {
     const ijb_model_desc &d = e->d;
-    const int *tpos = e->meta_dev + 2 * d.max_batch;
-    const int *tslot = e->meta_dev + 3 * d.max_batch;
     bool mma_ok = gn >= e->mma_min_batch;
     int dp = -1;
     for (int i = 0; i < nsegs && mma_ok; ++i) {
@@ -226,14 +225,32 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
         if (dp < 0) dp = sdp;
         mma_ok = w.has_mma && sdp == dp && (segs[i].w1 < 0 || e->w[segs[i].w1].has_mma);
     }
+    if (dp_out) *dp_out = dp;
+    return mma_ok;
+}
+
+// x16_ready: the activation tile of the (single, <= kMmaMaxN-token) tensor-core
+// chunk has already been built by the previous kernel.
+void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const float *x, long x_stride,
+                       const float *norm_w, const ProjSeg *segs, int nsegs, char *kbase, long v_off,
+                       bool x16_ready = false) {
+    const ijb_model_desc &d = e->d;
+    const int *tpos = e->meta_dev + 2 * d.max_batch;
+    const int *tslot = e->meta_dev + 3 * d.max_batch;
+    int dp = -1;
+    const bool mma_ok = proj_uses_mma(e, gn, segs, nsegs, &dp);
+    require(!x16_ready || (mma_ok && gn <= kMmaMaxN), "prepared activation without a single tensor-core chunk");
     const int cols = e->w[segs[0].w0].cols;
     if (mma_ok) {
         for (int t0 = 0; t0 < gn; t0 += kMmaMaxN) {
             const int tn = std::min(kMmaMaxN, gn - t0);
             const int n_pad = (tn + 15) / 16 * 16;
-            ck(mma_prep_launch(x + static_cast<long>(t0) * x_stride, x_stride, norm_w, d.eps, cols, tn, n_pad, dp,
-                               e->x16, e->x_inv, s, e->mma_pdl),
-               "activation prep launch");
+            if (!x16_ready) {
+                ck(mma_prep_launch(x + static_cast<long>(t0) * x_stride, x_stride, norm_w, d.eps, cols, tn, n_pad, dp,
+                                   e->x16, e->x_inv, s, e->mma_pdl),
+                   "activation prep launch");
+                ++g_launches;
+            }
             MmaParams m;
             std::memset(&m, 0, sizeof(m));
             for (int i = 0; i < nsegs; ++i) {
@@ -279,7 +296,7 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->mma_max_split, e->mma_split_cost, &m.bps);
             m.bulk_out = e->mma_bulk_out;
             ck(mma_gemm_launch(m, s, e->mma_pdl), "tensor-core GEMM launch");
-            g_launches += 2;
+            ++g_launches;
         }
         return;
     }
@@ -351,12 +368,20 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
             a.kv_map = e->kv_maps[l];
             a.has_map = 1;
         }
+        // the streaming attention's finish kernel also builds the O projection's
+        // activation tile when that projection is one tensor-core chunk
+        const ProjSeg o_segs[1] = {{L.o, -1, kEpiAdd, e->x, d.dim}};
+        int o_dp = 0;
+        const bool o_fused = attention_kernels(a) == 2 && n <= kMmaMaxN && proj_uses_mma(e, n, o_segs, 1, &o_dp);
+        if (o_fused) {
+            a.x16 = e->x16;
+            a.x_inv = e->x_inv;
+            a.n_pad = (n + 15) / 16 * 16;
+            a.use_dp4a = o_dp;
+        }
         ck(attention_launch(a, s, e->pdl), "attention launch");
         g_launches += attention_kernels(a);
-        {
-            const ProjSeg segs[1] = {{L.o, -1, kEpiAdd, e->x, d.dim}};
-            launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, segs, 1, nullptr, 0);
-        }
+        launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, o_segs, 1, nullptr, 0, o_fused);
         {
             const ProjSeg segs[1] = {{L.gate, L.up, kEpiSiluPair, e->h, d.hidden}};
             launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), segs,

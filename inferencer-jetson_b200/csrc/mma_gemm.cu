@@ -915,12 +915,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_c
 // with core j holding 64c + 4j + {0,2,1,3} and 64c + 32 + 4j + {0,2,1,3}.
 // Each thread owns cores; the 8 cores of a chunk sit on 8 adjacent lanes, so
 // a 32-wide quantisation group is an 8-lane shuffle reduction.
-__global__ void __launch_bounds__(256) mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
-                                                       int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
-                                                       float *x_inv) {
-    pdl_trigger();
-    pdl_wait();
-    const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__device__ void mma_prep_token(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch, int n,
+                               int n_pad, int use_dp4a, uint8_t *x16, float *x_inv) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ float part_s[8], amax_s[8];
     const long chunk_bytes = static_cast<long>(n_pad) * kKChunk * 2;
     const int cores = cols / 8;
@@ -1019,6 +1016,14 @@ __global__ void __launch_bounds__(256) mma_prep_kernel(const float *x, long x_st
         *reinterpret_cast<uint4 *>(dst_of(core)) = o;
     }
     if (tid == 0) x_inv[n] = ldexpf(1.0f, -kx);
+}
+
+__global__ void __launch_bounds__(256) mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
+                                                       int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
+                                                       float *x_inv) {
+    pdl_trigger();
+    pdl_wait();
+    mma_prep_token(x, x_stride, norm_w, eps, cols, batch, static_cast<int>(blockIdx.x), n_pad, use_dp4a, x16, x_inv);
 }
 
 // Bound of max|w| over GGUF blocks: Q4_K |d|*63*15 + |dmin|*63, Q6_K

@@ -90,6 +90,10 @@ struct MmaParams {
 // K-major layout.  Padding tokens up to n_pad are zero.
 cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
                             int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl);
+// The same for token n alone, by the 256 threads of the calling CTA (all of
+// them call it; it synchronises the block).
+__device__ void mma_prep_token(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch, int n,
+                               int n_pad, int use_dp4a, uint8_t *x16, float *x_inv);
 
 // Exponent e with max|w| * 2^e <= 2^15 for a quantised matrix (one reduction
 // over its block scales); written to *out_exp on the device.
