@@ -493,7 +493,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(
         fence_barrier_init();
     }
     pdl_trigger();
-    pdl_wait();
+    // work items from the step's token metadata (written before the step's first
+    // kernel), then wait for the previous kernel (Q and the newest K/V rows)
     if (warp == 0) {
         int run = 0;
         for (int b0 = 0; b0 < p.batch; b0 += 32) {
@@ -518,6 +519,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(
         if (lane == 0) first_s[0] = 0;
     }
     __syncthreads();
+    pdl_wait();
     const int total = first_s[p.batch];
     const int ps = p.page_size;
 
