@@ -6,7 +6,8 @@ import os
 import subprocess
 
 PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(PKG_ROOT, "lib", "libijb200.so")
+# IJB200_LIB selects another build of the same library (e.g. to compare two builds on one GPU)
+LIB_PATH = os.environ.get("IJB200_LIB") or os.path.join(PKG_ROOT, "lib", "libijb200.so")
 REPO_ROOT = os.path.dirname(PKG_ROOT)
 HEADER = os.path.join(REPO_ROOT, "include", "ijb200.h")
 
