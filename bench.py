@@ -270,9 +270,8 @@ def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one mma_gemm_kernel launch of
-# the gemm_q6k_b64 workload, from the ncu capture summarised in
-# profiles/mma_gemm_q6k_vocab_b64.md
-MMA_VOCAB_TRAFFIC = 215832576 + 15714304
+# the gemm_q6k_b64 workload, from an ncu capture of that launch
+MMA_VOCAB_TRAFFIC = 215909120 + 8392704
 
 
 def mma_roofline(eng, cuda, peak, iters=20, batch=64):
