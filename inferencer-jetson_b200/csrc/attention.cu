@@ -842,8 +842,17 @@ static cudaError_t attention_launch_t(const AttnParams &p, dim3 grid, cudaStream
     return cudaErrorInvalidValue;
 }
 
+// The streaming kernel serves fp16 caches with head_dim 64 up to 32 work items
+// (4096 positions) per sequence and kStreamMaxBatch tokens; anything else, or a
+// G it is not built for, goes to the CUDA-core split kernel.
+static bool stream_path(const AttnParams &p) {
+    const int G = p.kv_heads > 0 ? p.heads / p.kv_heads : 0;
+    return p.has_map && p.head_dim == 64 && !p.kv_f32 && p.work && p.num_ctas >= 1 && p.batch <= kStreamMaxBatch &&
+           p.max_splits <= 32 && (G == 1 || G == 2 || G == 4 || G == 8) && G * p.kv_heads == p.heads;
+}
+
 int attention_split_len() { return kAttnSplit; }
-int attention_kernels(const AttnParams &p) { return p.has_map && p.head_dim == 64 && !p.kv_f32 ? 2 : 1; }
+int attention_kernels(const AttnParams &p) { return stream_path(p) ? 2 : 1; }
 int attention_item_len() { return kAttnItem; }
 
 // Opts every instance in to its K/V tile shared memory on the current device
@@ -879,9 +888,8 @@ cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
     if (p.split_len != kAttnSplit || p.page_size < 8 || p.page_size > 32 || 32 % p.page_size)
         return cudaErrorInvalidValue;
     if (p.max_splits * kAttnItem < 1) return cudaErrorInvalidValue;
-    if (p.has_map && p.head_dim == 64 && !p.kv_f32) {
-        if (!p.work || p.num_ctas < 1 || p.batch > kStreamMaxBatch || p.max_splits > 32 ||
-            (p.x16 && (p.n_pad < p.batch || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.heads * 64 > kMaxCols)))
+    if (stream_path(p)) {
+        if (p.x16 && (p.n_pad < p.batch || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.heads * 64 > kMaxCols))
             return cudaErrorInvalidValue;
         const int G = p.heads / p.kv_heads;
         if (G == 4) return launch_attn_stream<4>(p, stream, pdl);

@@ -107,13 +107,16 @@ def test_1b_width_model_128_steps(cuda):
         assert agree >= 0.99, (kv_f32, agree)
 
 
-def test_ragged_step_matches_single_sequence_runs(cuda):
-    """Each sequence of a packed step matches the same sequence decoded alone."""
+@pytest.mark.parametrize("prompts,context", [((3, 40), 128), ((150, 300), 512)], ids=["one-item", "multi-item"])
+def test_ragged_step_matches_single_sequence_runs(cuda, prompts, context):
+    """Each sequence of a packed step matches the same sequence decoded alone
+    (multi-item: sequences longer than one 128-position attention work item,
+    so the split merge runs inside packed steps)."""
     cfg = synth.TINY
     weights = synth.make_model(cfg, seed=5)
-    reqs = synth.ragged_requests(5, prompt_range=(3, 40), output_range=(4, 8), seed=7, vocab_limit=cfg.vocab)
+    reqs = synth.ragged_requests(5, prompt_range=prompts, output_range=(4, 8), seed=7, vocab_limit=cfg.vocab)
     # batched engine
-    eng = Engine(cfg, weights, context=128, max_batch=8, max_seqs=8)
+    eng = Engine(cfg, weights, context=context, max_batch=8, max_seqs=8)
     seqs = [eng.seq_open() for _ in reqs]
     nxt = [eng.seq_prefill(s, r.prompt) for s, r in zip(seqs, reqs)]
     batched_logits, batched_tokens = [], []
@@ -126,7 +129,7 @@ def test_ragged_step_matches_single_sequence_runs(cuda):
     eng.close()
     # each sequence alone
     for i, r in enumerate(reqs):
-        e1 = Engine(cfg, weights, context=128, max_batch=1, max_seqs=2)
+        e1 = Engine(cfg, weights, context=context, max_batch=1, max_seqs=2)
         t = e1.prefill(r.prompt)
         assert t == nxt[i]
         for step in range(6):
@@ -136,6 +139,18 @@ def test_ragged_step_matches_single_sequence_runs(cuda):
             assert rel_l2(batched_logits[step][i], lg) < 1e-5
             assert t == batched_tokens[step][i]
         e1.close()
+
+
+def test_long_context_engine_uses_split_kernel(cuda):
+    """An fp16-cache, head_dim-64 engine whose context exceeds the streaming
+    attention's 32 work items (4096 positions) decodes through the CUDA-core
+    split kernel and still meets the logits and greedy bars."""
+    cfg = synth.TINY
+    weights = synth.make_model(cfg, seed=13)
+    prompt = synth.prompt_tokens(96, seed=4, vocab_limit=cfg.vocab)
+    errs, agree = _run_pair(cfg, weights, prompt, 8, context=4608)
+    assert errs.max() <= logits_bar(True), errs
+    assert agree >= 0.99
 
 
 def test_prefill_chunks_match_token_by_token(cuda):
