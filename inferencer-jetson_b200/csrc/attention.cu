@@ -346,11 +346,10 @@ __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
     return y;
 }
 
-constexpr int kMmaAttnTile = kAttnChunk * 128;  // one K or V tile: 32 rows of 64 fp16
 
-// One chunk of up to 32 positions on the tensor cores with positions as the
-// MMA rows and the group's query heads as its 8 columns (G <= 8):
-//   S^T[pos][head] = K[pos][:] . Q^T           (2 tiles of 16 positions)
+// One chunk of up to 16*MT positions on the tensor cores with positions as
+// the MMA rows and the group's query heads as its 8 columns (G <= 8):
+//   S^T[pos][head] = K[pos][:] . Q^T           (MT tiles of 16 positions)
 //   O^T[dim][head] += V^T[dim][pos] . P^T      (4 tiles of 16 dims)
 // The lane holds heads 2(lane%4) and 2(lane%4)+1: its online-softmax state
 // m[2], l[2]; the max and sum run over the 8 lanes of equal lane%4.  P^T
@@ -358,19 +357,21 @@ constexpr int kMmaAttnTile = kAttnChunk * 128;  // one K or V tile: 32 rows of 6
 // enter as fp16 hi + lo pairs (two MMAs each), so only the cache's own fp16
 // rounding remains; softmax is fp32 with __expf.  kt / vt: the chunk's
 // 128-byte-swizzled K and V tiles (V rows past cnt are zeroed here).
+template <int MT>
 __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, float scale, const uint32_t (&qb)[4][2][2],
                                              float (&o)[4][4], float (&m)[2], float (&l)[2], int lane) {
+    constexpr int CH = 16 * MT;  // positions of the chunk
     const int gid = lane >> 2, mi = lane >> 3;
-    if (cnt < kAttnChunk) {  // V rows past the last position: zero (their weights are zero, keep them finite)
-        for (int r = cnt + (lane >> 3); r < kAttnChunk; r += 4)
+    if (cnt < CH) {  // V rows past the last position: zero (their weights are zero, keep them finite)
+        for (int r = cnt + (lane >> 3); r < CH; r += 4)
             asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vt + r * 128 + (lane & 7) * 16), "r"(0u)
                          : "memory");
         __syncwarp();
     }
     // ---- scores: sc[mt] = S^T rows 16mt + gid (+8), heads 2(lane%4) (+1)
-    float sc[2][4];
+    float sc[MT][4];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
+    for (int mt = 0; mt < MT; ++mt) {
         sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -383,7 +384,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
     // ---- online softmax per head
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float v = 16 * mt + gid + 8 * (i >> 1) < cnt ? sc[mt][i] * scale : -INFINITY;
@@ -402,7 +403,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
     }
     float rs[2] = {0.f, 0.f};
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float pr = sc[mt][i] == -INFINITY ? 0.f : __expf(sc[mt][i] - m[i & 1]);
@@ -425,7 +426,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
     }
     // ---- O^T += V^T P^T, 16 positions per k-step
 #pragma unroll
-    for (int kp = 0; kp < 2; ++kp) {
+    for (int kp = 0; kp < MT; ++kp) {
         const __half2 ht = __floats2half2_rn(sc[kp][0], sc[kp][1]), hb = __floats2half2_rn(sc[kp][2], sc[kp][3]);
         const float2 ft = __half22float2(ht), fb = __half22float2(hb);
         const uint32_t bt = movm_t(*reinterpret_cast<const uint32_t *>(&ht));
@@ -458,10 +459,24 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 // itself when it covers the whole sequence.  The last CTA to finish resets the
 // item counter.
 
-constexpr int kStreamWarps = 8;
-constexpr int kStreamStages = 3;
+// Build-time shape of the streaming kernel (warps per CTA, chunks in flight per
+// warp, positions per chunk).  Measured on B200 (ragged64 step, same box):
+// 8 x 2 x 32 1.641 ms; 8 x 3 x 32 1.657; 6 x 2 x 64 1.673; 4 x 3 x 64 1.703;
+// 10 x 2 x 32 and 12 x 2 x 32 slower than 8 x 3 x 32.
+#ifndef IJB_STREAM_WARPS
+#define IJB_STREAM_WARPS 8
+#define IJB_STREAM_STAGES 2
+#define IJB_STREAM_CHUNK 32
+#endif
+constexpr int kStreamWarps = IJB_STREAM_WARPS;
+constexpr int kStreamStages = IJB_STREAM_STAGES;
+constexpr int kStreamChunk = IJB_STREAM_CHUNK;          // positions per chunk (per stage)
+constexpr int kMmaAttnTile = kStreamChunk * 128;       // one K or V tile: kStreamChunk rows of 64 fp16
 constexpr int kStreamQueue = kStreamStages + 1;  // items a warp's in-flight chunks can span, plus the one in use
-constexpr int kAttnItem = 128;                   // positions per work item
+#ifndef IJB_ATTN_ITEM
+#define IJB_ATTN_ITEM 128
+#endif
+constexpr int kAttnItem = IJB_ATTN_ITEM;         // positions per work item
 constexpr int kItemPages = kAttnItem / 8;        // page ids of an item (page_size >= 8)
 constexpr int kStreamMaxBatch = 256;
 constexpr int kStreamSmem = kStreamWarps * kStreamStages * 2 * kMmaAttnTile + 1024;  // + alignment slack
@@ -554,15 +569,15 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(
             it.j = r % nj;
             it.p0 = p0;
             it.p1 = p1;
-            it.nch = (p1 - p0 + kAttnChunk - 1) / kAttnChunk;
+            it.nch = (p1 - p0 + kStreamChunk - 1) / kStreamChunk;
         }
         __syncwarp();
         return true;
     };
     // chunk c of item `it` into stage `stage` (warp-uniform)
     auto issue = [&](const StreamItem &it, int c, int stage) {
-        const int t0 = it.p0 + c * kAttnChunk;
-        const int npg = (min(kAttnChunk, it.p1 - t0) + ps - 1) / ps;
+        const int t0 = it.p0 + c * kStreamChunk;
+        const int npg = (min(kStreamChunk, it.p1 - t0) + ps - 1) / ps;
         const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
         uint64_t *bb = &bar[warp][stage];
         if (lane == 0) mbar_arrive_expect_tx(bb, 2u * npg * ps * 128u);
@@ -647,8 +662,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(
         const int stage = done % ST;
         mbar_wait_bounded(&bar[warp][stage], (done / ST) & 1, p.status, &cta_abort);
         const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
-        const int t0 = it.p0 + cc * kAttnChunk;
-        attn_chunk_t(kt, vt, min(kAttnChunk, it.p1 - t0), p.scale, qa, o, m, l, lane);
+        const int t0 = it.p0 + cc * kStreamChunk;
+        attn_chunk_t<kStreamChunk / 16>(kt, vt, min(kStreamChunk, it.p1 - t0), p.scale, qa, o, m, l, lane);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic accesses before TMA refills the stage
         __syncwarp();
         ++done;
