@@ -462,7 +462,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 // Build-time shape of the streaming kernel (warps per CTA, chunks in flight per
 // warp, positions per chunk).  Measured on B200 (ragged64 step, same box):
 // 8 x 2 x 32 1.641 ms; 8 x 3 x 32 1.657; 6 x 2 x 64 1.673; 4 x 3 x 64 1.703;
-// 10 x 2 x 32 and 12 x 2 x 32 slower than 8 x 3 x 32.
+// 8 x 3 or 4 x 16 1.740; 10 x 2 x 32 and 12 x 2 x 32 slower than 8 x 3 x 32.
 #ifndef IJB_STREAM_WARPS
 #define IJB_STREAM_WARPS 8
 #define IJB_STREAM_STAGES 2
@@ -478,6 +478,8 @@ constexpr int kStreamQueue = kStreamStages + 1;  // items a warp's in-flight chu
 #endif
 constexpr int kAttnItem = IJB_ATTN_ITEM;         // positions per work item
 constexpr int kItemPages = kAttnItem / 8;        // page ids of an item (page_size >= 8)
+static_assert(kStreamChunk % 16 == 0 && kStreamChunk <= 64 && kAttnItem % kStreamChunk == 0 && kAttnItem <= 256,
+              "streaming attention shape");
 constexpr int kStreamMaxBatch = 256;
 constexpr int kStreamSmem = kStreamWarps * kStreamStages * 2 * kMmaAttnTile + 1024;  // + alignment slack
 
@@ -863,7 +865,8 @@ static cudaError_t attention_launch_t(const AttnParams &p, dim3 grid, cudaStream
 static bool stream_path(const AttnParams &p) {
     const int G = p.kv_heads > 0 ? p.heads / p.kv_heads : 0;
     return p.has_map && p.head_dim == 64 && !p.kv_f32 && p.work && p.num_ctas >= 1 && p.batch <= kStreamMaxBatch &&
-           p.max_splits <= 32 && (G == 1 || G == 2 || G == 4 || G == 8) && G * p.kv_heads == p.heads;
+           p.max_splits <= 32 && (G == 1 || G == 2 || G == 4 || G == 8) && G * p.kv_heads == p.heads &&
+           p.page_size <= kStreamChunk && kStreamChunk % p.page_size == 0;  // a chunk is whole pages
 }
 
 int attention_split_len() { return kAttnSplit; }
