@@ -3,9 +3,12 @@
 // graphs with programmatic dependent launch between kernels.
 //
 // It takes the place of FastGPU (inferencer.cu:1101-1180) and FastRunner
-// (:1182-1532).  Per layer a step launches five kernels where the reference
-// launches 13-17 (QKV + RoPE + KV write, attention, O + residual,
-// gate/up + SiLU, down + residual); the whole step is one CUDA graph.
+// (:1182-1532).  Per layer a step of 1-15 tokens launches five kernels where
+// the reference launches 13-17 (QKV + RoPE + KV write, attention, O +
+// residual, gate/up + SiLU, down + residual), plus the streaming attention's
+// finish kernel for an fp16, head_dim-64 cache; steps of 16-64 tokens add an
+// activation-prep launch before each tensor-core projection.  The whole step
+// is one CUDA graph.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -95,7 +98,7 @@ struct ijb_engine {
     std::vector<int> free_pages;
     int max_pages_per_seq = 0;
     int *page_table_dev = nullptr;
-    std::vector<CUtensorMap> kv_maps;  // per layer, for the tensor-core attention (fp16 cache, head_dim 64)
+    std::vector<CUtensorMap> kv_maps;  // per layer, for the streaming attention (fp16 cache, head_dim 64)
     int *page_table_host = nullptr;  // pinned mirror [max_seqs][max_pages_per_seq]
     std::vector<std::vector<int>> seq_pages;
     std::vector<int> seq_len;

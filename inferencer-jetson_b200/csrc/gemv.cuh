@@ -31,9 +31,9 @@ constexpr int kUnitBlocks = 8;  // super-blocks per streamed unit (2048 weights)
 //   [64, 128)  ql[g*64 + 32 + 16h .. +16]
 //   [128, 192) qh[g*32 + 16h .. +16]
 //   [192, 208) scales[g*8 + 2*part + h] for part 0..3 (4 bytes per lane)
-// Bodies start on 16-byte boundaries, so one block column of many rows is a
-// 2-D TMA box.  Only bytes move, so every weight is unchanged.  Q4_K rows keep
-// the GGUF layout (144-byte blocks are already 16-byte aligned).
+// Bodies start on 16-byte boundaries (the tensor-core path's chunked copy takes
+// them from here unchanged).  Only bytes move, so every weight is unchanged.
+// Q4_K rows keep the GGUF layout (144-byte blocks are already 16-byte aligned).
 __host__ __device__ inline int q6_unit_bytes(int nblocks) { return (nblocks * 210 + 15) / 16 * 16; }
 __host__ __device__ inline long q6_unit_row_bytes(int cols) {
     const int nb = cols / 256, full = nb / kUnitBlocks, rest = nb % kUnitBlocks;
