@@ -78,22 +78,28 @@ def hbm_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before the
+    warm-up; only the samples that arrive inside the timed region (mark_start /
+    mark_end) are reported."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval_ms: int = 50, cmd=None):
         self.index = index
-        self.rows = []
+        self.interval_ms = interval_ms
+        self.cmd = cmd
+        self.rows = []  # (arrival time, fields)
         self.proc = None
+        self.t0 = None
+        self.t1 = None
 
     def start(self):
+        cmd = self.cmd or ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                           "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)]
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except Exception:
@@ -103,7 +109,19 @@ class ClockSampler:
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) == 6:
-                self.rows.append(parts)
+                self.rows.append((time.perf_counter(), parts))
+
+    def wait_first(self, timeout_s: float = 3.0):
+        """Blocks until the sampler has produced a line (or timeout_s passed)."""
+        end = time.perf_counter() + timeout_s
+        while self.proc and not self.rows and time.perf_counter() < end and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
 
     def stop(self):
         if self.proc:
@@ -112,12 +130,15 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        rows = [r for t, r in self.rows if t0 <= t <= t1]
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[2 + i].lower() == "active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[2 + i].lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(rows), "interval_ms": self.interval_ms}
 
 
 def dist_setup(n_gpus):
@@ -411,14 +432,16 @@ def run_ours(args):
         pos += 1
         return 1, eng.last_step_ms(), wall, pos
 
+    sampler = ClockSampler(local)
+    sampler.start()
     # warm-up (includes graph capture)
     for _ in range(args.warmup):
         one_step()
         if args.workload == "ragged64":
             server.replace_finished()
+    sampler.wait_first()
     barrier(world)
-    sampler = ClockSampler(local)
-    sampler.start()
+    sampler.mark_start()
     launches0 = ijblib.load().ijb_kernel_launches()
     tokens, dev_ms, wall_s, kv_tokens, replaced_s = 0, 0.0, 0.0, 0, 0.0
     t_region = time.perf_counter()
@@ -437,6 +460,7 @@ def run_ours(args):
             server.replace_finished()
             replaced_s += time.perf_counter() - t0
     barrier(world)
+    sampler.mark_end()
     region_s = time.perf_counter() - t_region
     launches = ijblib.load().ijb_kernel_launches() - launches0
     clocks = sampler.stop()
