@@ -47,6 +47,26 @@ def test_matvec_tensor_core_path(cuda, batch, dp4a):
     eng.close()
 
 
+def test_split_k_results_are_bit_identical_across_runs(cuda):
+    """Projections wide enough to be split over a thread-block cluster (1B
+    widths: K = 2048 and 8192) give bit-identical outputs when run again: the
+    parts' partial sums are added in part order, whatever order they finish in."""
+    import torch
+    cfg = synth.ModelConfig("1b-width-1layer", dim=2048, layers=1, heads=32, kv_heads=8, hidden=8192, vocab=4096)
+    weights = synth.make_model(cfg, seed=21)
+    eng = Engine(cfg, weights, context=32, max_batch=64)
+    rng = np.random.default_rng(3)
+    shapes = {n: (t, r, c) for n, t, r, c in cfg.matrices()}
+    for name in ("blk.0.attn_q.weight", "blk.0.attn_output.weight", "blk.0.ffn_down.weight"):
+        _, rows, cols = shapes[name]
+        x = torch.from_numpy(rng.standard_normal((64, cols)).astype(np.float32)).to(cuda)
+        first = eng.matvec(name, x, 64).cpu().numpy()
+        for _ in range(3):
+            again = eng.matvec(name, x, 64).cpu().numpy()
+            assert np.array_equal(first, again), name
+    eng.close()
+
+
 def test_baseline_config_shapes_tensor_core(cuda):
     """BASELINE config 0 (Q4_K 8192x2048, d/dmin U[1e-3,1e-2]) and config 1
     (Q6_K 128256x2048) at batch 64 through a 1-layer engine's matvec."""
