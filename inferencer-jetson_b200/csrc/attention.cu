@@ -465,7 +465,11 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 // 8 x 3 or 4 x 16 1.740; 10 x 2 x 32 and 12 x 2 x 32 slower than 8 x 3 x 32.
 #ifndef IJB_STREAM_WARPS
 #define IJB_STREAM_WARPS 8
+#endif
+#ifndef IJB_STREAM_STAGES
 #define IJB_STREAM_STAGES 2
+#endif
+#ifndef IJB_STREAM_CHUNK
 #define IJB_STREAM_CHUNK 32
 #endif
 constexpr int kStreamWarps = IJB_STREAM_WARPS;
