@@ -177,3 +177,42 @@ def test_dp4a_path_noise_floor():
         err = np.linalg.norm(la - lb) / np.linalg.norm(la)
         assert lo <= err < hi, (dp4a, err)
         assert ta == tb
+
+
+def _reference_trees(values):
+    """argmax_blocks_cuda + argmax_final_cuda (inferencer.cu:1063-1099) in Python:
+    256-wide blocks, then one 512-wide pass, each a halving tree where a slot
+    takes its partner only if the partner is strictly greater."""
+    v = np.asarray(values, np.float32)
+    n = v.size
+    blocks = (n + 255) // 256
+    bv, bi = [], []
+    for b in range(blocks):
+        vals = [float(v[b * 256 + l]) if b * 256 + l < n else -np.inf for l in range(256)]
+        idx = [b * 256 + l for l in range(256)]
+        stride = 128
+        while stride:
+            for l in range(stride):
+                if vals[l + stride] > vals[l]:
+                    vals[l], idx[l] = vals[l + stride], idx[l + stride]
+            stride //= 2
+        bv.append(vals[0]); bi.append(idx[0])
+    bv += [-np.inf] * (512 - blocks); bi += [2 ** 31 - 1] * (512 - blocks)
+    stride = 256
+    while stride:
+        for i in range(stride):
+            if bv[i + stride] > bv[i]:
+                bv[i], bi[i] = bv[i + stride], bi[i + stride]
+        stride //= 2
+    return bi[0]
+
+
+@pytest.mark.parametrize("nan_at", [[0], [3], [700], [0, 2500], [256, 300], [131]])
+def test_oracle_argmax_nan_semantics_follow_the_reference_trees(nan_at):
+    """With NaN inputs the reference's trees neither skip NaN nor let it win
+    everywhere: a NaN in a left slot stays there and hides the partner subtree.
+    The oracle reproduces that exactly (the GPU argmax does not: there NaN never
+    wins)."""
+    v = np.random.default_rng(len(nan_at)).standard_normal(3000).astype(np.float32)
+    v[nan_at] = np.nan
+    assert O.argmax(v) == _reference_trees(v)
