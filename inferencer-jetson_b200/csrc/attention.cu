@@ -3,12 +3,18 @@
 // Replaces attention_cuda / attention_batch_cuda (inferencer.cu:982-1041): the
 // reference runs one 128-thread CTA per query head and walks positions 0..pos
 // serially with two block barriers per position over an fp32 [layer][ctx][kv]
-// cache.  Here one CTA handles one (token, kv head, split of positions): the
-// group's query heads share every K/V row it loads, lanes own positions while
-// scoring and head-dim elements while accumulating V, and each split keeps an
-// online-softmax state (max, sum, unnormalised output).  The last CTA of a
-// (token, kv head) to finish merges the splits (no device-wide wait: it is
-// elected with an atomic counter that it resets for the next launch).
+// cache.  Two kernels here, both splitting a sequence's positions and keeping
+// an online-softmax state (max, sum, unnormalised output) per split, the KV
+// group's query heads sharing every K/V row loaded:
+//  * attention_stream_kernel (fp16 cache, head_dim 64): persistent, one CTA of
+//    streaming warps per SM, 128-position work items, tensor-core chunks; the
+//    splits are merged by attention_finish_kernel (one CTA per token);
+//  * attention_kernel (fp32 cache or head_dim 128, and beyond the streaming
+//    kernel's limits): one CTA per (token, kv head, split of 512 positions) on
+//    CUDA cores, lanes owning positions while scoring and head-dim elements
+//    while accumulating V; the last CTA of a (token, kv head) to finish merges
+//    the splits (elected with an atomic counter that it resets for the next
+//    launch).
 //
 // Softmax: score = (q . k) * scale, p = exp(score - max), out = sum(p v)/sum(p),
 // with __expf as in the reference.  K/V are read as fp16 or fp32 (the
