@@ -14,25 +14,31 @@
 //     Q6_K: [64][208 B] block bodies and [64] fp16 d), with plain bulk copies
 //     into a 4-stage ring.
 //   * warp 6, lane 0: activation producer: per 64-wide K stage, one bulk copy
-//     of the prepared fp16 activation chunk into a 4-stage ring.
-//   * warps 7..14: dequantise.  Warps 7-10 convert the even 64-wide groups of
-//     a block column, warps 11-14 the odd ones, one thread per row, into fp16
-//     K-major tiles [128 rows][64 K] (UMMA canonical no-swizzle layout).
-//     Nibbles become fp16 through exponent-bias patterns (0x6400 | q is
-//     1024 + q) and one fp16 FMA applies the sub-block scale and offset; the
-//     K order inside each 8-wide core is permuted so that this needs no byte
-//     shuffles, and the activation tile is written in the same order.
-//   * warp 1, lane 0: issues tcgen05.mma (kind::f16, M=128, N = tokens
-//     rounded up to 16, K=16) into an fp32 accumulator in TMEM, double
-//     buffered across tiles; tcgen05.commit releases stages and signals
-//     finished accumulators.
-//   * warps 2..5 (one per TMEM lane quadrant): read the accumulator with
+//     of the prepared fp16 activation chunk into an 8-stage ring (two block
+//     columns in flight).
+//   * warps 7..22: dequantise, four groups of four warps; group g converts
+//     64-wide group g of every block column, each warp the 32 rows of its TMEM
+//     lane quadrant, one thread per row, straight into TMEM with tcgen05.st
+//     (the MMA's A operand).  Nibbles become fp16 through exponent-bias
+//     patterns (0x6400 | q is 1024 + q) and one fp16 FMA applies the sub-block
+//     scale and offset; the K order inside each 8-wide core is permuted so that
+//     this needs no byte shuffles, and the activation tile is written in the
+//     same order.
+//   * MMA issue: tcgen05.mma (kind::f16, M=128, N = tokens rounded up to 16,
+//     K=16) into two fp32 accumulator chains in TMEM (even and odd 64-wide
+//     groups); tcgen05.commit releases stages and signals finished
+//     accumulators.  A thread issues about one MMA per 100 cycles whatever N,
+//     so a CTA with a single tile has warps 2 and 3 issue one chain each
+//     before their epilogue work; a CTA with several tiles issues from warp 1
+//     with the accumulators double-buffered across tiles.
+//   * warps 2..5 (one per TMEM lane quadrant): read and add the two chains with
 //     tcgen05.ld, undo the two power-of-two scales and apply the fused
 //     epilogue of the GEMV (store, residual add, RoPE + paged K write, V write,
-//     SiLU * up, logits + argmax key).  With split K the parts first leave
-//     their partial sums in shared memory; each part then sums a slice of the
-//     tokens over the cluster's shared memory (DSMEM) in part order, so the
-//     result does not depend on timing.
+//     SiLU * up, logits + argmax key) through a [token][row] shared-memory
+//     tile, storing with coalesced thread stores.  With split K the parts
+//     first stage their partial sums in shared memory; each part then sums a
+//     slice of the tokens over the cluster's shared memory (DSMEM) in part
+//     order, so the result does not depend on timing.
 // All waits are bounded; TMEM is always released before the CTA exits.
 #include <cmath>
 #include <cstdio>
