@@ -2,18 +2,24 @@
 """Decode-throughput benchmark of the B200 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload ragged64|decode1]
+                    [--workload ragged64|decode1|gemv_q4k|gemv_q6k|gemm_q6k_b64|gemm_layer]
 
 Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
-  ragged64  Llama-3.2-1B-architecture Q4_K_M, 64 concurrent sequences, prompts
-            U[16,1024], targets U[32,256]; finished sequences are replaced
-            from the same distributions; paged fp16 KV, 16-token pages.  A
-            step is one packed decode step over the 64 live sequences.
+  ragged64  (default) Llama-3.2-1B-architecture Q4_K_M, 64 concurrent
+            sequences, prompts U[16,1024], targets U[32,256]; finished
+            sequences are replaced from the same distributions; paged fp16 KV,
+            16-token pages.  The population starts pre-aged (each sequence at
+            a uniform point of its output, its generated part prefilled), so
+            replacements happen inside the timed window and contexts sit at
+            the steady-state mix.  A step is one packed decode step over the
+            64 live sequences.  The line also carries a `decode1` record
+            (the batch-1 configuration on the same GPU).
   decode1   same model, one sequence: 512-token prompt (ids U[0,128000),
             seed 1), then greedy decode steps.
-  gemm_q6k_b64  the dominant kernel of ragged64 alone: the tensor-core
-            quantised GEMM (+ its activation prep) on the 1B vocab
-            projection, Q6_K 128256x2048, 64 tokens, through ijb_matvec.
+  gemv_q4k / gemv_q6k  BASELINE configs 0 / 1 (batch 1) in GB/s.
+  gemm_q6k_b64  the vocab projection alone (tensor-core GEMM, 64 tokens).
+  gemm_layer    one layer's seven projections alone (tensor-core GEMM, 64
+            tokens): the kernel the ragged64 roofline reports.
 `value` is whole-job decode tokens/s: tokens generated in the K timed steps
 on all ranks / max over ranks of the device time of those steps (CUDA events
 around each step's graph).  Replacement prefills run between timed steps and
@@ -33,6 +39,7 @@ import argparse
 import ctypes
 import json
 import os
+import re
 import subprocess
 import sys
 import threading
@@ -48,23 +55,32 @@ from ijb200 import lib as ijblib, synth  # noqa: E402
 
 MEASURED_PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
+PROFILES = os.path.join(REPO, "profiles")
+REF_HARNESS = os.path.join(REPO, "oracle", "_ref", "libref_harness.so")
+
+# arithmetic of each path (what the step computes in, not a precision claim)
+DTYPE_TC = ("fp16 x fp16 tcgen05 MMA, fp32 accumulate (weights: exact Q4_K/Q6_K dequant rounded to fp16; "
+            "activations: the reference's int8 per-32 quantise-dequantise rounded to fp16); fp16 KV")
+DTYPE_DP4A = "int8 x q4/q6 dp4a dot products, fp32 accumulate; fp16 KV"
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=48)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["ragged64", "decode1", "gemv_q4k", "gemv_q6k", "gemm_q6k_b64"],
-                    default="ragged64")
+    ap.add_argument("--workload", choices=["ragged64", "decode1", "gemv_q4k", "gemv_q6k", "gemm_q6k_b64",
+                                           "gemm_layer"], default="ragged64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="ragged64: skip the decode1 record, kernel timings and reference CUDA timings")
     ap.add_argument("--prompt", type=int, default=512, help="decode1 prompt length")
     ap.add_argument("--prompt-max", type=int, default=1024,
                     help="ragged64 longest prompt (1024 in the BASELINE config; smaller for profiling captures)")
     ap.add_argument("--nvtx-step", action="store_true",
                     help="wrap the last timed step in an NVTX range 'step' (ncu --nvtx-include step/)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 # --------------------------------------------------------------- helpers --
@@ -77,10 +93,35 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def profile_figure(name: str, key: str):
+    """A figure recorded in a profiles/ summary as a `key: value` line (an
+    ncu measurement of the same kernel, e.g. its DRAM bytes per launch)."""
+    try:
+        with open(os.path.join(PROFILES, name)) as f:
+            for line in f:
+                m = re.match(rf"\s*[-*]?\s*`?{re.escape(key)}`?\s*:\s*([0-9.eE+]+)", line)
+                if m:
+                    return float(m.group(1))
+    except OSError:
+        pass
+    return None
+
+
+REASON_NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+def _clock_record(rows, interval_ms, source):
+    sm = [r[0] for r in rows if r[0] is not None]
+    mx = [r[1] for r in rows if r[1] is not None]
+    reasons = sorted({n for r in rows for n in r[2]})
+    return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(rows), "interval_ms": interval_ms, "source": source}
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before the
-    warm-up; only the samples that arrive inside the timed region (mark_start /
-    mark_end) are reported."""
+    """nvidia-smi clocks and throttle reasons, sampled every `interval_ms` from
+    before the warm-up; only the samples that arrive inside the timed region
+    (mark_start / mark_end) are reported.  Fallback of NvmlClockSampler."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -90,7 +131,7 @@ class ClockSampler:
         self.index = index
         self.interval_ms = interval_ms
         self.cmd = cmd
-        self.rows = []  # (arrival time, fields)
+        self.rows = []  # (arrival time, (sm, max, reasons))
         self.proc = None
         self.t0 = None
         self.t1 = None
@@ -109,7 +150,9 @@ class ClockSampler:
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) == 6:
-                self.rows.append((time.perf_counter(), parts))
+                num = lambda s: float(s) if s.replace(".", "").isdigit() else None  # noqa: E731
+                reasons = [REASON_NAMES[i] for i in range(4) if parts[2 + i].lower() == "active"]
+                self.rows.append((time.perf_counter(), (num(parts[0]), num(parts[1]), reasons)))
 
     def wait_first(self, timeout_s: float = 3.0):
         """Blocks until the sampler has produced a line (or timeout_s passed)."""
@@ -132,13 +175,81 @@ class ClockSampler:
                 self.proc.kill()
         t0 = self.t0 if self.t0 is not None else float("-inf")
         t1 = self.t1 if self.t1 is not None else float("inf")
-        rows = [r for t, r in self.rows if t0 <= t <= t1]
-        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[2 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows), "interval_ms": self.interval_ms}
+        return _clock_record([r for t, r in self.rows if t0 <= t <= t1], self.interval_ms, "nvidia-smi")
+
+
+class NvmlClockSampler:
+    """Read-only NVML queries of the SM clock and the active clock-event
+    reasons every `interval_ms` (default 5 ms, so a timed region of a few tens
+    of milliseconds still holds several samples).  The GPU is found by its PCI
+    bus id, so the record belongs to the device this rank runs on whatever
+    CUDA_VISIBLE_DEVICES says.  Nothing is set."""
+
+    # nvmlClocksEventReason* bits
+    BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, cuda_index: int, interval_ms: float = 5.0):
+        import pynvml
+        import torch
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(cuda_index)
+        bus = "%08x:%02x:%02x.0" % (getattr(props, "pci_domain_id", 0), props.pci_bus_id, props.pci_device_id)
+        self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        self.interval_ms = interval_ms
+        self.rows = []
+        self.t0 = self.t1 = None
+        self._stop = threading.Event()
+
+    def _sample(self):
+        nv = self.nv
+        sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+        get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        bits = int(get(self.h))
+        return sm, self.max_mhz, [n for n, b in self.BITS.items() if bits & b]
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self.rows.append((time.perf_counter(), self._sample()))
+            except Exception:
+                pass
+            time.sleep(self.interval_ms / 1e3)
+
+    def start(self):
+        self._sample()  # fails here (not in the thread) when NVML cannot be read
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
+
+    def wait_first(self, timeout_s: float = 3.0):
+        end = time.perf_counter() + timeout_s
+        while not self.rows and time.perf_counter() < end:
+            time.sleep(0.001)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
+    def stop(self):
+        self._stop.set()
+        self.thread.join(timeout=2)
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        return _clock_record([r for t, r in self.rows if t0 <= t <= t1], self.interval_ms, "nvml")
+
+
+def make_clock_sampler(cuda_index: int):
+    try:
+        s = NvmlClockSampler(cuda_index)
+        s.start()
+        return s
+    except Exception:
+        s = ClockSampler(cuda_index)
+        s.start()
+        return s
 
 
 def dist_setup(n_gpus):
@@ -195,9 +306,15 @@ def job_throughput(world, tokens, dev_ms, wall_s):
 # ------------------------------------------------------------ workloads --
 
 class RaggedServer:
-    """64 live sequences; replaces finished ones from the request stream."""
+    """`batch` live sequences; replaces finished ones from the request stream.
 
-    def __init__(self, eng, batch, seed, vocab_limit=128000, prompt_max=1024):
+    aged: each initial sequence starts at a uniform point g0 in [0, target) of
+    its output, its prompt and the g0 tokens it would have generated prefilled
+    (seeded synthetic ids stand in for them), so the population is already in
+    its steady state when timing starts: sequences finish and are replaced
+    throughout the timed window, and contexts follow the steady-state mix."""
+
+    def __init__(self, eng, batch, seed, vocab_limit=128000, prompt_max=1024, aged=True):
         self.eng = eng
         self.prompt_max = prompt_max
         self.batch = batch
@@ -206,19 +323,21 @@ class RaggedServer:
         self.live = []  # [seq_id, next_token, generated, target]
         self.prefill_tokens = 0
         self.prefill_s = 0.0
+        self.replaced = 0
         for _ in range(batch):
-            self.live.append(self._admit())
+            self.live.append(self._admit(aged))
 
-    def _admit(self):
+    def _admit(self, aged=False):
         plen = int(self.rng.integers(16, self.prompt_max + 1))
         target = int(self.rng.integers(32, 257))
-        prompt = self.rng.integers(0, self.vocab_limit, size=plen).astype(np.int32)
+        g0 = int(self.rng.integers(0, target)) if aged else 0
+        prompt = self.rng.integers(0, self.vocab_limit, size=plen + g0).astype(np.int32)
         s = self.eng.seq_open()
         t0 = time.perf_counter()
         nxt = self.eng.seq_prefill(s, prompt)
         self.prefill_s += time.perf_counter() - t0
-        self.prefill_tokens += plen
-        return [s, nxt, 0, target]
+        self.prefill_tokens += len(prompt)
+        return [s, nxt, g0, target]
 
     def contexts(self):
         return [self.eng.seq_length(e[0]) for e in self.live]
@@ -242,15 +361,16 @@ class RaggedServer:
             if e[2] >= e[3]:
                 self.eng.seq_close(e[0])
                 self.live[i] = self._admit()
+                self.replaced += 1
 
 
 GEMV_CASES = (("q4k_ffn_gate_8192x2048", 12, 8192, 2048), ("q6k_lm_head_128256x2048", 14, 128256, 2048))
 
 
 def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
-    """Dominant kernel (gemv_kernel, the fused quantised GEMV) timed alone with
-    CUDA events on its stream: the 1B ffn_gate Q4_K shape
-    and the Q6_K lm_head (config 1), weights rotated over > 4x L2."""
+    """The CUDA-core GEMV (ijb_gemv_kernel, the batch-1 projection) timed
+    alone with CUDA events on its stream: the 1B ffn_gate Q4_K shape (BASELINE
+    config 0) and the Q6_K lm_head (config 1), weights rotated over > 4x L2."""
     import torch
     L = ijblib.load()
     out = {}
@@ -290,17 +410,70 @@ def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
     return out
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one mma_gemm_kernel launch of
-# the gemm_q6k_b64 workload, from an ncu capture of that launch
-MMA_VOCAB_TRAFFIC = 215909120 + 8392704
+def _timed_launches(fn, iters, stream_obj):
+    """Mean milliseconds per fn() over `iters` calls, CUDA events on stream_obj."""
+    import torch
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream_obj):
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream_obj)
+        for _ in range(iters):
+            fn()
+        b.record(stream_obj)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
 
 
-def mma_roofline(eng, cuda, peak, iters=20, batch=64):
-    """The tensor-core GEMM timed alone with CUDA events on its stream: the
-    vocab projection (Q6_K 128256x2048, the largest launch of a decode step)
-    for `batch` tokens through ijb_matvec, each launch = activation prep +
-    mma_gemm_kernel.  Algorithmic bytes: the Q6_K weights as stored (unit
-    layout), the fp32 activations read and the fp32 logits written."""
+def layer_roofline(eng, cuda, peak, iters=20, batch=64, layer=0):
+    """The step's dominant kernel: the tensor-core GEMM (ijb_mma_gemm_kernel,
+    each launch preceded by its activation prep ijb_mma_prep_kernel) over one
+    layer's seven projections (q, k, v, o, gate, up, down) for `batch` tokens
+    through ijb_matvec, timed with CUDA events on its own stream.  Algorithmic
+    bytes: the weights as stored + the fp32 activations read + the fp32
+    outputs written.  In the step the same weights go through four fused
+    launches (QKV, O, gate/up, down); here each matrix is one launch."""
+    import torch
+    L = ijblib.load()
+    cfg = eng.cfg
+    side = torch.cuda.Stream(device=cuda)
+    stream = side.cuda_stream
+    shapes = {n: (t, r, c) for n, t, r, c in cfg.matrices()}
+    names = [f"blk.{layer}.{m}.weight" for m in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate",
+                                                 "ffn_up", "ffn_down")]
+    per = {}
+    total_ms, total_bytes, w_bytes = 0.0, 0, 0
+    for name in names:
+        t, rows, cols = shapes[name]
+        x = torch.randn(batch, cols, device=cuda)
+        y = torch.empty(batch, rows, device=cuda)
+        idx = eng.tensor_index(name)
+
+        def launch():
+            ijblib.check(L.ijb_matvec(eng.h, idx, x.data_ptr(), y.data_ptr(), cols, rows, batch,
+                                      ctypes.c_void_p(stream)), eng.h)
+        ms = _timed_launches(launch, iters, side)
+        wb = rows * (cols // 256) * synth.BLOCK_BYTES[t]
+        algo = wb + batch * cols * 4 + batch * rows * 4
+        per[name.split(".")[2]] = {"us": ms * 1e3, "gbs": algo / (ms * 1e-3) / 1e9}
+        total_ms += ms
+        total_bytes += algo
+        w_bytes += wb
+    gbs = total_bytes / (total_ms * 1e-3) / 1e9
+    traffic = profile_figure("mma_gemm_layer_ragged64.md", "dram_bytes_per_layer")
+    return {"kernel": f"ijb_mma_gemm_kernel + ijb_mma_prep_kernel, one layer's 7 projections, {batch} tokens "
+                      f"(1B widths)", "us_per_layer": total_ms * 1e3, "algorithmic_bytes": total_bytes,
+            "weight_bytes": w_bytes, "gbs": gbs, "frac": gbs / peak, "traffic": traffic,
+            "traffic_source": "profiles/mma_gemm_layer_ragged64.md (ncu dram__bytes_read.sum + "
+                              "dram__bytes_write.sum over the layer's 14 launches)" if traffic else None,
+            "per_projection": per}
+
+
+def mma_vocab_roofline(eng, cuda, peak, iters=20, batch=64):
+    """The vocab projection (Q6_K 128256x2048, the largest single launch of a
+    step) through ijb_matvec for `batch` tokens: activation prep +
+    ijb_mma_gemm_kernel, CUDA events on its own stream."""
     import torch
     L = ijblib.load()
     cfg = eng.cfg
@@ -308,55 +481,53 @@ def mma_roofline(eng, cuda, peak, iters=20, batch=64):
     cols, rows = cfg.dim, cfg.vocab
     x = torch.randn(batch, cols, device=cuda)
     y = torch.empty(batch, rows, device=cuda)
-    side = torch.cuda.Stream(device=cuda)  # a real stream handle (0 would mean the engine's own stream)
+    side = torch.cuda.Stream(device=cuda)
     stream = side.cuda_stream
+
     def launch():
         ijblib.check(L.ijb_matvec(eng.h, idx, x.data_ptr(), y.data_ptr(), cols, rows, batch, ctypes.c_void_p(stream)),
                      eng.h)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(side):
-        for _ in range(3):
-            launch()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(side)
-        for _ in range(iters):
-            launch()
-        b.record(side)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / iters
-    w_bytes = rows * L.ijb_q6k_planar_row_bytes(cols)
+    ms = _timed_launches(launch, iters, side)
+    w_bytes = rows * (cols // 256) * 210
     algo = w_bytes + batch * cols * 4 + batch * rows * 4
     gbs = algo / (ms * 1e-3) / 1e9
+    traffic = profile_figure("mma_gemm_q6k_vocab_b64.md", "dram_bytes_per_launch")
     return {"us_per_launch": ms * 1e3, "algorithmic_bytes": algo, "gbs": gbs, "frac": gbs / peak,
-            "kernel": f"mma_gemm_kernel + activation prep (Q6_K {rows}x{cols} vocab projection, {batch} tokens)",
-            "traffic": MMA_VOCAB_TRAFFIC}
+            "kernel": f"ijb_mma_gemm_kernel + ijb_mma_prep_kernel (Q6_K {rows}x{cols} vocab projection, {batch} tokens)",
+            "traffic": traffic}
 
 
-def run_gemm(args):
-    """The dominant kernel of ragged64 alone (see mma_roofline)."""
-    import torch
-    world, rank, local = dist_setup(args.gpus)
-    cuda = torch.device(f"cuda:{local}")
-    peak, src = hbm_peak()
-    full = synth.LLAMA_1B
-    cfg = synth.ModelConfig("llama-3.2-1b-1layer", dim=full.dim, layers=1, heads=full.heads,
-                            kv_heads=full.kv_heads, hidden=full.hidden, vocab=full.vocab)
-    from ijb200.engine import Engine
-    eng = Engine(cfg, synth.make_model(cfg, seed=0), context=32, max_batch=64, device=local)
-    r = mma_roofline(eng, cuda, peak, iters=max(args.steps, 5))
-    eng.close()
-    if rank != 0:
-        return None
-    return {"metric": "GEMM HBM GB/s (Q6_K 128256x2048 vocab projection, 64 tokens)", "value": r["gbs"],
-            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 3, "ms_per_step": r["us_per_launch"] / 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16 x fp16 (exact dequant, int8-path activations), fp32 accumulate",
-            "data": "synthetic (seeded)", "config": {"workload": "gemm_q6k_b64", "l2": "weights 216 MB > L2"},
-            "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peak, "unit": "GB/s", "frac": r["frac"],
-                         "traffic": r["traffic"], "kernel": r["kernel"], "peak_source": src}}
+def reference_cuda_gemv(cases=GEMV_CASES):
+    """The reference's own CUDA GEMVs (FastGPU::matvec: quantize_x32_cuda +
+    gemv_q4_dp4a / gemv_q6_dp4a, inferencer.cu:544-674, :1156-1171, built
+    unmodified for sm_100a into oracle/_ref/) timed on this GPU with CUDA
+    events over weights rotated across > 4x L2, same inputs as gemv_roofline."""
+    if not os.path.exists(REF_HARNESS):
+        return {"unavailable": "oracle/_ref/libref_harness.so not built (the reference tree was absent at build)"}
+    L = ctypes.CDLL(REF_HARNESS)
+    L.ref_time_matvec.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.POINTER(ctypes.c_float)]
+    L.ref_last_error.restype = ctypes.c_char_p
+    rng = np.random.default_rng(0)
+    out = {}
+    for name, qt, rows, cols in cases:
+        w = synth.quant_matrix(rng, qt, rows, cols)
+        x = np.random.default_rng(1).standard_normal(cols).astype(np.float32)
+        copies = max(1, int(np.ceil(4 * 126e6 / w.nbytes)))
+        ms = ctypes.c_float()
+        rc = L.ref_time_matvec(qt, w.ctypes.data, cols, rows, x.ctypes.data, 1, 1, 4, copies, max(20, 4 * copies),
+                               ctypes.byref(ms))
+        if rc:
+            out[name] = {"error": L.ref_last_error().decode()}
+            continue
+        algo = w.nbytes + cols * 4 + rows * 4
+        out[name] = {"us_per_launch": ms.value * 1e3, "gbs": algo / (ms.value * 1e-3) / 1e9,
+                     "path": "INT8 DP4A (reference default), 4 warps per Q6_K CTA"}
+    return out
 
 
-def cpu_baseline(cfg, weights, contexts, threads, budget_s=20.0):
+def cpu_forward(cfg, weights, contexts, threads, budget_s=20.0):
     """The oracle's FastRunner::forward on the host cores: decode one token at
     each sampled context length; returns tokens/s and the sample used."""
     import oracle as O
@@ -377,6 +548,27 @@ def cpu_baseline(cfg, weights, contexts, threads, budget_s=20.0):
     return done / t_total, used
 
 
+def cpu_gemv(threads, budget_s=6.0):
+    """The oracle's FastGPU::matvec (INT8 path) on the host cores over the two
+    GEMV configs, GB/s of quantised weights + activation + output."""
+    import oracle as O
+    O.set_threads(threads)
+    rng = np.random.default_rng(0)
+    out = {}
+    for name, qt, rows, cols in GEMV_CASES:
+        w = synth.quant_matrix(rng, qt, rows, cols)
+        x = rng.standard_normal(cols).astype(np.float32)
+        n, t = 0, 0.0
+        while t < budget_s / 2 and n < 50:
+            t0 = time.perf_counter()
+            O.matvec(qt, w, x, cols, rows)
+            t += time.perf_counter() - t0
+            n += 1
+        algo = w.nbytes + cols * 4 + rows * 4
+        out[name] = {"ms_per_call": t / n * 1e3, "gbs": algo * n / t / 1e9, "calls": n}
+    return out
+
+
 # ------------------------------------------------------------------ arms --
 
 def run_gemv(args):
@@ -391,17 +583,81 @@ def run_gemv(args):
         return None
     return {"metric": "GEMV HBM GB/s (" + case[0] + ", batch 1)", "value": r["gbs"], "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["us_per_launch"] / 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dp4a x q4/q6",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_DP4A,
             "data": "synthetic (seeded)", "config": {"workload": case[0], "rotated_copies": r["rotated_copies"]},
             "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peak, "unit": "GB/s", "frac": r["frac"],
-                         "traffic": None, "peak_source": src}}
+                         "traffic": None, "peak_source": src},
+            "reference_cuda": reference_cuda_gemv((case,)).get(case[0])}
+
+
+def _layer_engine(local, layers=1):
+    full = synth.LLAMA_1B
+    cfg = synth.ModelConfig(f"llama-3.2-1b-{layers}layer", dim=full.dim, layers=layers, heads=full.heads,
+                            kv_heads=full.kv_heads, hidden=full.hidden, vocab=full.vocab)
+    from ijb200.engine import Engine
+    return Engine(cfg, synth.make_model(cfg, seed=0), context=32, max_batch=64, device=local)
+
+
+def run_gemm(args):
+    """The tensor-core GEMM alone: the vocab projection (gemm_q6k_b64) or one
+    layer's seven projections (gemm_layer)."""
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    cuda = torch.device(f"cuda:{local}")
+    peak, src = hbm_peak()
+    eng = _layer_engine(local)
+    if args.workload == "gemm_layer":
+        r = layer_roofline(eng, cuda, peak, iters=max(args.steps, 5))
+        metric, value, ms = "GEMM HBM GB/s (one 1B layer's 7 projections, 64 tokens)", r["gbs"], r["us_per_layer"] / 1e3
+    else:
+        r = mma_vocab_roofline(eng, cuda, peak, iters=max(args.steps, 5))
+        metric, value, ms = "GEMM HBM GB/s (Q6_K 128256x2048 vocab projection, 64 tokens)", r["gbs"], r["us_per_launch"] / 1e3
+    eng.close()
+    if rank != 0:
+        return None
+    return {"metric": metric, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 3,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_TC,
+            "data": "synthetic (seeded)", "config": {"workload": args.workload, "l2": "weights > L2 per pass"},
+            "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                         "traffic": r["traffic"], "kernel": r["kernel"], "peak_source": src}}
+
+
+def decode1_record(cuda, local, cfg, weights, peak, steps, warmup, prompt_len=512):
+    """BASELINE config 2 on this GPU: batch 1 after a 512-token prompt,
+    `steps` greedy steps (device time per step from CUDA events around the
+    step graph; e2e wall time of the ijb_forward calls)."""
+    from ijb200.engine import Engine
+    eng = Engine(cfg, weights, context=prompt_len + steps + warmup + 8, max_batch=1, max_seqs=2, device=local)
+    prompt = synth.prompt_tokens(prompt_len, seed=1)
+    nxt = eng.prefill(prompt)
+    pos = len(prompt)
+    for _ in range(warmup):
+        nxt = eng.forward(nxt, pos, True)
+        pos += 1
+    dev_ms, wall, ctx = 0.0, 0.0, 0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        nxt = eng.forward(nxt, pos, True)
+        wall += time.perf_counter() - t0
+        dev_ms += eng.last_step_ms()
+        pos += 1
+        ctx += pos
+    eng.close()
+    step_bytes = cfg.weight_bytes() + cfg.kv_bytes_per_token(2) * ctx / steps
+    ms = dev_ms / steps
+    return {"metric": "decode tokens/s (1B Q4_K_M, batch 1)", "value": steps / (dev_ms / 1e3), "unit": "tokens/s",
+            "ms_per_step": ms, "steps": steps, "warmup": warmup, "dtype": DTYPE_DP4A,
+            "e2e": {"value": steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
+            "config": {"workload": f"llama-3.2-1b Q4_K_M decode, batch 1, {prompt_len}-token prompt"},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
+                              "frac": step_bytes / (ms * 1e-3) / 1e9 / peak}}
 
 
 def run_ours(args):
     import torch
     if args.workload.startswith("gemv"):
         return run_gemv(args)
-    if args.workload == "gemm_q6k_b64":
+    if args.workload.startswith("gemm"):
         return run_gemm(args)
     world, rank, local = dist_setup(args.gpus)
     cuda = torch.device(f"cuda:{local}")
@@ -411,7 +667,7 @@ def run_ours(args):
     weights = synth.make_model(cfg, seed=0)
     from ijb200.engine import Engine
     if args.workload == "ragged64":
-        batch, context = 64, 1024 + 256 + 16
+        batch, context = 64, args.prompt_max + 256 + 16
         eng = Engine(cfg, weights, context=context, max_batch=batch, max_seqs=batch + 1, device=local)
         server = RaggedServer(eng, batch, seed=1000 + rank, prompt_max=args.prompt_max)
     else:
@@ -432,14 +688,14 @@ def run_ours(args):
         pos += 1
         return 1, eng.last_step_ms(), wall, pos
 
-    sampler = ClockSampler(local)
-    sampler.start()
+    sampler = make_clock_sampler(local)
     # warm-up (includes graph capture)
     for _ in range(args.warmup):
         one_step()
         if args.workload == "ragged64":
             server.replace_finished()
     sampler.wait_first()
+    replaced0 = server.replaced if args.workload == "ragged64" else 0
     barrier(world)
     sampler.mark_start()
     launches0 = ijblib.load().ijb_kernel_launches()
@@ -464,6 +720,8 @@ def run_ours(args):
     region_s = time.perf_counter() - t_region
     launches = ijblib.load().ijb_kernel_launches() - launches0
     clocks = sampler.stop()
+    if clocks.get("sm_mhz"):
+        clocks["ms_per_step_x_sm_mhz"] = dev_ms / args.steps * clocks["sm_mhz"]
 
     value, e2e, max_dev_ms = job_throughput(world, tokens, dev_ms, wall_s)
     ms_per_step = max_dev_ms / args.steps
@@ -477,45 +735,74 @@ def run_ours(args):
 
     result = None
     if rank == 0:
-        kern = gemv_roofline(cuda, peak)
-        dom = mma_roofline(eng, cuda, peak) if args.workload == "ragged64" else dict(
-            kern["q6k_lm_head_128256x2048"], kernel="gemv_kernel (Q6_K lm_head 128256x2048, B=1)", traffic=None)
-        cpu = None
+        ragged = args.workload == "ragged64"
+        extras = ragged and not args.no_extras
+        kern = gemv_roofline(cuda, peak) if (extras or not ragged) else None
+        if ragged:
+            dom = layer_roofline(eng, cuda, peak)
+            vocab = mma_vocab_roofline(eng, cuda, peak) if extras else None
+        else:
+            dom = dict(kern["q6k_lm_head_128256x2048"], traffic=None,
+                       kernel="ijb_gemv_kernel (Q6_K lm_head 128256x2048, B=1)")
+            vocab = None
+        ctxs = ([int(c) for c in server.contexts()[:8]] if ragged else [pos] * 4)
+        eng.close()
+        eng = None
+        torch.cuda.empty_cache()
+        d1 = decode1_record(cuda, local, cfg, weights, peak, 32, 4) if extras else None
+        cpu = cpu_extra = None
         if world == 1 and not args.no_cpu_baseline:
-            ctxs = ([int(c) for c in server.contexts()[:8]] if args.workload == "ragged64" else [pos] * 4)
             nthreads = os.cpu_count() or 1
-            tps, used = cpu_baseline(cfg, weights, ctxs, nthreads)
+            tps, used = cpu_forward(cfg, weights, ctxs, nthreads)
             cpu = {"value": tps, "unit": "tokens/s", "cores": nthreads, "kind": "port",
                    "sample": f"oracle FastRunner::forward (INT8 path), one decode token at each context {used}, "
                              f"{nthreads} threads"}
+            if extras:
+                tps1, used1 = cpu_forward(cfg, weights, ctxs[:2], 1, budget_s=8.0)
+                cpu_extra = {"forward_1_thread": {"value": tps1, "unit": "tokens/s", "cores": 1,
+                                                  "sample": f"one decode token at each context {used1}"},
+                             "gemv_1_thread": cpu_gemv(1), f"gemv_{nthreads}_threads": cpu_gemv(nthreads)}
         h2d = 4 * batch * 4  # token, seq, position, KV slot per entry (int32)
         result = {
-            "metric": "decode tokens/s (1B Q4_K_M, batch 64)" if args.workload == "ragged64"
-            else "decode tokens/s (1B Q4_K_M, batch 1)",
+            "metric": "decode tokens/s (1B Q4_K_M, batch 64)" if ragged else "decode tokens/s (1B Q4_K_M, batch 1)",
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8xq4/q6 dp4a, fp32 accumulate, fp16 KV", "data": "synthetic (random-init weights, seeded)",
+            "dtype": DTYPE_TC if ragged else DTYPE_DP4A, "data": "synthetic (random-init weights, seeded)",
             "config": {"workload": f"llama-3.2-1b Q4_K_M ragged decode, 64 seqs, prompts U[16,{args.prompt_max}], "
-                                   "outputs U[32,256], replacement" if args.workload == "ragged64"
+                                   "outputs U[32,256], replacement, pre-aged population" if ragged
                        else f"llama-3.2-1b Q4_K_M decode, batch 1, {args.prompt}-token prompt",
                        "batch_per_gpu": batch, "page_size": 16, "kv": "fp16 paged",
                        "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (836 MB weights/step)",
-                       "mean_context": kv_tokens / args.steps / batch},
+                       "mean_context": kv_tokens / args.steps / batch,
+                       "replaced_in_window": (server.replaced - replaced0) if ragged else 0},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * batch},
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": dom["frac"], "traffic": dom["traffic"], "kernel": dom["kernel"],
-                         "us_per_launch": dom["us_per_launch"], "peak_source": peak_src},
+                         "peak_source": peak_src,
+                         **({k: dom[k] for k in ("us_per_layer", "weight_bytes", "algorithmic_bytes",
+                                                 "traffic_source", "per_projection")} if ragged else
+                            {"us_per_launch": dom["us_per_launch"]})},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak},
-            "gemv": kern,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "setup_s": setup_s,
             "region_wall_s": region_s,
         }
-        if args.workload == "ragged64":
+        if vocab:
+            result["vocab_projection"] = vocab
+        if kern:
+            result["gemv"] = kern
+        if d1:
+            result["decode1"] = d1
+        if cpu_extra:
+            result["cpu_baseline_extra"] = cpu_extra
+        if extras:
+            result["reference_cuda"] = {"gemv": reference_cuda_gemv()}
+        if ragged:
             result["prefill"] = {"tokens": server.prefill_tokens, "seconds": server.prefill_s}
-    eng.close()
+    if eng is not None:
+        eng.close()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -179,6 +179,17 @@ int ijb_gemv(int type, const void *w_dev, const float *x_dev, float *y_dev, int 
  * on `stream`.  No counterpart in the reference. */
 int ijb_argmax_noalloc(const float *values_dev, int n, int *index_dev, void *stream);
 
+/* Exercises the engine's failure path without a fault: launches, on the
+ * engine's stream, one kernel whose bounded wait on a barrier that nothing
+ * signals gives up after limit_ns (1 us .. 100 ms), records the timeout in
+ * the engine's device status word and returns.  The call then fails the way a
+ * step whose kernel gave up a wait fails: IJB_ERR_DEVICE, with the status word
+ * cleared and the engine usable for the next step.  Every device-side wait of
+ * the library is bounded the same way (2 s in the step kernels).  No
+ * counterpart in the reference, whose device work has no waits of its own
+ * (its errors surface through cuda_check, inferencer.cu:126-128). */
+int ijb_probe_wait_timeout(ijb_engine *engine, uint64_t limit_ns);
+
 /* Number of kernels the library launched since load (for launch accounting). */
 uint64_t ijb_kernel_launches(void);
 

@@ -6,10 +6,10 @@
 // cache.  Two kernels here, both splitting a sequence's positions and keeping
 // an online-softmax state (max, sum, unnormalised output) per split, the KV
 // group's query heads sharing every K/V row loaded:
-//  * attention_stream_kernel (fp16 cache, head_dim 64): persistent, one CTA of
+//  * ijb_attention_stream_kernel (fp16 cache, head_dim 64): persistent, one CTA of
 //    streaming warps per SM, 128-position work items, tensor-core chunks; the
-//    splits are merged by attention_finish_kernel (one CTA per token);
-//  * attention_kernel (fp32 cache or head_dim 128, and beyond the streaming
+//    splits are merged by ijb_attention_finish_kernel (one CTA per token);
+//  * ijb_attention_kernel (fp32 cache or head_dim 128, and beyond the streaming
 //    kernel's limits): one CTA per (token, kv head, split of 512 positions) on
 //    CUDA cores, lanes owning positions while scoring and head-dim elements
 //    while accumulating V; the last CTA of a (token, kv head) to finish merges
@@ -88,7 +88,7 @@ __device__ __forceinline__ void loadn(const float *p, float (&f)[N]) {
 // not collide in banks), and the warp keeps an online-softmax state per query
 // head across its chunks, accumulating V with lanes owning head-dim elements.
 template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads) ijb_attention_kernel(const __grid_constant__ AttnParams p) {
     constexpr int DPL = HD / 32;  // head-dim elements per lane in the V phase
     constexpr int CH = HD / 8;    // 8-element chunks per row
     constexpr int ST = attn_stages<HD, KT>();
@@ -461,7 +461,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 // items its in-flight chunks belong to), refilling a stage as soon as it is
 // used, so a warp's copies never drain between items and no CTA waits for
 // another wave.  A finished item leaves its softmax state (max, sum,
-// unnormalised output) per head for attention_finish_kernel, or the output
+// unnormalised output) per head for ijb_attention_finish_kernel, or the output
 // itself when it covers the whole sequence.  The last CTA to finish resets the
 // item counter.
 
@@ -499,7 +499,7 @@ struct StreamItem {
 };
 
 template <int G>
-__global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_kernel(const __grid_constant__ AttnParams p) {
     constexpr int HD = 64, ST = kStreamStages, QN = kStreamQueue;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
 
@@ -738,7 +738,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) attention_stream_kernel(
 // then builds the token's fp16 activation row for it (mma_prep_token), which
 // takes the place of the projection's own prep launch.
 template <int G>
-__global__ void __launch_bounds__(256) attention_finish_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(256) ijb_attention_finish_kernel(const __grid_constant__ AttnParams p) {
     constexpr int HD = 64, KB = G >= 8 ? 4 : 8;
     pdl_trigger();
     pdl_wait();
@@ -801,12 +801,12 @@ static cudaError_t launch_attn_stream(const AttnParams &p, cudaStream_t stream, 
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attention_stream_kernel<G>, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, ijb_attention_stream_kernel<G>, p);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(p.x16 ? p.n_pad : p.batch);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&cfg, attention_finish_kernel<G>, p);
+    return cudaLaunchKernelEx(&cfg, ijb_attention_finish_kernel<G>, p);
 }
 
 typedef CUresult (*EncodeTiledFnA)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -849,7 +849,7 @@ static cudaError_t launch_attn(const AttnParams &p, dim3 grid, cudaStream_t stre
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attention_kernel<HD, G, KT>, p);
+    return cudaLaunchKernelEx(&cfg, ijb_attention_kernel<HD, G, KT>, p);
 }
 
 template <typename KT>
@@ -888,7 +888,7 @@ int attention_item_len() { return kAttnItem; }
 template <int HD, int G, typename KT>
 static cudaError_t set_attr() {
     const int smem = attn_smem<HD, KT>();
-    return cudaFuncSetAttribute(attention_kernel<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    return cudaFuncSetAttribute(ijb_attention_kernel<HD, G, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 template <typename KT>
@@ -903,10 +903,10 @@ static cudaError_t set_attrs_t() {
 
 cudaError_t attention_prepare() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(attention_stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(attention_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(attention_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)))
+    if ((e = cudaFuncSetAttribute(ijb_attention_stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)))
         return e;
     e = set_attrs_t<__half>();
     return e != cudaSuccess ? e : set_attrs_t<float>();

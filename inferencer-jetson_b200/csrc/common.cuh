@@ -18,6 +18,8 @@ constexpr uint32_t kDevErrWaitTimeout = 1u;  // a bounded mbarrier/flag wait exp
 constexpr uint32_t kDevErrBadIndex = 2u;     // an index failed its bounds check
 
 // Wall-clock limit for any device-side wait (nanoseconds, %globaltimer).
+// Every wait of the library's kernels uses it; ijb_probe_wait_timeout passes
+// a shorter one to exercise the failure path.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -64,7 +66,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Slow path of mbar_wait_bounded, kept out of line so that the many wait
 // sites of a kernel stay small in the instruction cache.
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, uint32_t *status,
-                                            volatile uint32_t *cta_abort) {
+                                                   volatile uint32_t *cta_abort, uint64_t limit_ns) {
     if (*cta_abort) return false;
     uint64_t start = 0;
     for (uint32_t n = 1;; ++n) {
@@ -74,7 +76,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parit
             const uint64_t now = global_timer_ns();
             if (start == 0) {
                 start = now;
-            } else if (now - start > kWaitLimitNs) {
+            } else if (now - start > limit_ns) {
                 *cta_abort = 1u;
                 if (status) atomicOr(status, kDevErrWaitTimeout);
                 return false;
@@ -84,15 +86,15 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parit
 }
 
 // Waits for the barrier phase with the given parity.  Gives up after
-// kWaitLimitNs: records kDevErrWaitTimeout in the launch's device status word
+// limit_ns (kWaitLimitNs unless given): records kDevErrWaitTimeout in the launch's device status word
 // and raises `cta_abort` (a flag in the CTA's shared memory, zeroed at kernel
 // start), after which every later wait of the CTA returns at once, so a CTA
 // that lost one wait ends within one time limit.  Each poll suspends the
 // thread for up to 1 ms; the clock and the flag are read every 16 polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *status,
-                                                  volatile uint32_t *cta_abort) {
+                                                  volatile uint32_t *cta_abort, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
-    return mbar_wait_slow(bar, parity, status, cta_abort);
+    return mbar_wait_slow(bar, parity, status, cta_abort, limit_ns);
 }
 
 // 1-D bulk copy global -> shared, completing on `bar` (transaction bytes).

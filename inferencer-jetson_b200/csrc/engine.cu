@@ -409,6 +409,22 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
     ++g_launches;
 }
 
+// Reads the engine's device status word after the stream has synchronised:
+// a kernel that gave up a bounded wait, or failed a bounds check, left a
+// non-zero code there.  The word is cleared and the call fails with
+// IJB_ERR_DEVICE; the engine stays usable (nothing faulted).
+void check_device_status(ijb_engine *e) {
+    uint32_t st = 0;
+    ck(cudaMemcpy(&st, e->status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
+    if (st) {
+        ck(cudaMemset(e->status, 0, sizeof(uint32_t)), "status clear");
+        std::string what;
+        if (st & kDevErrWaitTimeout) what += " (a bounded wait expired)";
+        if (st & kDevErrBadIndex) what += " (an index failed its bounds check)";
+        throw Error(IJB_ERR_DEVICE, "kernel reported device error code " + std::to_string(st) + what);
+    }
+}
+
 // Captures (once per n / need_logits) and replays the whole step: H2D of the
 // step's metadata, every kernel, D2H of the next tokens.
 void run_step(ijb_engine *e, int n, bool need_logits) {
@@ -447,12 +463,7 @@ void run_step(ijb_engine *e, int n, bool need_logits) {
     ck(cudaEventRecord(e->ev_end, e->stream), "step timer end");
     ck(cudaStreamSynchronize(e->stream), "step synchronize");
     ck(cudaEventElapsedTime(&e->last_step_ms, e->ev_start, e->ev_end), "step timer");
-    uint32_t st = 0;
-    ck(cudaMemcpy(&st, e->status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
-    if (st) {
-        cudaMemset(e->status, 0, sizeof(uint32_t));
-        throw Error(IJB_ERR_DEVICE, "kernel reported device error code " + std::to_string(st));
-    }
+    check_device_status(e);
     e->last_n = n;
 }
 
@@ -997,6 +1008,21 @@ int ijb_gemv(int type, const void *w, const float *x, float *y, int cols, int ro
         return IJB_OK;
     } catch (const std::exception &ex) {
         return fail(nullptr, ex);
+    }
+}
+
+int ijb_probe_wait_timeout(ijb_engine *e, uint64_t limit_ns) {
+    try {
+        require(e != nullptr, "null engine");
+        require(limit_ns >= 1000 && limit_ns <= 100000000ull, "limit_ns must be 1 us .. 100 ms");
+        ck(cudaSetDevice(e->d.device), "cudaSetDevice");
+        ck(wait_probe_launch(e->status, limit_ns, e->stream), "wait probe launch");
+        ++g_launches;
+        ck(cudaStreamSynchronize(e->stream), "wait probe synchronize");
+        check_device_status(e);
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
     }
 }
 

@@ -516,7 +516,7 @@ __device__ void epilogue(const GemvParams &p, const GemvSeg &s, int li, int b, f
 // ----------------------------------------------------------------- kernel --
 
 template <int B>
-__global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) ijb_gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t cta_abort;
     const SmemLayout L = smem_layout(p.cols, B, p.need_q4, p.need_q6, p.need_f);
@@ -621,8 +621,8 @@ static cudaError_t prepare_attributes() {
     int optin = 0;
     e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
-    const void *fns[4] = {(const void *)gemv_kernel<1>, (const void *)gemv_kernel<2>, (const void *)gemv_kernel<4>,
-                          (const void *)gemv_kernel<8>};
+    const void *fns[4] = {(const void *)ijb_gemv_kernel<1>, (const void *)ijb_gemv_kernel<2>, (const void *)ijb_gemv_kernel<4>,
+                          (const void *)ijb_gemv_kernel<8>};
     int limit = optin;
     for (int i = 0; i < 4; ++i) {
         cudaFuncAttributes fa;
@@ -654,7 +654,7 @@ static cudaError_t launch_b(const GemvParams &p, int grid, int smem, cudaStream_
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<B>, p);
+    return cudaLaunchKernelEx(&cfg, ijb_gemv_kernel<B>, p);
 }
 
 // Tokens the kernel instance is compiled for: the smallest of 1, 2, 4, 8

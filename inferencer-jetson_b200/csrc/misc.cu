@@ -14,7 +14,7 @@ long q6_planar_row_bytes(int cols) { return q6_unit_row_bytes(cols); }
 
 // GGUF Q6_K row (nb blocks of ql[128] qh[64] scales[16] d[2]) -> the unit
 // layout described in gemv.cuh.  Bytes are only moved.
-__global__ void repack_q6_kernel(const uint8_t *src, uint8_t *dst, int rows, int nb, long dst_row_bytes) {
+__global__ void ijb_repack_q6_kernel(const uint8_t *src, uint8_t *dst, int rows, int nb, long dst_row_bytes) {
     const long row = blockIdx.x;
     if (row >= rows) return;
     const uint8_t *s = src + row * nb * 210;
@@ -63,7 +63,7 @@ __device__ __forceinline__ float q6_planar_value(const uint8_t *row, int nb, int
 
 // embedding_cuda / embedding_batch_cuda (inferencer.cu:806-819) over the
 // planar token_embd; also clears the per-token argmax keys of the step.
-__global__ void embed_kernel(const uint8_t *emb, long row_bytes, int dim, const int *tokens, int n, float *x,
+__global__ void ijb_embed_kernel(const uint8_t *emb, long row_bytes, int dim, const int *tokens, int n, float *x,
                              long x_stride, unsigned long long *keys) {
     pdl_trigger();
     pdl_wait();
@@ -80,7 +80,7 @@ __global__ void embed_kernel(const uint8_t *emb, long row_bytes, int dim, const 
 // q4_value (inferencer.cu:454-471): d*sc*q - dmin*m.  d*sc and (d*sc)*q are
 // exact in fp32 (at most 11+6+4 significant bits), so the only rounding is
 // the final subtraction, with or without a fused multiply-add.
-__global__ void dequant_kernel(int type, const uint8_t *blocks, long nblocks, float *out) {
+__global__ void ijb_dequant_kernel(int type, const uint8_t *blocks, long nblocks, float *out) {
     const long idx = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x;
     if (idx >= nblocks * 256) return;
     const long blk = idx / 256;
@@ -117,7 +117,7 @@ __global__ void dequant_kernel(int type, const uint8_t *blocks, long nblocks, fl
 
 // Stand-alone argmax with the reference's tie rule (see argmax_key): one
 // pass of atomicMax over packed keys, then a one-thread decode.
-__global__ void argmax_keys_kernel(const float *v, int n, unsigned long long *key) {
+__global__ void ijb_argmax_keys_kernel(const float *v, int n, unsigned long long *key) {
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const unsigned long long k = argmax_key(v[i], i);
@@ -131,8 +131,12 @@ __global__ void argmax_keys_kernel(const float *v, int n, unsigned long long *ke
     if ((threadIdx.x & 31) == 0 && best) atomicMax(key, best);
 }
 
-// keys[b] -> tokens[b]; zero keys (all logits NaN) decode to -1.
-__global__ void keys_to_tokens_kernel(const unsigned long long *keys, int n, int *tokens) {
+// keys[b] -> tokens[b].  A key is zero only when no value reached it (no
+// token was scanned); such keys decode to -1.  NaN values get keys above zero
+// but below every non-NaN value, so NaN never wins against a number, and an
+// all-NaN row decodes to index 0 (the smallest rank), which is also what the
+// reference's trees return for it.
+__global__ void ijb_keys_to_tokens_kernel(const unsigned long long *keys, int n, int *tokens) {
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -154,7 +158,7 @@ static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, cudaStream_t stream,
 
 cudaError_t repack_q6_launch(const void *src, void *dst, int rows, int cols, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    repack_q6_kernel<<<rows, 256, 0, stream>>>(static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst), rows,
+    ijb_repack_q6_kernel<<<rows, 256, 0, stream>>>(static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst), rows,
                                                cols / 256, q6_planar_row_bytes(cols));
     return cudaGetLastError();
 }
@@ -163,13 +167,13 @@ cudaError_t embed_launch(const uint8_t *emb, long row_bytes, int dim, const int 
                          long x_stride, unsigned long long *keys, cudaStream_t stream, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_config(dim3((dim + 255) / 256, n), dim3(256), stream, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, embed_kernel, emb, row_bytes, dim, tokens, n, x, x_stride, keys);
+    return cudaLaunchKernelEx(&cfg, ijb_embed_kernel, emb, row_bytes, dim, tokens, n, x, x_stride, keys);
 }
 
 cudaError_t dequant_launch(int type, const void *blocks, long nblocks, float *out, cudaStream_t stream) {
     const long total = nblocks * 256;
     if (total <= 0) return cudaSuccess;
-    dequant_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+    ijb_dequant_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
         type, static_cast<const uint8_t *>(blocks), nblocks, out);
     return cudaGetLastError();
 }
@@ -179,8 +183,27 @@ cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch
     if (e != cudaSuccess) return e;
     int blocks = (n + 255) / 256;
     if (blocks > 1024) blocks = 1024;
-    argmax_keys_kernel<<<blocks, 256, 0, stream>>>(v, n, key_scratch);
-    keys_to_tokens_kernel<<<1, 32, 0, stream>>>(key_scratch, 1, index);
+    ijb_argmax_keys_kernel<<<blocks, 256, 0, stream>>>(v, n, key_scratch);
+    ijb_keys_to_tokens_kernel<<<1, 32, 0, stream>>>(key_scratch, 1, index);
+    return cudaGetLastError();
+}
+
+// Failure-path probe: one thread waits on a shared-memory barrier that
+// nothing signals, with the given limit, so the wait expires, records
+// kDevErrWaitTimeout in *status and returns; nothing faults or hangs.
+__global__ void ijb_wait_probe_kernel(uint32_t *status, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ uint32_t abort_flag;
+    if (threadIdx.x == 0) {
+        abort_flag = 0u;
+        mbar_init(&bar, 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait_bounded(&bar, 0, status, &abort_flag, limit_ns);
+}
+
+cudaError_t wait_probe_launch(uint32_t *status, uint64_t limit_ns, cudaStream_t stream) {
+    ijb_wait_probe_kernel<<<1, 32, 0, stream>>>(status, limit_ns);
     return cudaGetLastError();
 }
 
@@ -188,7 +211,7 @@ cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *to
                                   bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_config(dim3((n + 127) / 128), dim3(128), stream, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, keys_to_tokens_kernel, keys, n, tokens);
+    return cudaLaunchKernelEx(&cfg, ijb_keys_to_tokens_kernel, keys, n, tokens);
 }
 
 // ------------------------------------------- argmax without allocation --
@@ -208,7 +231,7 @@ constexpr int kNoAllocArgmaxSlots = 512;  // 512 winners x 256 values = the refe
 static __device__ __align__(256) unsigned long long g_argmax_slots[kNoAllocArgmaxSlots];
 
 // Pass 1: CTA b writes the best packed key of values [256b, 256b + 256).
-__global__ void argmax_slots_kernel(const float *v, int n, unsigned long long *slots) {
+__global__ void ijb_argmax_slots_kernel(const float *v, int n, unsigned long long *slots) {
     __shared__ unsigned long long warp_best[8];
     const int i = blockIdx.x * 256 + threadIdx.x;
     unsigned long long best = i < n ? argmax_key(v[i], i) : 0ull;
@@ -226,9 +249,10 @@ __global__ void argmax_slots_kernel(const float *v, int n, unsigned long long *s
     }
 }
 
-// Pass 2: one CTA reduces the winners and writes the index (-1 if every
-// value was NaN).
-__global__ void argmax_slots_final_kernel(const unsigned long long *slots, int nslots, int *index) {
+// Pass 2: one CTA reduces the winners and writes the index.  NaN values lose
+// to every number; an all-NaN input gives index 0, as the reference's trees
+// do (every key is non-zero for n >= 1, so the -1 branch is never taken).
+__global__ void ijb_argmax_slots_final_kernel(const unsigned long long *slots, int nslots, int *index) {
     __shared__ unsigned long long warp_best[kNoAllocArgmaxSlots / 32];
     unsigned long long best = static_cast<int>(threadIdx.x) < nslots ? slots[threadIdx.x] : 0ull;
 #pragma unroll
@@ -286,8 +310,8 @@ extern "C" int ijb_argmax_noalloc(const float *values_dev, int n, int *index_dev
     if (e == cudaSuccess) {
         const int nslots = (n + 255) / 256;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        argmax_slots_kernel<<<nslots, 256, 0, s>>>(values_dev, n, slots);
-        argmax_slots_final_kernel<<<1, kNoAllocArgmaxSlots, 0, s>>>(slots, nslots, index_dev);
+        ijb_argmax_slots_kernel<<<nslots, 256, 0, s>>>(values_dev, n, slots);
+        ijb_argmax_slots_final_kernel<<<1, kNoAllocArgmaxSlots, 0, s>>>(slots, nslots, index_dev);
         e = cudaGetLastError();
         count_launches(2);
     }

@@ -18,6 +18,10 @@ cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch
 void set_thread_error(const std::string &msg);
 void count_launches(uint64_t n);
 
+// One kernel whose bounded wait (limit_ns) on a barrier that nothing signals
+// expires and records kDevErrWaitTimeout in *status.
+cudaError_t wait_probe_launch(uint32_t *status, uint64_t limit_ns, cudaStream_t stream);
+
 cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *tokens, cudaStream_t stream, bool pdl);
 
 }  // namespace ijb

@@ -299,7 +299,7 @@ __device__ __forceinline__ int tile_row(const MmaSeg &s, int lt, int r, bool &va
 // For Q4_K these are the low nibbles (sub-block 2g) and high nibbles
 // (sub-block 2g+1) of the 32-bit word j of the group's 32 bytes, so a mask
 // of 0x000F000F / 0x00F000F0 on the word and on the word >> 8 yields the four
-// fp16 pairs.  mma_prep_kernel writes the activation in the same order.
+// fp16 pairs.  ijb_mma_prep_kernel writes the activation in the same order.
 
 // Q4_K group g of a raw block column -> fp16 stage.  The weight is
 // (d*sc)*q - dmin*m as in q4_value (inferencer.cu:454-471), with the scale
@@ -564,7 +564,7 @@ __device__ void epi_argmax(const float *stage, const EpiTok &tk, int row_base, i
 
 // ----------------------------------------------------------------- kernel --
 
-__global__ void __launch_bounds__(kMmaThreads, 1) mma_gemm_kernel(const __grid_constant__ MmaParams p) {
+__global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __grid_constant__ MmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr MmaSmem L = mma_smem();
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
@@ -1024,7 +1024,7 @@ __device__ void mma_prep_token(const float *x, long x_stride, const float *norm_
     if (tid == 0) x_inv[n] = ldexpf(1.0f, -kx);
 }
 
-__global__ void __launch_bounds__(256) mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
+__global__ void __launch_bounds__(256) ijb_mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
                                                        int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
                                                        float *x_inv) {
     pdl_trigger();
@@ -1035,7 +1035,7 @@ __global__ void __launch_bounds__(256) mma_prep_kernel(const float *x, long x_st
 // Bound of max|w| over GGUF blocks: Q4_K |d|*63*15 + |dmin|*63, Q6_K
 // |d|*128*32; atomicMax on the float's bits (non-negative floats order as
 // integers).
-__global__ void mma_scale_scan_kernel(int type, const uint8_t *w, long nblocks, unsigned int *out) {
+__global__ void ijb_mma_scale_scan_kernel(int type, const uint8_t *w, long nblocks, unsigned int *out) {
     float best = 0.f;
     for (long b = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; b < nblocks;
          b += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -1049,7 +1049,8 @@ __global__ void mma_scale_scan_kernel(int type, const uint8_t *w, long nblocks, 
             const uint8_t *bp = w + b * 210;
             bound = fabsf(half_bits_to_float(*reinterpret_cast<const uint16_t *>(bp + 208))) * 4096.f;
         }
-        if (!(bound <= 3.0e38f)) bound = 3.0e38f;  // inf / NaN scales
+        if (bound != bound) bound = 0.f;                // a NaN scale makes only its own block NaN
+        else if (!(bound <= 3.0e38f)) bound = 3.0e38f;  // inf scales
         best = fmaxf(best, bound);
     }
     best = warp_max(best);
@@ -1070,13 +1071,13 @@ cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, 
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, mma_prep_kernel, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a, x16, x_inv);
+    return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a, x16, x_inv);
 }
 
 cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks, int *out_max_bits, cudaStream_t stream) {
     cudaError_t e = cudaMemsetAsync(out_max_bits, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
-    mma_scale_scan_kernel<<<256, 256, 0, stream>>>(type, w, nblocks, reinterpret_cast<unsigned int *>(out_max_bits));
+    ijb_mma_scale_scan_kernel<<<256, 256, 0, stream>>>(type, w, nblocks, reinterpret_cast<unsigned int *>(out_max_bits));
     return cudaGetLastError();
 }
 
@@ -1088,7 +1089,7 @@ long mma_tile_bytes(int type, int rows, int cols) {
 }
 
 // One CTA per (row group, block column), one thread per row of the group.
-__global__ void mma_tile_repack_kernel(int type, const uint8_t *src, long row_bytes, int rows, int nb, uint8_t *dst) {
+__global__ void ijb_mma_tile_repack_kernel(int type, const uint8_t *src, long row_bytes, int rows, int nb, uint8_t *dst) {
     const long g = blockIdx.x / nb;
     const int b = blockIdx.x % nb, i = threadIdx.x;
     const long row = g * kMmaRowGroup + i;
@@ -1116,7 +1117,7 @@ cudaError_t mma_tile_repack_launch(int type, const uint8_t *src, long row_bytes,
         return cudaErrorInvalidValue;
     const int nb = cols / 256;
     const long groups = mma_tile_bytes(type, rows, cols) / (static_cast<long>(nb) * (type == kQ4K ? kMmaChunkQ4 : kMmaChunkQ6));
-    mma_tile_repack_kernel<<<static_cast<unsigned>(groups * nb), kMmaRowGroup, 0, stream>>>(type, src, row_bytes, rows,
+    ijb_mma_tile_repack_kernel<<<static_cast<unsigned>(groups * nb), kMmaRowGroup, 0, stream>>>(type, src, row_bytes, rows,
                                                                                             nb, dst);
     return cudaGetLastError();
 }
@@ -1127,7 +1128,7 @@ static std::mutex g_cap_mu;
 
 cudaError_t mma_prepare() {
     cudaError_t e =
-        cudaFuncSetAttribute(mma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem().total);
+        cudaFuncSetAttribute(ijb_mma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem().total);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(g_cap_mu);
     int dev = 0, sms = 0;
@@ -1148,7 +1149,7 @@ cudaError_t mma_prepare() {
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, mma_gemm_kernel, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxActiveClusters(&n, ijb_mma_gemm_kernel, &cfg) != cudaSuccess) {
             cudaGetLastError();
             n = 0;
         }
@@ -1197,7 +1198,7 @@ cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, mma_gemm_kernel, p);
+    return cudaLaunchKernelEx(&cfg, ijb_mma_gemm_kernel, p);
 }
 
 }  // namespace ijb

@@ -47,7 +47,12 @@ class Engine:
             v = views[i]
             v.name = name.encode()
             v.data_dev = t.data_ptr()
-            if name in shapes:
+            if name == "output.weight" and name not in shapes:
+                # an untied lm_head: [vocab][row_bytes] Q4_K or Q6_K blocks
+                per_block = arr.shape[1] // (cfg.dim // 256)
+                v.type, v.n_dims = {144: 12, 210: 14}[per_block], 2
+                v.dims[0], v.dims[1] = cfg.dim, cfg.vocab
+            elif name in shapes:
                 qt, rows, cols = shapes[name]
                 v.type, v.n_dims = qt, 2
                 v.dims[0], v.dims[1] = cols, rows
@@ -129,6 +134,13 @@ class Engine:
         out = (ctypes.c_int * n)()
         _L.check(self.lib.ijb_decode_step(self.h, n, s, t, out), self.h)
         return np.frombuffer(out, dtype=np.int32).copy()
+
+    def probe_wait_timeout(self, limit_ns: int) -> int:
+        """ijb_probe_wait_timeout: the status code of a step whose bounded wait expired."""
+        return int(self.lib.ijb_probe_wait_timeout(self.h, int(limit_ns)))
+
+    def last_error(self) -> str:
+        return self.lib.ijb_last_error(self.h).decode()
 
     def last_step_ms(self) -> float:
         """Device time of the last step (CUDA events on the engine's stream)."""

@@ -76,6 +76,7 @@ def load():
         "ijb_q6k_planar_row_bytes": ([I], L64),
         "ijb_repack_q6k": ([P, P, I, I, P], I),
         "ijb_gemv": ([I, P, P, P, I, I, I, I, P], I),
+        "ijb_probe_wait_timeout": ([P, ctypes.c_uint64], I),
         "ijb_kernel_launches": ([], ctypes.c_uint64),
         "ijb_last_step_ms": ([P], ctypes.c_float),
     }

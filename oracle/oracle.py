@@ -71,6 +71,10 @@ def lib():
         L.orc_state_fill_kv.argtypes = [P, i32]
         L.orc_forward.argtypes = [P, i32, i32, i32, P]
         L.orc_forward.restype = i32
+        L.orc_matvec_multi.argtypes = [i32, P, P, P, i32, i64, i32, i32, i32, i32]
+        L.orc_matvec_multi.restype = i32
+        L.orc_forward_multi.argtypes = [P, P, P, i32, i32, P, P]
+        L.orc_forward_multi.restype = i32
         _lib = L
     return _lib
 
@@ -127,6 +131,18 @@ def matvec(qtype, w, x, cols, rows, use_dp4a=True, use_q6_dp4a=True, contract=1)
     x = np.ascontiguousarray(x, dtype=np.float32)
     y = np.empty(rows, dtype=np.float32)
     rc = lib().orc_matvec(qtype, _p(w), _p(x), _p(y), cols, rows, int(use_dp4a), int(use_q6_dp4a), contract)
+    assert rc == 0
+    return y
+
+
+def matvec_multi(qtype, w, xs, cols, rows, use_dp4a=True, use_q6_dp4a=True, contract=1):
+    """matvec over each row of xs [n][cols] -> [n][rows], decoding each weight
+    block once for all vectors (every output equals matvec's for its vector)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    xs = np.ascontiguousarray(xs, dtype=np.float32).reshape(-1, cols)
+    y = np.empty((xs.shape[0], rows), dtype=np.float32)
+    rc = lib().orc_matvec_multi(qtype, _p(w), _p(xs), _p(y), cols, rows, xs.shape[0], int(use_dp4a),
+                                int(use_q6_dp4a), contract)
     assert rc == 0
     return y
 
@@ -218,6 +234,35 @@ class OracleModel:
 
     def new_state(self):
         return OracleState(self)
+
+    def forward_multi(self, states, tokens, positions, need_logits=True, want_logits=False):
+        """One packed step: entry i feeds tokens[i] at positions[i] to states[i]
+        (entries may repeat a state at consecutive positions, in order).  Same
+        per-token arithmetic as OracleState.forward, layer by layer over all
+        entries.  Returns the argmax per entry (-1 without logits) and, with
+        want_logits, the [n][vocab] logits."""
+        n = len(states)
+        arr = (ctypes.c_void_p * n)(*[s._s for s in states])
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        nxt = np.empty(n, dtype=np.int32)
+        lg = np.empty((n, self.cfg.vocab), dtype=np.float32) if (need_logits and want_logits) else None
+        r = lib().orc_forward_multi(arr, _p(tok), _p(pos), n, int(need_logits),
+                                    _p(lg) if lg is not None else None, _p(nxt))
+        if r == -2:
+            raise ValueError("Token or position outside model context")
+        return (nxt, lg) if want_logits else nxt
+
+    def prefill(self, state, tokens, start=0, chunk=64):
+        """Feeds tokens at positions start.. through forward_multi in chunks;
+        returns the argmax after the last token."""
+        nxt = -1
+        for c in range(0, len(tokens), chunk):
+            part = tokens[c:c + chunk]
+            last = c + len(part) == len(tokens)
+            out = self.forward_multi([state] * len(part), part, np.arange(start + c, start + c + len(part)), last)
+            nxt = int(out[-1])
+        return nxt
 
     def __del__(self):
         try:

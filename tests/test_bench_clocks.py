@@ -38,3 +38,42 @@ def test_missing_sampler_gives_empty_record():
     s.mark_end()
     rec = s.stop()
     assert rec["samples"] == 0 and rec["sm_mhz"] is None and rec["reasons"] == []
+
+
+def test_nvml_sampler_with_a_fake_nvml(monkeypatch):
+    """The NVML sampler reads (never sets) the SM clock and the clock-event
+    reason bits, finds the GPU by PCI bus id and keeps only in-region samples."""
+    import types
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=1, nvmlInit=lambda: None,
+        nvmlDeviceGetHandleByPciBusId=lambda bus: ("h", bus),
+        nvmlDeviceGetMaxClockInfo=lambda h, c: 1965,
+        nvmlDeviceGetClockInfo=lambda h, c: 1900,
+        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x4 | 0x1)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+
+    class Props:
+        pci_bus_id, pci_device_id, pci_domain_id = 0x1b, 0, 0
+
+    import torch
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda i: Props())
+    s = bench.NvmlClockSampler(0, interval_ms=2)
+    assert s.h == ("h", "00000000:1b:00.0")
+    s.start()
+    s.wait_first()
+    time.sleep(0.02)
+    s.mark_start()
+    time.sleep(0.05)
+    s.mark_end()
+    rec = s.stop()
+    assert rec["samples"] >= 5 and rec["sm_mhz"] == 1900.0 and rec["sm_max_mhz"] == 1965.0
+    assert rec["reasons"] == ["sw_power_cap"] and rec["source"] == "nvml"
+
+
+def test_profile_figures_are_read_from_summaries(tmp_path, monkeypatch):
+    p = tmp_path / "k.md"
+    p.write_text("# kernel\n- dram_bytes_per_launch: 224301824\n- other: 1\n")
+    monkeypatch.setattr(bench, "PROFILES", str(tmp_path))
+    assert bench.profile_figure("k.md", "dram_bytes_per_launch") == 224301824
+    assert bench.profile_figure("k.md", "missing") is None
+    assert bench.profile_figure("absent.md", "x") is None

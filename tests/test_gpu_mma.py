@@ -4,12 +4,14 @@ Weights are dequantised exactly (the reference's q4_value / q6_value) and
 rounded once to fp16 with a per-matrix power-of-two scale; activations are
 the reference's int8-dequantised values (INT8 path) or the fp32 values (FP32
 path) rounded once to fp16 with a per-token power-of-two scale; products
-accumulate in fp32.  Per projection that is within rel-L2 2e-3 of the oracle
-(typically ~3e-4).  Whole-model logits: the FP32 activation path is held to
-1e-2; in the INT8 path the fp16 roundings are amplified by the per-32 int8
-requantisation at every projection (the path's own floor is ~1%, see
-test_oracle.py::test_dp4a_path_noise_floor), so it is held to max 3e-2 and
-mean 2e-2 over the steps, with the same greedy-agreement bar."""
+accumulate in fp32.  Per projection that is within rel-L2 1e-3 of the oracle
+(~5e-4 at worst, ~3e-4 typically).  Whole-model logits: the FP32 activation
+path is held to 1e-2 with >= 99% greedy agreement; in the INT8 path every
+rounding difference is amplified by the per-32 int8 requantisation at the
+next projection, so the test measures the path's own floor (two oracle
+variants differing in one multiply-add contraction) on the same sequences and
+holds the GPU to twice it, with the same greedy bar.  The same checks at the
+1B widths and 64 sequences are in test_gpu_headline.py."""
 import numpy as np
 import pytest
 
@@ -19,7 +21,7 @@ from ijb200.engine import Engine
 
 pytestmark = pytest.mark.gpu
 
-PROJ_BAR = 2e-3
+PROJ_BAR = 1e-3
 
 
 def rel_l2(a, b):
@@ -98,8 +100,8 @@ def test_baseline_config_shapes_tensor_core(cuda):
     eng.close()
 
 
-@pytest.mark.parametrize("dp4a,bar,mean_bar", [(False, 1e-2, 1e-2), (True, 3e-2, 2e-2)])
-def test_ragged_step_tensor_core_vs_oracle(cuda, dp4a, bar, mean_bar):
+@pytest.mark.parametrize("dp4a", [False, True], ids=["fp32-path", "int8-path"])
+def test_ragged_step_tensor_core_vs_oracle(cuda, dp4a):
     """20 sequences decoded together (the tensor-core path) against the
     oracle run per sequence, teacher-forced; the oracle keeps fp16 K/V like
     the engine."""
@@ -108,28 +110,36 @@ def test_ragged_step_tensor_core_vs_oracle(cuda, dp4a, bar, mean_bar):
     reqs = synth.ragged_requests(20, prompt_range=(3, 60), output_range=(4, 8), seed=9, vocab_limit=cfg.vocab)
     eng = Engine(cfg, weights, context=128, max_batch=64, max_seqs=24, use_dp4a=dp4a, use_q6_dp4a=dp4a)
     om = O.OracleModel(cfg, weights, 128, dp4a, dp4a, kv_fp16=True)
+    alt = O.OracleModel(cfg, weights, 128, dp4a, dp4a, contract=0, kv_fp16=True)  # the INT8 floor
     O.set_threads(8)
     states = [om.new_state() for _ in reqs]
+    alts = [alt.new_state() for _ in reqs]
     seqs = [eng.seq_open() for _ in reqs]
     cur = []
-    for s, st, r in zip(seqs, states, reqs):
+    for s, st, sa, r in zip(seqs, states, alts, reqs):
         eng.seq_prefill(s, r.prompt)
-        for i, t in enumerate(r.prompt):
-            nt = st.forward(int(t), i, i + 1 == len(r.prompt))
-        cur.append(nt)
-    errs, agree, total = [], 0, 0
-    for step in range(5):
+        cur.append(om.prefill(st, r.prompt))
+        alt.prefill(sa, r.prompt)
+    errs, floor, agree, total = [], [], 0, 0
+    for step in range(10):
         out = eng.decode_step(seqs, cur)
         lg = eng.logits(len(seqs))
-        nxt = []
-        for i, (st, r) in enumerate(zip(states, reqs)):
-            want = st.forward(int(cur[i]), len(r.prompt) + step, True)
-            errs.append(rel_l2(lg[i], st.logits()))
-            agree += int(out[i] == want)
+        pos = [len(r.prompt) + step for r in reqs]
+        want, ref = om.forward_multi(states, cur, pos, True, want_logits=True)
+        _, ref_alt = alt.forward_multi(alts, cur, pos, True, want_logits=True)
+        for i in range(len(reqs)):
+            errs.append(rel_l2(lg[i], ref[i]))
+            floor.append(rel_l2(ref_alt[i], ref[i]))
+            agree += int(out[i] == want[i])
             total += 1
-            nxt.append(want)  # teacher-forced
-        cur = nxt
+        cur = [int(t) for t in want]  # teacher-forced
     eng.close()
-    assert max(errs) < bar, max(errs)
-    assert float(np.mean(errs)) < mean_bar, float(np.mean(errs))
-    assert agree / total >= 0.95, agree / total
+    errs, floor = np.array(errs), np.array(floor)
+    print(f"\nlogits rel-L2 max {errs.max():.3e} mean {errs.mean():.3e}; floor max {floor.max():.3e} "
+          f"mean {floor.mean():.3e}; greedy {agree / total:.3f}")
+    if dp4a:
+        assert errs.max() <= 2 * floor.max(), (errs.max(), floor.max())
+        assert errs.mean() <= 2 * floor.mean(), (errs.mean(), floor.mean())
+    else:
+        assert errs.max() <= 1e-2, errs.max()
+    assert agree / total >= 0.99, agree / total

@@ -216,3 +216,45 @@ def test_oracle_argmax_nan_semantics_follow_the_reference_trees(nan_at):
     v = np.random.default_rng(len(nan_at)).standard_normal(3000).astype(np.float32)
     v[nan_at] = np.nan
     assert O.argmax(v) == _reference_trees(v)
+
+
+@pytest.mark.parametrize("dp4a", [True, False], ids=["int8", "fp32"])
+@pytest.mark.parametrize("contract", [1, 0])
+def test_packed_forward_is_bit_identical_to_token_by_token(dp4a, contract):
+    """orc_forward_multi (layer by layer over many entries, weights decoded once
+    per block for all of them) gives exactly orc_forward's results: chunked
+    prefills of several sequences, then packed decode steps over all of them."""
+    cfg = synth.TINY
+    w = synth.make_model(cfg, seed=4)
+    O.set_threads(4)
+    m = O.OracleModel(cfg, w, 128, dp4a, dp4a, contract=contract, kv_fp16=True)
+    reqs = synth.ragged_requests(5, prompt_range=(3, 40), output_range=(4, 8), seed=2, vocab_limit=cfg.vocab)
+    a = [m.new_state() for _ in reqs]
+    b = [m.new_state() for _ in reqs]
+    na, nb = [], []
+    for sa, sb, r in zip(a, b, reqs):
+        for i, t in enumerate(r.prompt):
+            x = sa.forward(int(t), i, i + 1 == len(r.prompt))
+        na.append(x)
+        nb.append(m.prefill(sb, r.prompt, chunk=7))
+    assert na == nb
+    cur = na
+    for step in range(4):
+        want = [sa.forward(int(t), len(r.prompt) + step, True) for sa, t, r in zip(a, cur, reqs)]
+        la = np.stack([s.logits() for s in a])
+        got, lb = m.forward_multi(b, cur, [len(r.prompt) + step for r in reqs], True, want_logits=True)
+        assert list(got) == want
+        assert np.array_equal(la, lb)
+        cur = want
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(12, 300, 512), (14, 200, 1024)])
+def test_multi_vector_matvec_equals_matvec(qt, rows, cols):
+    rng = np.random.default_rng(0)
+    W = synth.quant_matrix(rng, qt, rows, cols)
+    xs = rng.standard_normal((9, cols)).astype(np.float32)
+    for dp in (True, False):
+        for c in (0, 1):
+            y = O.matvec_multi(qt, W, xs, cols, rows, dp, dp, c)
+            for i in range(9):
+                assert np.array_equal(y[i], O.matvec(qt, W, xs[i], cols, rows, dp, dp, c))
