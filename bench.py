@@ -527,6 +527,55 @@ def reference_cuda_gemv(cases=GEMV_CASES):
     return out
 
 
+def decode_3b_b1(local, prompt_len=128, steps=64, scratch="/tmp"):
+    """The only full-model configuration the reference's runner accepts
+    (Llama-3.2-3B shape, inferencer.cu:1215-1217), batch 1, on this GPU: the
+    reference's own GGUF + FastRunner (unmodified, built into oracle/_ref/;
+    steady decode as in its main loop, inferencer.cu:1870-1883: each
+    forward() ends in its blocking token download) and this build's engine on
+    the same seeded weights, prompt and step count.  Tokens/s over the decode
+    steps; the reference's number is wall time (its own measure), the
+    engine's is given both ways."""
+    out = {"config": f"llama-3.2-3b-shape Q4_K_M random-init, batch 1, {prompt_len}-token prompt, {steps} steps"}
+    cfg = synth.LLAMA_3B
+    weights = synth.make_model(cfg, seed=7)
+    prompt = synth.prompt_tokens(prompt_len, seed=5)
+    if os.path.exists(REF_HARNESS):
+        try:
+            import gguf_writer
+            path = os.path.join(scratch, "bench_llama3b_seed7.gguf")
+            gguf_writer.write_gguf(path, cfg, weights)
+            L = ctypes.CDLL(REF_HARNESS)
+            L.ref_last_error.restype = ctypes.c_char_p
+            L.ref_time_decode.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+            secs = ctypes.c_double()
+            p32 = np.ascontiguousarray(prompt, dtype=np.int32)
+            rc = L.ref_time_decode(path.encode(), prompt_len + steps + 8, p32.ctypes.data, prompt_len, steps, 0,
+                                   ctypes.byref(secs))
+            os.remove(path)
+            out["reference"] = ({"tokens_per_s": steps / secs.value, "ms_per_token": secs.value / steps * 1e3,
+                                 "timing": "wall, blocking token download per step"} if rc == 0
+                                else {"error": L.ref_last_error().decode()})
+        except Exception as ex:  # reported, not fatal
+            out["reference"] = {"error": repr(ex)}
+    else:
+        out["reference"] = {"unavailable": "oracle/_ref/libref_harness.so not built"}
+    from ijb200.engine import Engine
+    eng = Engine(cfg, weights, context=prompt_len + steps + 8, max_batch=1, max_seqs=2, device=local)
+    nxt = eng.prefill(prompt)
+    dev_ms, wall = 0.0, 0.0
+    for i in range(steps):
+        t0 = time.perf_counter()
+        nxt = eng.forward(nxt, prompt_len + i, True)
+        wall += time.perf_counter() - t0
+        dev_ms += eng.last_step_ms()
+    eng.close()
+    out["ours"] = {"tokens_per_s_device": steps / (dev_ms / 1e3), "tokens_per_s_wall": steps / wall,
+                   "ms_per_token_device": dev_ms / steps}
+    return out
+
+
 def cpu_forward(cfg, weights, contexts, threads, budget_s=20.0):
     """The oracle's FastRunner::forward on the host cores: decode one token at
     each sampled context length; returns tokens/s and the sample used."""
@@ -799,6 +848,10 @@ def run_ours(args):
             result["cpu_baseline_extra"] = cpu_extra
         if extras:
             result["reference_cuda"] = {"gemv": reference_cuda_gemv()}
+            try:
+                result["reference_cuda"]["decode_3b_b1"] = decode_3b_b1(local)
+            except Exception as ex:  # reported, not fatal
+                result["reference_cuda"]["decode_3b_b1"] = {"error": repr(ex)}
         if ragged:
             result["prefill"] = {"tokens": server.prefill_tokens, "seconds": server.prefill_s}
     if eng is not None:

@@ -114,6 +114,30 @@ int ijb_forward(ijb_engine *engine, int token, int pos, int need_logits, int *ne
  * after the last one.  Drop-in for FastRunner::prefill (inferencer.cu:1279-1423). */
 int ijb_prefill(ijb_engine *engine, const int *tokens, int n, int *next_token);
 
+/* FastRunner::forward with its debug traces (inferencer.cu:1424-1426): as
+ * ijb_forward; when non-NULL, layer_trace [layers][dim] receives the residual
+ * stream after every layer, and quant_trace [layers][3*dim + hidden] the int8
+ * activations the reference's INT8 path quantises in each layer (the
+ * attention input, the attention output, the feed-forward input, the
+ * down-projection input), computed with the reference's RMSNorm and per-32
+ * quantiser.  Slower than ijb_forward (a separate step graph with trace
+ * copies). */
+int ijb_forward_traced(ijb_engine *engine, int token, int pos, int need_logits, int *next_token, float *layer_trace,
+                       int8_t *quant_trace);
+
+/* FastRunner::prefill with its debug traces (inferencer.cu:1279-1283): as
+ * ijb_prefill; all_layer_trace [n][layers][dim] receives every token's
+ * residual after every layer, first_quant_trace / last_quant_trace
+ * [layers][3*dim + hidden] the first and last token's quantised activations.
+ * Any trace pointer may be NULL. */
+int ijb_prefill_traced(ijb_engine *engine, const int *tokens, int n, int *next_token, float *all_layer_trace,
+                       int8_t *first_quant_trace, int8_t *last_quant_trace);
+
+/* Entries in the last step run (1 after ijb_forward; the last chunk's size
+ * after a prefill): row (size - 1) of ijb_logits_dev / ijb_residual_dev is the
+ * last token's, which FastGPU::logits / FastGPU::x hold in the reference. */
+int ijb_last_step_size(const ijb_engine *engine);
+
 /* Forgets sequence 0's cached positions (FastRunner::reset, inferencer.cu:1264). */
 int ijb_reset(ijb_engine *engine);
 

@@ -125,7 +125,13 @@ struct ijb_engine {
     uint32_t *status = nullptr;
     unsigned long long *scratch_key = nullptr;
 
-    std::unordered_map<int, StepGraph> graphs;  // key: n * 2 + need_logits
+    std::unordered_map<int, StepGraph> graphs;  // key: (n * 2 + need_logits) * 2 + traced
+    // debug traces of traced steps (allocated on first use): the residual after
+    // every layer [max_batch][layers][dim] and the four int8 activations the
+    // INT8 path quantises per layer [max_batch][layers][trace_q_stride]
+    float *trace_x = nullptr;
+    int8_t *trace_q = nullptr;
+    long trace_q_stride = 0;
     cudaEvent_t ev_start = nullptr, ev_end = nullptr;
     bool pdl = false;      // programmatic dependent launch between the step's kernels
     bool mma_pdl = true;   // the same for the tensor-core path's prep and GEMM launches
@@ -322,7 +328,15 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
 }
 
 // Every kernel of one packed step over n tokens (meta already on the device).
-void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
+void enqueue_trace_quant(ijb_engine *e, int n, const float *x, long x_stride, const float *norm_w, int cols, int l,
+                         long offset, cudaStream_t s) {
+    const long row = static_cast<long>(e->d.layers) * e->trace_q_stride;
+    ck(trace_quant_launch(x, x_stride, norm_w, e->d.eps, cols, n, e->trace_q + l * e->trace_q_stride + offset, row, s),
+       "trace launch");
+    ++g_launches;
+}
+
+void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool traced = false) {
     const ijb_model_desc &d = e->d;
     const int *tok = e->meta_dev;
     const int *tseq = e->meta_dev + d.max_batch;
@@ -335,6 +349,9 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
     for (int l = 0; l < d.layers; ++l) {
         const auto &L = e->layers[l];
         char *kbase = static_cast<char *>(e->kv) + l * layer_pool * e->kv_elem;
+        if (traced)
+            enqueue_trace_quant(e, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), d.dim, l, 0,
+                                s);
         {
             const ProjSeg segs[3] = {{L.q, -1, kEpiRopeQ, e->q, d.dim},
                                      {L.k, -1, kEpiRopeKCache, nullptr, 0},
@@ -388,16 +405,26 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s) {
         // tensor-core steps chain their launches with programmatic dependent launch
         ck(attention_launch(a, s, e->pdl || (n >= e->mma_min_batch && e->attn_pdl)), "attention launch");
         g_launches += attention_kernels(a);
-        launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, o_segs, 1, nullptr, 0, o_fused);
+        if (traced) enqueue_trace_quant(e, n, e->attn, d.dim, nullptr, d.dim, l, d.dim, s);
+        launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, o_segs, 1, nullptr, 0, o_fused && !traced);
+        if (traced)
+            enqueue_trace_quant(e, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), d.dim, l,
+                                2L * d.dim, s);
         {
             const ProjSeg segs[1] = {{L.gate, L.up, kEpiSiluPair, e->h, d.hidden}};
             launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), segs,
                               1, nullptr, 0);
         }
+        if (traced) enqueue_trace_quant(e, n, e->h, d.hidden, nullptr, d.hidden, l, 3L * d.dim, s);
         {
             const ProjSeg segs[1] = {{L.down, -1, kEpiAdd, e->x, d.dim}};
             launch_projection(e, s, 0, n, e->h, d.hidden, nullptr, segs, 1, nullptr, 0);
         }
+        if (traced)  // residual after the layer -> trace_x[token][l]
+            ck(cudaMemcpy2DAsync(e->trace_x + static_cast<long>(l) * d.dim, static_cast<size_t>(d.layers) * d.dim * 4,
+                                 e->x, static_cast<size_t>(d.dim) * 4, static_cast<size_t>(d.dim) * 4, n,
+                                 cudaMemcpyDeviceToDevice, s),
+               "layer trace copy");
     }
     if (!need_logits) return;
     {
@@ -427,8 +454,8 @@ void check_device_status(ijb_engine *e) {
 
 // Captures (once per n / need_logits) and replays the whole step: H2D of the
 // step's metadata, every kernel, D2H of the next tokens.
-void run_step(ijb_engine *e, int n, bool need_logits) {
-    const int key = n * 2 + (need_logits ? 1 : 0);
+void run_step(ijb_engine *e, int n, bool need_logits, bool traced = false) {
+    const int key = (n * 2 + (need_logits ? 1 : 0)) * 2 + (traced ? 1 : 0);
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         cudaGraph_t graph;
@@ -438,7 +465,7 @@ void run_step(ijb_engine *e, int n, bool need_logits) {
             ck(cudaMemcpyAsync(e->meta_dev, e->meta_host, 4 * e->d.max_batch * sizeof(int), cudaMemcpyHostToDevice,
                                e->stream),
                "meta H2D");
-            enqueue_step(e, n, need_logits, e->stream);
+            enqueue_step(e, n, need_logits, e->stream, traced);
             if (need_logits)
                 ck(cudaMemcpyAsync(e->next_host, e->next_dev, n * sizeof(int), cudaMemcpyDeviceToHost, e->stream),
                    "next D2H");
@@ -489,7 +516,8 @@ int slot_for(ijb_engine *e, int seq, int pos) {
 }
 
 // Fills meta for entries (seq, token) at explicit positions and runs a step.
-void packed_step(ijb_engine *e, int n, const int *seqs, const int *tokens, const int *positions, bool need_logits) {
+void packed_step(ijb_engine *e, int n, const int *seqs, const int *tokens, const int *positions, bool need_logits,
+                 bool traced = false) {
     const ijb_model_desc &d = e->d;
     require(n >= 1 && n <= d.max_batch, "step size must be 1..max_batch", IJB_ERR_CAPACITY);
     int *mt = e->meta_host;
@@ -504,7 +532,31 @@ void packed_step(ijb_engine *e, int n, const int *seqs, const int *tokens, const
         mt[3 * d.max_batch + i] = slot_for(e, sq, pos);
     }
     for (int i = n; i < d.max_batch; ++i) mt[i] = mt[d.max_batch + i] = mt[2 * d.max_batch + i] = mt[3 * d.max_batch + i] = 0;
-    run_step(e, n, need_logits);
+    run_step(e, n, need_logits, traced);
+}
+
+void ensure_trace_buffers(ijb_engine *e) {
+    if (e->trace_x) return;
+    const ijb_model_desc &d = e->d;
+    e->trace_q_stride = (3L * d.dim + d.hidden + 15) / 16 * 16;
+    e->trace_x = dev_alloc<float>(static_cast<size_t>(d.max_batch) * d.layers * d.dim, "layer trace");
+    e->trace_q = dev_alloc<int8_t>(static_cast<size_t>(d.max_batch) * d.layers * e->trace_q_stride, "quant trace");
+}
+
+// Copies token i of the last traced step: its residuals [layers][dim] and its
+// quantised activations [layers][3*dim + hidden] (either pointer may be null).
+void download_trace(ijb_engine *e, int i, float *layer_trace, int8_t *quant_trace) {
+    const ijb_model_desc &d = e->d;
+    if (layer_trace)
+        ck(cudaMemcpy(layer_trace, e->trace_x + static_cast<long>(i) * d.layers * d.dim,
+                      static_cast<size_t>(d.layers) * d.dim * 4, cudaMemcpyDeviceToHost),
+           "layer trace download");
+    if (quant_trace) {
+        const long width = 3L * d.dim + d.hidden;
+        ck(cudaMemcpy2D(quant_trace, width, e->trace_q + static_cast<long>(i) * d.layers * e->trace_q_stride,
+                        e->trace_q_stride, width, d.layers, cudaMemcpyDeviceToHost),
+           "quant trace download");
+    }
 }
 
 void validate_weight(const Weight &w, int type_a, int type_b, int rows, int cols) {
@@ -793,6 +845,8 @@ void ijb_destroy(ijb_engine *e) {
     cudaFree(e->attn_counters);
     cudaFree(e->status);
     cudaFree(e->scratch_key);
+    cudaFree(e->trace_x);
+    cudaFree(e->trace_q);
     if (e->ev_start) cudaEventDestroy(e->ev_start);
     if (e->ev_end) cudaEventDestroy(e->ev_end);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -839,6 +893,56 @@ int ijb_forward(ijb_engine *e, int token, int pos, int need_logits, int *next_to
         return fail(e, ex);
     }
 }
+
+int ijb_forward_traced(ijb_engine *e, int token, int pos, int need_logits, int *next_token, float *layer_trace,
+                       int8_t *quant_trace) {
+    try {
+        require(e != nullptr, "null engine");
+        require(pos >= 0 && pos < e->d.context && token >= 0 && token < e->d.vocab,
+                "Token or position outside model context");
+        require(pos <= e->seq_len[0], "position beyond the cached length of the sequence");
+        ensure_trace_buffers(e);
+        const int seq = 0;
+        packed_step(e, 1, &seq, &token, &pos, need_logits != 0, true);
+        e->seq_len[0] = pos + 1;
+        if (next_token) *next_token = need_logits ? e->next_host[0] : -1;
+        download_trace(e, 0, layer_trace, quant_trace);
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_prefill_traced(ijb_engine *e, const int *tokens, int n, int *next_token, float *all_layer_trace,
+                       int8_t *first_quant_trace, int8_t *last_quant_trace) {
+    try {
+        require(e != nullptr && tokens != nullptr && n >= 1, "bad arguments");
+        require(n <= e->d.context, "prompt exceeds context", IJB_ERR_CAPACITY);
+        ensure_trace_buffers(e);
+        e->seq_len[0] = 0;
+        const ijb_model_desc &d = e->d;
+        std::vector<int> seqs(d.max_batch, 0), pos(d.max_batch);
+        for (int c = 0; c < n; c += d.max_batch) {
+            const int cn = std::min(d.max_batch, n - c);
+            for (int i = 0; i < cn; ++i) pos[i] = c + i;
+            const bool last = c + cn == n;
+            packed_step(e, cn, seqs.data(), tokens + c, pos.data(), last, true);
+            e->seq_len[0] = c + cn;
+            for (int i = 0; i < cn && all_layer_trace; ++i)
+                download_trace(e, i, all_layer_trace + static_cast<long>(c + i) * d.layers * d.dim, nullptr);
+            if (c == 0) download_trace(e, 0, nullptr, first_quant_trace);
+            if (last) {
+                download_trace(e, cn - 1, nullptr, last_quant_trace);
+                if (next_token) *next_token = e->next_host[cn - 1];
+            }
+        }
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_last_step_size(const ijb_engine *e) { return e ? e->last_n : -1; }
 
 int ijb_seq_prefill(ijb_engine *e, int seq, const int *tokens, int n, int *next_token) {
     try {

@@ -188,6 +188,46 @@ cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch
     return cudaGetLastError();
 }
 
+// Debug trace of an activation the INT8 path quantises (what the reference
+// records in FastRunner::forward's quant_trace, inferencer.cu:1447-1452,
+// :1471-1476, :1490-1495, :1503-1508): per token (one CTA of 256 threads) an
+// optional RMSNorm with rmsnorm_cuda's 256 strided partial sums and tree
+// (:821-834), then quantize_x32_cuda's per-32 int8 codes (:544-556).
+__global__ void __launch_bounds__(256) ijb_trace_quant_kernel(const float *x, long x_stride, const float *norm_w,
+                                                              float eps, int cols, int8_t *out, long out_stride) {
+    __shared__ float partial[256];
+    const float *xr = x + blockIdx.x * x_stride;
+    int8_t *o = out + blockIdx.x * out_stride;
+    float r = 1.f;
+    if (norm_w) {
+        float sum = 0.f;
+        for (int i = threadIdx.x; i < cols; i += 256) sum = fmaf(xr[i], xr[i], sum);
+        partial[threadIdx.x] = sum;
+        __syncthreads();
+        for (int stride = 128; stride > 0; stride /= 2) {
+            if (static_cast<int>(threadIdx.x) < stride) partial[threadIdx.x] += partial[threadIdx.x + stride];
+            __syncthreads();
+        }
+        r = rsqrtf(partial[0] / cols + eps);
+    }
+    const int lane = threadIdx.x & 31;
+    for (int g = threadIdx.x >> 5; g < cols / 32; g += 8) {
+        const int i = g * 32 + lane;
+        float v = xr[i];
+        if (norm_w) v = __fmul_rn(__fmul_rn(v, r), norm_w[i]);
+        float amax = fabsf(v);
+        for (int o2 = 16; o2 > 0; o2 >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o2));
+        const float scale = amax > 0.f ? amax / 127.f : 1.f;
+        o[i] = static_cast<int8_t>(max(-127, min(127, __float2int_rn(v / scale))));
+    }
+}
+
+cudaError_t trace_quant_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int n,
+                               int8_t *out, long out_stride, cudaStream_t stream) {
+    ijb_trace_quant_kernel<<<n, 256, 0, stream>>>(x, x_stride, norm_w, eps, cols, out, out_stride);
+    return cudaGetLastError();
+}
+
 // Failure-path probe: one thread waits on a shared-memory barrier that
 // nothing signals, with the given limit, so the wait expires, records
 // kDevErrWaitTimeout in *status and returns; nothing faults or hangs.

@@ -18,6 +18,11 @@ cudaError_t argmax_launch(const float *v, int n, unsigned long long *key_scratch
 void set_thread_error(const std::string &msg);
 void count_launches(uint64_t n);
 
+// Debug trace: per token, optional RMSNorm then the per-32 int8 codes of x
+// (row stride x_stride) into out (row stride out_stride).
+cudaError_t trace_quant_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int n,
+                               int8_t *out, long out_stride, cudaStream_t stream);
+
 // One kernel whose bounded wait (limit_ns) on a barrier that nothing signals
 // expires and records kDevErrWaitTimeout in *status.
 cudaError_t wait_probe_launch(uint32_t *status, uint64_t limit_ns, cudaStream_t stream);

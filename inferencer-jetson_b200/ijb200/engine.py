@@ -83,6 +83,31 @@ class Engine:
         _L.check(self.lib.ijb_prefill(self.h, arr, len(tokens), ctypes.byref(nxt)), self.h)
         return nxt.value
 
+    def forward_traced(self, token: int, pos: int, need_logits: bool = True):
+        """FastRunner::forward with its traces: (next, layer_trace [layers][dim],
+        quant_trace [layers][3*dim + hidden] int8)."""
+        c = self.cfg
+        lt = np.zeros((c.layers, c.dim), np.float32)
+        qt = np.zeros((c.layers, 3 * c.dim + c.hidden), np.int8)
+        nxt = ctypes.c_int(-1)
+        _L.check(self.lib.ijb_forward_traced(self.h, int(token), int(pos), int(need_logits), ctypes.byref(nxt),
+                                             lt.ctypes.data, qt.ctypes.data), self.h)
+        return nxt.value, lt, qt
+
+    def prefill_traced(self, tokens):
+        """FastRunner::prefill with its traces: (next, all_layer_trace
+        [n][layers][dim], first_quant_trace, last_quant_trace)."""
+        c = self.cfg
+        n = len(tokens)
+        arr = (ctypes.c_int * n)(*[int(t) for t in tokens])
+        allt = np.zeros((n, c.layers, c.dim), np.float32)
+        fq = np.zeros((c.layers, 3 * c.dim + c.hidden), np.int8)
+        lq = np.zeros_like(fq)
+        nxt = ctypes.c_int(-1)
+        _L.check(self.lib.ijb_prefill_traced(self.h, arr, n, ctypes.byref(nxt), allt.ctypes.data, fq.ctypes.data,
+                                             lq.ctypes.data), self.h)
+        return nxt.value, allt, fq, lq
+
     def reset(self) -> None:
         _L.check(self.lib.ijb_reset(self.h), self.h)
 

@@ -77,6 +77,9 @@ def load():
         "ijb_repack_q6k": ([P, P, I, I, P], I),
         "ijb_gemv": ([I, P, P, P, I, I, I, I, P], I),
         "ijb_probe_wait_timeout": ([P, ctypes.c_uint64], I),
+        "ijb_forward_traced": ([P, I, I, I, IP, P, P], I),
+        "ijb_prefill_traced": ([P, IP, I, IP, P, P, P], I),
+        "ijb_last_step_size": ([P], I),
         "ijb_kernel_launches": ([], ctypes.c_uint64),
         "ijb_last_step_ms": ([P], ctypes.c_float),
     }

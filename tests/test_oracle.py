@@ -1,6 +1,8 @@
 """The CPU oracle pinned against the reference: golden vectors captured from
 the reference's own kernels on a B200 (tests/golden/ref_kernels.npz) and the
 independent gguf package dequantiser."""
+import os
+
 import numpy as np
 import pytest
 
@@ -258,3 +260,61 @@ def test_multi_vector_matvec_equals_matvec(qt, rows, cols):
             y = O.matvec_multi(qt, W, xs, cols, rows, dp, dp, c)
             for i in range(9):
                 assert np.array_equal(y[i], O.matvec(qt, W, xs[i], cols, rows, dp, dp, c))
+
+
+RUNNER_GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ref_runner_3b.npz")
+
+
+@pytest.fixture(scope="module")
+def runner_golden():
+    if not os.path.exists(RUNNER_GOLDEN):
+        pytest.skip("tests/golden/ref_runner_3b.npz not captured yet (make_ref_runner_golden.py)")
+    import make_ref_runner_golden as G
+    g = dict(np.load(RUNNER_GOLDEN))
+    return g, G, synth.make_model(synth.LLAMA_3B, seed=int(g["seed"]))
+
+
+def _sample_rel(logits, g, tag):
+    rows = g["sample_rows"]
+    a = logits[:, rows].astype(np.float64)
+    b = g[f"{tag}_sample"].astype(np.float64)
+    return np.linalg.norm(a - b, axis=1) / np.linalg.norm(b, axis=1)
+
+
+@pytest.mark.parametrize("tag,dp4a", [("fp32", False), ("int8", True)])
+def test_oracle_full_model_matches_the_reference_runner(runner_golden, tag, dp4a):
+    """The oracle's whole layer sequence (embedding, 28 layers of norm / QKV /
+    RoPE / cache / attention / O / residual / norm / gate-up / SiLU / down /
+    residual, output norm, tied Q6_K lm_head, argmax) against the reference's
+    own GGUF + FastRunner::forward (inferencer.cu:1424-1531) run on a B200 on
+    the same seeded 3B-shape model and tokens (tests/golden/ref_runner_3b.npz).
+    FP32 path: the GEMVs are bit-exact and only rsqrtf / __expf differ from
+    the oracle's 1/sqrtf / expf, so the logits agree to ~1e-5.  INT8 path:
+    those ulp differences flip int8 codes, so the bar is twice the path's own
+    floor (the oracle against itself with one contraction changed)."""
+    g, G, weights = runner_golden
+    toks = g["tokens"]
+    O.set_threads(8)
+
+    def run(contract):
+        m = O.OracleModel(synth.LLAMA_3B, weights, G.CONTEXT, dp4a, dp4a, contract=contract)
+        st = m.new_state()
+        nxt, lg = m.forward_multi([st] * len(toks), toks, np.arange(len(toks)), True, want_logits=True)
+        return nxt, lg
+
+    nxt, lg = run(1)
+    rel = _sample_rel(lg, g, tag)
+    agree = float(np.mean(nxt == g[f"{tag}_next"]))
+    top_match = float(np.mean(np.take_along_axis(lg, g[f"{tag}_top_idx"], axis=1)[:, 0] == g[f"{tag}_top_val"][:, 0]))
+    print(f"\n{tag}: sampled logits rel-L2 max {rel.max():.3e} mean {rel.mean():.3e}; argmax agreement {agree:.3f}; "
+          f"top-1 value equal {top_match:.3f}")
+    if not dp4a:
+        assert rel.max() < 1e-4, rel
+        assert agree == 1.0
+    else:
+        _, lg_alt = run(0)
+        floor = np.linalg.norm((lg_alt - lg)[:, g["sample_rows"]], axis=1) / np.linalg.norm(lg[:, g["sample_rows"]],
+                                                                                              axis=1)
+        print(f"int8 floor max {floor.max():.3e} mean {floor.mean():.3e}")
+        assert rel.max() <= 2 * max(floor.max(), 1e-6), (rel.max(), floor.max())
+        assert agree >= 0.95
