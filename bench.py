@@ -16,6 +16,9 @@ Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
             (the batch-1 configuration on the same GPU).
   decode1   same model, one sequence: 512-token prompt (ids U[0,128000),
             seed 1), then greedy decode steps.
+  ragged256_3b  Llama-3.2-3B-architecture Q4_K_M (head_dim 128, 24 / 8
+            heads), 256 ragged sequences per GPU, prompts U[64,4096], outputs
+            U[64,512], pre-aged and replaced as in ragged64.
   gemv_q4k / gemv_q6k  BASELINE configs 0 / 1 (batch 1) in GB/s.
   gemm_q6k_b64  the vocab projection alone (tensor-core GEMM, 64 tokens).
   gemm_layer    one layer's seven projections alone (tensor-core GEMM, 64
@@ -70,8 +73,8 @@ def parse(argv=None):
     ap.add_argument("--steps", type=int, default=48)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["ragged64", "decode1", "gemv_q4k", "gemv_q6k", "gemm_q6k_b64",
-                                           "gemm_layer"], default="ragged64")
+    ap.add_argument("--workload", choices=["ragged64", "decode1", "ragged256_3b", "gemv_q4k", "gemv_q6k",
+                                           "gemm_q6k_b64", "gemm_layer"], default="ragged64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="ragged64: skip the decode1 record, kernel timings and reference CUDA timings")
@@ -314,9 +317,12 @@ class RaggedServer:
     its steady state when timing starts: sequences finish and are replaced
     throughout the timed window, and contexts follow the steady-state mix."""
 
-    def __init__(self, eng, batch, seed, vocab_limit=128000, prompt_max=1024, aged=True):
+    def __init__(self, eng, batch, seed, vocab_limit=128000, prompt_max=1024, aged=True, prompt_min=16,
+                 out_range=(32, 256)):
         self.eng = eng
+        self.prompt_min = prompt_min
         self.prompt_max = prompt_max
+        self.out_range = out_range
         self.batch = batch
         self.rng = np.random.default_rng(seed)
         self.vocab_limit = vocab_limit
@@ -328,8 +334,8 @@ class RaggedServer:
             self.live.append(self._admit(aged))
 
     def _admit(self, aged=False):
-        plen = int(self.rng.integers(16, self.prompt_max + 1))
-        target = int(self.rng.integers(32, 257))
+        plen = int(self.rng.integers(self.prompt_min, self.prompt_max + 1))
+        target = int(self.rng.integers(self.out_range[0], self.out_range[1] + 1))
         g0 = int(self.rng.integers(0, target)) if aged else 0
         prompt = self.rng.integers(0, self.vocab_limit, size=plen + g0).astype(np.int32)
         s = self.eng.seq_open()
@@ -711,7 +717,8 @@ def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     cuda = torch.device(f"cuda:{local}")
     peak, peak_src = hbm_peak()
-    cfg = synth.LLAMA_1B
+    big = args.workload == "ragged256_3b"
+    cfg = synth.LLAMA_3B if big else synth.LLAMA_1B
     t_setup = time.perf_counter()
     weights = synth.make_model(cfg, seed=0)
     from ijb200.engine import Engine
@@ -719,6 +726,11 @@ def run_ours(args):
         batch, context = 64, args.prompt_max + 256 + 16
         eng = Engine(cfg, weights, context=context, max_batch=batch, max_seqs=batch + 1, device=local)
         server = RaggedServer(eng, batch, seed=1000 + rank, prompt_max=args.prompt_max)
+    elif big:
+        pmax = min(args.prompt_max * 4, 4096)  # 4096 by default
+        batch, context = 256, pmax + 512 + 16
+        eng = Engine(cfg, weights, context=context, max_batch=batch, max_seqs=batch + 1, device=local)
+        server = RaggedServer(eng, batch, seed=2000 + rank, prompt_max=pmax, prompt_min=64, out_range=(64, 512))
     else:
         batch, context = 1, args.prompt + 16 + args.steps + args.warmup + 8
         eng = Engine(cfg, weights, context=context, max_batch=1, max_seqs=2, device=local)
@@ -727,9 +739,11 @@ def run_ours(args):
         pos = len(prompt)
     setup_s = time.perf_counter() - t_setup
 
+    ragged = args.workload in ("ragged64", "ragged256_3b")
+
     def one_step():
         nonlocal nxt, pos
-        if args.workload == "ragged64":
+        if ragged:
             return server.step()
         t0 = time.perf_counter()
         nxt = eng.forward(nxt, pos, True)
@@ -741,10 +755,10 @@ def run_ours(args):
     # warm-up (includes graph capture)
     for _ in range(args.warmup):
         one_step()
-        if args.workload == "ragged64":
+        if ragged:
             server.replace_finished()
     sampler.wait_first()
-    replaced0 = server.replaced if args.workload == "ragged64" else 0
+    replaced0 = server.replaced if ragged else 0
     barrier(world)
     sampler.mark_start()
     launches0 = ijblib.load().ijb_kernel_launches()
@@ -760,7 +774,7 @@ def run_ours(args):
         dev_ms += ms
         wall_s += wall
         kv_tokens += ctx
-        if args.workload == "ragged64":
+        if ragged:
             t0 = time.perf_counter()
             server.replace_finished()
             replaced_s += time.perf_counter() - t0
@@ -784,10 +798,16 @@ def run_ours(args):
 
     result = None
     if rank == 0:
-        ragged = args.workload == "ragged64"
-        extras = ragged and not args.no_extras
+        extras = args.workload == "ragged64" and not args.no_extras
         kern = gemv_roofline(cuda, peak) if (extras or not ragged) else None
-        if ragged:
+        if big:
+            # KV bytes are ~97% of this step: the roofline is the step's own
+            dom = {"gbs": step_gbs, "frac": step_gbs / peak, "traffic": None,
+                   "kernel": "whole decode step (attention over the paged KV cache is ~97% of its bytes)",
+                   "us_per_layer": ms_per_step * 1e3 / cfg.layers, "weight_bytes": w_bytes,
+                   "algorithmic_bytes": step_bytes, "traffic_source": None, "per_projection": None}
+            vocab = None
+        elif ragged:
             dom = layer_roofline(eng, cuda, peak)
             vocab = mma_vocab_roofline(eng, cuda, peak) if extras else None
         else:
@@ -812,16 +832,22 @@ def run_ours(args):
                                                   "sample": f"one decode token at each context {used1}"},
                              "gemv_1_thread": cpu_gemv(1), f"gemv_{nthreads}_threads": cpu_gemv(nthreads)}
         h2d = 4 * batch * 4  # token, seq, position, KV slot per entry (int32)
+        metric = ("decode tokens/s (3B Q4_K_M, batch 256)" if big else
+                  "decode tokens/s (1B Q4_K_M, batch 64)" if ragged else "decode tokens/s (1B Q4_K_M, batch 1)")
+        workload = (f"llama-3.2-3b Q4_K_M ragged decode, 256 seqs, prompts U[64,{server.prompt_max}], outputs "
+                    "U[64,512], replacement, pre-aged population" if big else
+                    f"llama-3.2-1b Q4_K_M ragged decode, 64 seqs, prompts U[16,{args.prompt_max}], "
+                    "outputs U[32,256], replacement, pre-aged population" if ragged
+                    else f"llama-3.2-1b Q4_K_M decode, batch 1, {args.prompt}-token prompt")
         result = {
-            "metric": "decode tokens/s (1B Q4_K_M, batch 64)" if ragged else "decode tokens/s (1B Q4_K_M, batch 1)",
+            "metric": metric,
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE_TC if ragged else DTYPE_DP4A, "data": "synthetic (random-init weights, seeded)",
-            "config": {"workload": f"llama-3.2-1b Q4_K_M ragged decode, 64 seqs, prompts U[16,{args.prompt_max}], "
-                                   "outputs U[32,256], replacement, pre-aged population" if ragged
-                       else f"llama-3.2-1b Q4_K_M decode, batch 1, {args.prompt}-token prompt",
+            "config": {"workload": workload,
                        "batch_per_gpu": batch, "page_size": 16, "kv": "fp16 paged",
-                       "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (836 MB weights/step)",
+                       "parallelism": f"replicas x{world}",
+                       "l2": f"inputs larger than L2 ({w_bytes / 1e6:.0f} MB weights/step)",
                        "mean_context": kv_tokens / args.steps / batch,
                        "replaced_in_window": (server.replaced - replaced0) if ragged else 0},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * batch},
@@ -868,7 +894,8 @@ def run_reference(args):
     if rank != 0:
         return None
     import oracle as O
-    cfg = synth.LLAMA_1B
+    big = args.workload == "ragged256_3b"
+    cfg = synth.LLAMA_3B if big else synth.LLAMA_1B
     weights = synth.make_model(cfg, seed=0)
     threads = os.cpu_count() or 1
     O.set_threads(threads)
@@ -876,6 +903,8 @@ def run_reference(args):
     if args.workload == "ragged64":
         # contexts of a steady ragged population: prompt U[16,1024] + generated so far
         ctxs = [int(rng.integers(16, 1025) + rng.integers(0, 257)) for _ in range(args.steps + args.warmup)]
+    elif big:
+        ctxs = [int(rng.integers(64, 4097) + rng.integers(0, 513)) for _ in range(args.steps + args.warmup)]
     else:
         ctxs = [512 + i for i in range(args.steps + args.warmup)]
     m = O.OracleModel(cfg, weights, max(ctxs) + 2, True, True)
@@ -891,12 +920,13 @@ def run_reference(args):
         del st
     value = args.steps / t_total
     return {
-        "impl": "reference", "metric": "decode tokens/s (1B Q4_K_M, batch 64)" if args.workload == "ragged64"
-        else "decode tokens/s (1B Q4_K_M, batch 1)",
+        "impl": "reference", "metric": "decode tokens/s (3B Q4_K_M, batch 256)" if big else
+        "decode tokens/s (1B Q4_K_M, batch 64)" if args.workload == "ragged64" else "decode tokens/s (1B Q4_K_M, batch 1)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t_total / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8xq4/q6 dp4a, fp32 accumulate, fp32 KV", "data": "synthetic (random-init weights, seeded)",
-        "config": {"workload": "llama-3.2-1b Q4_K_M ragged decode, 64 seqs" if args.workload == "ragged64"
+        "config": {"workload": "llama-3.2-3b Q4_K_M ragged decode, 256 seqs" if big else
+                   "llama-3.2-1b Q4_K_M ragged decode, 64 seqs" if args.workload == "ragged64"
                    else "llama-3.2-1b Q4_K_M decode, batch 1", "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"one decode token per step of one sequence at the workload's context lengths "

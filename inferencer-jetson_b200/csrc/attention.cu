@@ -860,11 +860,15 @@ static cudaError_t attention_launch_t(const AttnParams &p, dim3 grid, cudaStream
         if (G == 8) return launch_attn<64, 8, KT>(p, grid, stream, pdl);
         if (G == 2) return launch_attn<64, 2, KT>(p, grid, stream, pdl);
         if (G == 1) return launch_attn<64, 1, KT>(p, grid, stream, pdl);
+        if (G == 3) return launch_attn<64, 3, KT>(p, grid, stream, pdl);
+        if (G == 6) return launch_attn<64, 6, KT>(p, grid, stream, pdl);
     } else if (p.head_dim == 128) {
         if (G == 4) return launch_attn<128, 4, KT>(p, grid, stream, pdl);
         if (G == 8) return launch_attn<128, 8, KT>(p, grid, stream, pdl);
         if (G == 2) return launch_attn<128, 2, KT>(p, grid, stream, pdl);
         if (G == 1) return launch_attn<128, 1, KT>(p, grid, stream, pdl);
+        if (G == 3) return launch_attn<128, 3, KT>(p, grid, stream, pdl);
+        if (G == 6) return launch_attn<128, 6, KT>(p, grid, stream, pdl);
     }
     return cudaErrorInvalidValue;
 }
@@ -875,7 +879,7 @@ static cudaError_t attention_launch_t(const AttnParams &p, dim3 grid, cudaStream
 static bool stream_path(const AttnParams &p) {
     const int G = p.kv_heads > 0 ? p.heads / p.kv_heads : 0;
     return p.has_map && p.head_dim == 64 && !p.kv_f32 && p.work && p.num_ctas >= 1 && p.batch <= kStreamMaxBatch &&
-           p.max_splits <= 32 && (G == 1 || G == 2 || G == 4 || G == 8) && G * p.kv_heads == p.heads &&
+           p.max_splits <= 32 && (G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8) && G * p.kv_heads == p.heads &&
            p.page_size <= kStreamChunk && kStreamChunk % p.page_size == 0;  // a chunk is whole pages
 }
 
@@ -896,7 +900,8 @@ static cudaError_t set_attrs_t() {
     cudaError_t e;
     if ((e = set_attr<64, 1, KT>()) || (e = set_attr<64, 2, KT>()) || (e = set_attr<64, 4, KT>()) ||
         (e = set_attr<64, 8, KT>()) || (e = set_attr<128, 1, KT>()) || (e = set_attr<128, 2, KT>()) ||
-        (e = set_attr<128, 4, KT>()) || (e = set_attr<128, 8, KT>()))
+        (e = set_attr<128, 4, KT>()) || (e = set_attr<128, 8, KT>()) || (e = set_attr<64, 3, KT>()) ||
+        (e = set_attr<64, 6, KT>()) || (e = set_attr<128, 3, KT>()) || (e = set_attr<128, 6, KT>()))
         return e;
     return cudaSuccess;
 }
@@ -906,7 +911,9 @@ cudaError_t attention_prepare() {
     if ((e = cudaFuncSetAttribute(ijb_attention_stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
         (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
         (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)))
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)))
         return e;
     e = set_attrs_t<__half>();
     return e != cudaSuccess ? e : set_attrs_t<float>();
@@ -924,6 +931,8 @@ cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
         if (G == 8) return launch_attn_stream<8>(p, stream, pdl);
         if (G == 2) return launch_attn_stream<2>(p, stream, pdl);
         if (G == 1) return launch_attn_stream<1>(p, stream, pdl);
+        if (G == 3) return launch_attn_stream<3>(p, stream, pdl);
+        if (G == 6) return launch_attn_stream<6>(p, stream, pdl);
     }
     // one CTA per split of kAttnSplit positions (the partial records are kept
     // at kAttnItem granularity, so max_splits counts items)

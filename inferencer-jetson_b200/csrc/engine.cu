@@ -584,7 +584,8 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         e->kv_dim = e->head_dim * d.kv_heads;
         const int G = d.heads / d.kv_heads;
         require(e->head_dim == 64 || e->head_dim == 128, "head_dim must be 64 or 128");
-        require(G == 1 || G == 2 || G == 4 || G == 8, "heads / kv_heads must be 1, 2, 4 or 8");
+        require(G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8,
+                "heads / kv_heads must be 1, 2, 3, 4, 6 or 8");
         require(d.vocab > 0 && d.vocab <= 512 * 256, "vocab must be <= 131072 (the reference's two-pass argmax)");
         require(d.layers > 0 && d.context > 0 && d.max_batch > 0 && d.max_seqs > 0, "bad limits");
         require(d.page_size == 16 || d.page_size == 32 || d.page_size == 8, "page_size must be 8, 16 or 32");

@@ -131,6 +131,9 @@ LLAMA_1B = ModelConfig("llama-3.2-1b", dim=2048, layers=16, heads=32, kv_heads=8
 LLAMA_3B = ModelConfig("llama-3.2-3b", dim=3072, layers=28, heads=24, kv_heads=8, hidden=8192, vocab=128256)
 TINY = ModelConfig("tiny", dim=512, layers=2, heads=8, kv_heads=2, hidden=1024, vocab=4096)
 TINY_HD128 = ModelConfig("tiny-hd128", dim=512, layers=2, heads=4, kv_heads=2, hidden=768, vocab=2048)
+# three query heads per KV head, as in the 3B shape (24 / 8)
+TINY_G3 = ModelConfig("tiny-g3", dim=768, layers=2, heads=12, kv_heads=4, hidden=1024, vocab=4096)
+TINY_HD128_G3 = ModelConfig("tiny-hd128-g3", dim=768, layers=2, heads=6, kv_heads=2, hidden=768, vocab=2048)
 
 # Weight scale ranges for random-init models.  They are chosen so every
 # projection of a unit-RMS input has roughly unit RMS output (sigma_w close to

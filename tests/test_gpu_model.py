@@ -72,7 +72,8 @@ def _run_pair(cfg, weights, prompt, steps, dp4a=True, q6_dp4a=True, context=256,
     return np.array(errs), agree / steps
 
 
-@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_HD128], ids=lambda c: c.name)
+@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_HD128, synth.TINY_G3, synth.TINY_HD128_G3],
+                         ids=lambda c: c.name)
 @pytest.mark.parametrize("mode", [(True, True), (False, False), (True, False)], ids=["dp4a", "fp32", "float-q6"])
 @pytest.mark.parametrize("kv_f32", [True, False], ids=["kv32", "kv16"])
 def test_small_model_logits_and_greedy(cuda, cfg, mode, kv_f32):
@@ -107,12 +108,12 @@ def test_1b_width_model_128_steps(cuda):
         assert agree >= 0.99, (kv_f32, agree)
 
 
+@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_G3], ids=lambda c: c.name)
 @pytest.mark.parametrize("prompts,context", [((3, 40), 128), ((150, 300), 512)], ids=["one-item", "multi-item"])
-def test_ragged_step_matches_single_sequence_runs(cuda, prompts, context):
+def test_ragged_step_matches_single_sequence_runs(cuda, prompts, context, cfg):
     """Each sequence of a packed step matches the same sequence decoded alone
     (multi-item: sequences longer than one 128-position attention work item,
     so the split merge runs inside packed steps)."""
-    cfg = synth.TINY
     weights = synth.make_model(cfg, seed=5)
     reqs = synth.ragged_requests(5, prompt_range=prompts, output_range=(4, 8), seed=7, vocab_limit=cfg.vocab)
     # batched engine

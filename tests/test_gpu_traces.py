@@ -46,9 +46,11 @@ def test_prefill_traces_agree_with_token_by_token(cuda, max_batch):
     cfg = synth.TINY
     w = synth.make_model(cfg, seed=12)
     prompt = synth.prompt_tokens(21, seed=2, vocab_limit=cfg.vocab)
-    eng = Engine(cfg, w, context=64, max_batch=max_batch, max_seqs=2)
+    # FP32 activation path: the INT8 path's requantisation would turn the
+    # tensor-core path's fp16 rounding into ~1% differences (its own floor)
+    eng = Engine(cfg, w, context=64, max_batch=max_batch, max_seqs=2, use_dp4a=False, use_q6_dp4a=False)
     nxt, allt, fq, lq = eng.prefill_traced(prompt)
-    seq = Engine(cfg, w, context=64, max_batch=1, max_seqs=2)
+    seq = Engine(cfg, w, context=64, max_batch=1, max_seqs=2, use_dp4a=False, use_q6_dp4a=False)
     for i, t in enumerate(prompt):
         n1, lt, qt = seq.forward_traced(int(t), i, i + 1 == len(prompt))
         tol = 5e-3 if max_batch >= 16 else 1e-5  # the tensor-core path rounds to fp16
