@@ -46,7 +46,8 @@ int main(int argc, char **argv) {
         model.upload();
         const int context = 64;
         FastRunner ref(model, context, dp4a, dp4a, false, false, 4, 4, 32);
-        ijb_host::FastRunner ours(model, context, dp4a, dp4a, false, false, 4, 4, 32);
+        // the reference caches K/V in fp32 (inferencer.cu:1132); the shim is built with the same format
+        ijb_host::FastRunner ours(model, context, dp4a, dp4a, false, false, 4, 4, 32, 0, true);
         if (ours.dim != ref.dim || ours.layers != ref.layers || ours.vocab != ref.vocab)
             throw std::runtime_error("shape fields differ");
 
