@@ -2,7 +2,8 @@
 """Decode-throughput benchmark of the B200 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload ragged64|decode1|gemv_q4k|gemv_q6k|gemm_q6k_b64|gemm_layer]
+                    [--workload ragged64|decode1|ragged256_3b|gemv_q4k|gemv_q6k|gemm_q6k_b64|gemm_layer|
+                                tp_lm_head]
 
 Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
   ragged64  (default) Llama-3.2-1B-architecture Q4_K_M, 64 concurrent
@@ -21,8 +22,13 @@ Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
             U[64,512], pre-aged and replaced as in ragged64.
   gemv_q4k / gemv_q6k  BASELINE configs 0 / 1 (batch 1) in GB/s.
   gemm_q6k_b64  the vocab projection alone (tensor-core GEMM, 64 tokens).
-  gemm_layer    one layer's seven projections alone (tensor-core GEMM, 64
-            tokens): the kernel the ragged64 roofline reports.
+  gemm_layer    one layer's four projection launches alone (tensor-core GEMM,
+            64 tokens): the kernel the ragged64 roofline reports.
+  tp_lm_head  the 3B lm_head (Q6_K 128256x3072) row-split over the N ranks,
+            256 tokens per step: each rank's slice on the tensor cores, then
+            an NCCL all-gather of the logits (the line's value) or one
+            all-reduce of the packed argmax keys (`keys_only`); total work is
+            fixed (strong scaling), checked against one GPU's full lm_head.
 `value` is whole-job decode tokens/s: tokens generated in the K timed steps
 on all ranks / max over ranks of the device time of those steps (CUDA events
 around each step's graph).  Replacement prefills run between timed steps and
@@ -74,7 +80,7 @@ def parse(argv=None):
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["ragged64", "decode1", "ragged256_3b", "gemv_q4k", "gemv_q6k",
-                                           "gemm_q6k_b64", "gemm_layer"], default="ragged64")
+                                           "gemm_q6k_b64", "gemm_layer", "tp_lm_head"], default="ragged64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="ragged64: skip the decode1 record, kernel timings and reference CUDA timings")
@@ -432,25 +438,38 @@ def _timed_launches(fn, iters, stream_obj):
     return a.elapsed_time(b) / iters
 
 
-def layer_roofline(eng, cuda, peak, iters=20, batch=64, layer=0):
-    """The step's dominant kernel: the tensor-core GEMM (ijb_mma_gemm_kernel,
-    each launch preceded by its activation prep ijb_mma_prep_kernel) over one
-    layer's seven projections (q, k, v, o, gate, up, down) for `batch` tokens
-    through ijb_matvec, timed with CUDA events on its own stream.  Algorithmic
-    bytes: the weights as stored + the fp32 activations read + the fp32
-    outputs written.  In the step the same weights go through four fused
-    launches (QKV, O, gate/up, down); here each matrix is one launch."""
+def layer_roofline(cuda, peak, local, iters=20, batch=64):
+    """The step's dominant kernel, timed as the step issues it: one layer's
+    four tensor-core projection launches (QKV with RoPE and the K/V cache
+    write, O + residual, gate/up + SiLU, down + residual; ijb_mma_gemm_kernel,
+    each preceded by its activation prep ijb_mma_prep_kernel) for `batch`
+    tokens, replayed `iters` times in one CUDA graph by
+    ijb_time_layer_projections on a one-layer engine of the 1B widths (CUDA
+    events on the engine's stream).  Algorithmic bytes per layer: the weights as
+    stored + each projection's fp32 input read and output written (a residual
+    add counts its read and its write) + the fp16 K/V written.  Each matrix
+    alone through ijb_matvec (prep + GEMM per matrix) is reported beside it."""
     import torch
     L = ijblib.load()
+    eng = _layer_engine(local, context=max(128, batch))
     cfg = eng.cfg
+    ms = ctypes.c_float()
+    ijblib.check(L.ijb_time_layer_projections(eng.h, batch, iters, ctypes.byref(ms)), eng.h)
+    shapes = {n: (t, r, c) for n, t, r, c in cfg.matrices()}
+    w_bytes = sum(r * (c // 256) * synth.BLOCK_BYTES[t] for n, (t, r, c) in shapes.items() if n.startswith("blk.0."))
+    D, F, KV = cfg.dim, cfg.hidden, cfg.kv_dim
+    act = batch * 4 * (D + D          # QKV: x read, q written
+                       + D + 2 * D    # O: attention output read, residual read + written
+                       + D + F        # gate/up: x read, h written
+                       + F + 2 * D)   # down: h read, residual read + written
+    act += batch * 2 * KV * 2 + 2 * D * 4  # K and V written (fp16), the two norm weight vectors
+    algo = w_bytes + act
+    gbs = algo / (ms.value * 1e-3) / 1e9
     side = torch.cuda.Stream(device=cuda)
     stream = side.cuda_stream
-    shapes = {n: (t, r, c) for n, t, r, c in cfg.matrices()}
-    names = [f"blk.{layer}.{m}.weight" for m in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate",
-                                                 "ffn_up", "ffn_down")]
     per = {}
-    total_ms, total_bytes, w_bytes = 0.0, 0, 0
-    for name in names:
+    for m in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
+        name = f"blk.0.{m}.weight"
         t, rows, cols = shapes[name]
         x = torch.randn(batch, cols, device=cuda)
         y = torch.empty(batch, rows, device=cuda)
@@ -459,21 +478,18 @@ def layer_roofline(eng, cuda, peak, iters=20, batch=64, layer=0):
         def launch():
             ijblib.check(L.ijb_matvec(eng.h, idx, x.data_ptr(), y.data_ptr(), cols, rows, batch,
                                       ctypes.c_void_p(stream)), eng.h)
-        ms = _timed_launches(launch, iters, side)
-        wb = rows * (cols // 256) * synth.BLOCK_BYTES[t]
-        algo = wb + batch * cols * 4 + batch * rows * 4
-        per[name.split(".")[2]] = {"us": ms * 1e3, "gbs": algo / (ms * 1e-3) / 1e9}
-        total_ms += ms
-        total_bytes += algo
-        w_bytes += wb
-    gbs = total_bytes / (total_ms * 1e-3) / 1e9
+        us = _timed_launches(launch, iters, side) * 1e3
+        b = rows * (cols // 256) * synth.BLOCK_BYTES[t] + batch * (cols + rows) * 4
+        per[m] = {"us": us, "gbs": b / (us * 1e-6) / 1e9}
+    eng.close()
     traffic = profile_figure("mma_gemm_layer_ragged64.md", "dram_bytes_per_layer")
-    return {"kernel": f"ijb_mma_gemm_kernel + ijb_mma_prep_kernel, one layer's 7 projections, {batch} tokens "
-                      f"(1B widths)", "us_per_layer": total_ms * 1e3, "algorithmic_bytes": total_bytes,
-            "weight_bytes": w_bytes, "gbs": gbs, "frac": gbs / peak, "traffic": traffic,
+    return {"kernel": f"ijb_mma_gemm_kernel + ijb_mma_prep_kernel: one layer's 4 projection launches as the step "
+                      f"issues them, {batch} tokens (1B widths)", "us_per_layer": ms.value * 1e3,
+            "algorithmic_bytes": algo, "weight_bytes": w_bytes, "gbs": gbs, "frac": gbs / peak,
+            "traffic": traffic,
             "traffic_source": "profiles/mma_gemm_layer_ragged64.md (ncu dram__bytes_read.sum + "
-                              "dram__bytes_write.sum over the layer's 14 launches)" if traffic else None,
-            "per_projection": per}
+                              "dram__bytes_write.sum over the layer's 8 launches)" if traffic else None,
+            "per_matrix_alone": per}
 
 
 def mma_vocab_roofline(eng, cuda, peak, iters=20, batch=64):
@@ -645,12 +661,12 @@ def run_gemv(args):
             "reference_cuda": reference_cuda_gemv((case,)).get(case[0])}
 
 
-def _layer_engine(local, layers=1):
+def _layer_engine(local, layers=1, context=32):
     full = synth.LLAMA_1B
     cfg = synth.ModelConfig(f"llama-3.2-1b-{layers}layer", dim=full.dim, layers=layers, heads=full.heads,
                             kv_heads=full.kv_heads, hidden=full.hidden, vocab=full.vocab)
     from ijb200.engine import Engine
-    return Engine(cfg, synth.make_model(cfg, seed=0), context=32, max_batch=64, device=local)
+    return Engine(cfg, synth.make_model(cfg, seed=0), context=context, max_batch=64, max_seqs=2, device=local)
 
 
 def run_gemm(args):
@@ -660,14 +676,15 @@ def run_gemm(args):
     world, rank, local = dist_setup(args.gpus)
     cuda = torch.device(f"cuda:{local}")
     peak, src = hbm_peak()
-    eng = _layer_engine(local)
     if args.workload == "gemm_layer":
-        r = layer_roofline(eng, cuda, peak, iters=max(args.steps, 5))
-        metric, value, ms = "GEMM HBM GB/s (one 1B layer's 7 projections, 64 tokens)", r["gbs"], r["us_per_layer"] / 1e3
+        r = layer_roofline(cuda, peak, local, iters=max(args.steps, 5))
+        metric, value, ms = ("GEMM HBM GB/s (one 1B layer's 4 projection launches, 64 tokens)", r["gbs"],
+                             r["us_per_layer"] / 1e3)
     else:
+        eng = _layer_engine(local)
         r = mma_vocab_roofline(eng, cuda, peak, iters=max(args.steps, 5))
         metric, value, ms = "GEMM HBM GB/s (Q6_K 128256x2048 vocab projection, 64 tokens)", r["gbs"], r["us_per_launch"] / 1e3
-    eng.close()
+        eng.close()
     if rank != 0:
         return None
     return {"metric": metric, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 3,
@@ -708,8 +725,70 @@ def decode1_record(cuda, local, cfg, weights, peak, steps, warmup, prompt_len=51
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / peak}}
 
 
+def run_tp_lm_head(args):
+    """BASELINE config 4's optional variant: the lm_head row-split over the
+    ranks with an NCCL all-gather of the logits (ijb200.tp)."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup(args.gpus)
+    cuda = torch.device(f"cuda:{local}")
+    peak, src = hbm_peak()
+    from ijb200 import tp
+    cfg = synth.LLAMA_3B
+    rng = np.random.default_rng(7)
+    blocks = synth.quant_matrix(rng, 14, cfg.vocab, cfg.dim, d_range=(2e-5, 4e-5))
+    norm_w = torch.from_numpy(rng.uniform(0.8, 1.2, cfg.dim).astype(np.float32)).to(cuda)
+    n = 256
+    x = torch.from_numpy(np.random.default_rng(8).standard_normal((n, cfg.dim)).astype(np.float32)).to(cuda)
+    head = tp.RowSplitLmHead(blocks, 14, cfg.vocab, cfg.dim, rank, world, local)
+    timings = {}
+    tokens = logits = None
+    for mode in ("keys", "logits"):
+        for _ in range(max(3, args.warmup)):
+            head.forward(x, norm_w, cfg.eps, True, gather=mode)
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            tokens, logits = head.forward(x, norm_w, cfg.eps, True, gather=mode)
+        b.record()
+        barrier(world)
+        (ms_max,), _ = reduce_max_sum(world, [a.elapsed_time(b) / args.steps], [0.0])
+        timings[mode] = ms_max
+    check = None
+    if rank == 0:
+        full = tp.RowSplitLmHead(blocks, 14, cfg.vocab, cfg.dim, 0, 1, local)
+        ft, fl = full.forward(x, norm_w, cfg.eps, True, gather="logits")
+        rel = float(torch.linalg.norm(logits - fl) / torch.linalg.norm(fl))
+        check = {"logits_rel_l2_vs_one_gpu": rel, "tokens_equal": float((tokens == ft).float().mean())}
+        full.close()
+    head.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    step_bytes = cfg.vocab * (cfg.dim // 256) * 210 + n * cfg.dim * 4 + n * cfg.vocab * 4
+    ms = timings["logits"]
+    achieved = step_bytes / world / (ms * 1e-3) / 1e9
+    return {"metric": "lm_head tokens/s (3B Q6_K 128256x3072, row-split, all-gather of logits)",
+            "value": n / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": DTYPE_TC, "data": "synthetic (seeded)",
+            "config": {"workload": "tp_lm_head", "tokens": n, "rows_per_rank": -(-cfg.vocab // world),
+                       "parallelism": f"tp{world} (lm_head rows)"},
+            "keys_only": {"ms_per_step": timings["keys"], "value": n / (timings["keys"] * 1e-3),
+                          "bytes_per_rank": n * 8},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "ijb_mma_gemm_kernel (each rank's lm_head slice) + NCCL all-gather",
+                         "peak_source": src},
+            "check": check}
+
+
 def run_ours(args):
     import torch
+    if args.workload == "tp_lm_head":
+        return run_tp_lm_head(args)
     if args.workload.startswith("gemv"):
         return run_gemv(args)
     if args.workload.startswith("gemm"):
@@ -805,10 +884,10 @@ def run_ours(args):
             dom = {"gbs": step_gbs, "frac": step_gbs / peak, "traffic": None,
                    "kernel": "whole decode step (attention over the paged KV cache is ~97% of its bytes)",
                    "us_per_layer": ms_per_step * 1e3 / cfg.layers, "weight_bytes": w_bytes,
-                   "algorithmic_bytes": step_bytes, "traffic_source": None, "per_projection": None}
+                   "algorithmic_bytes": step_bytes, "traffic_source": None, "per_matrix_alone": None}
             vocab = None
         elif ragged:
-            dom = layer_roofline(eng, cuda, peak)
+            dom = layer_roofline(cuda, peak, local)
             vocab = mma_vocab_roofline(eng, cuda, peak) if extras else None
         else:
             dom = dict(kern["q6k_lm_head_128256x2048"], traffic=None,
@@ -856,7 +935,7 @@ def run_ours(args):
                          "frac": dom["frac"], "traffic": dom["traffic"], "kernel": dom["kernel"],
                          "peak_source": peak_src,
                          **({k: dom[k] for k in ("us_per_layer", "weight_bytes", "algorithmic_bytes",
-                                                 "traffic_source", "per_projection")} if ragged else
+                                                 "traffic_source", "per_matrix_alone")} if ragged else
                             {"us_per_launch": dom["us_per_launch"]})},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak},
             "cpu_baseline": cpu,

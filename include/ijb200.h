@@ -214,6 +214,49 @@ int ijb_argmax_noalloc(const float *values_dev, int n, int *index_dev, void *str
  * (its errors surface through cuda_check, inferencer.cu:126-128). */
 int ijb_probe_wait_timeout(ijb_engine *engine, uint64_t limit_ns);
 
+/* Timing helper: replays layer 0's four projection launches exactly as a
+ * packed step of n tokens issues them (QKV with RoPE and the K/V cache write,
+ * O with the residual add, gate/up with SiLU, down with the residual add, each
+ * with its activation preparation; no attention), `reps` times in one CUDA
+ * graph, and writes the mean device time of one layer's chain in
+ * milliseconds (CUDA events on the engine's stream).  Sequence 0 must be
+ * empty; its pages take the timed K/V writes and are released afterwards.
+ * The engine's activations are overwritten.  No counterpart in the reference
+ * (a measurement aid for the dominant kernel). */
+int ijb_time_layer_projections(ijb_engine *engine, int n, int reps, float *ms_per_layer);
+
+/* ---- one quantised matrix on the tensor cores, outside an engine ----
+ * For callers that hold one matrix or a slice of one, e.g. each rank's
+ * row slice of a row-split lm_head (the reference's lm_head GEMV,
+ * inferencer.cu:1519-1526, with its argmax, :1063-1099). */
+typedef struct ijb_weight ijb_weight;
+
+/* Prepares rows x cols of GGUF-layout Q4_K / Q6_K blocks at w_dev (16-byte
+ * aligned, on `device`) for ijb_weight_matmul: the same chunked copy and
+ * power-of-two scale ijb_create makes for packed steps (the source may be
+ * freed afterwards). */
+int ijb_weight_create(int type, const void *w_dev, int rows, int cols, int device, ijb_weight **out);
+void ijb_weight_destroy(ijb_weight *weight);
+
+/* y[t][r] = W norm(x[t]) for n tokens (x_dev [n][cols] fp32; y_dev rows
+ * t*y_stride .. +rows), on the INT8 (use_dp4a, the reference's per-32
+ * activation quantisation) or FP32 activation path; with norm_w_dev non-NULL
+ * an RMSNorm with those weights and eps comes first.  With keys_dev non-NULL
+ * it also receives, per token, the packed argmax key of (logit, key_offset +
+ * row) over this matrix's rows with the reference's tie rule: keys of several
+ * row slices combine by taking their maximum, and ijb_keys_to_tokens turns a
+ * key into the token index.  Asynchronous on `stream`; calls on one weight
+ * must not overlap (they share its activation buffer). */
+int ijb_weight_matmul(ijb_weight *weight, const float *x_dev, int n, const float *norm_w_dev, float eps, int use_dp4a,
+                      float *y_dev, long y_stride, int key_offset, unsigned long long *keys_dev, void *stream);
+
+/* IJB_ERR_DEVICE (and clears it) if a kernel of this weight reported a
+ * device error (a bounded wait expired); call after synchronising. */
+int ijb_weight_status(ijb_weight *weight);
+
+/* Packed argmax keys -> token indices (n keys, device memory). */
+int ijb_keys_to_tokens(const unsigned long long *keys_dev, int n, int *tokens_dev, void *stream);
+
 /* Number of kernels the library launched since load (for launch accounting). */
 uint64_t ijb_kernel_launches(void);
 

@@ -336,6 +336,34 @@ void enqueue_trace_quant(ijb_engine *e, int n, const float *x, long x_stride, co
     ++g_launches;
 }
 
+// The four projection launches of layer l for a packed step of n tokens (the
+// step's meta already on the device).
+void enqueue_qkv(ijb_engine *e, int l, int n, cudaStream_t s) {
+    const ijb_model_desc &d = e->d;
+    const auto &L = e->layers[l];
+    char *kbase = static_cast<char *>(e->kv) + l * e->num_pages * e->page_stride * e->kv_elem;
+    const long v_off = static_cast<long>(d.kv_heads) * d.page_size * e->head_dim;
+    const ProjSeg segs[3] = {{L.q, -1, kEpiRopeQ, e->q, d.dim},
+                             {L.k, -1, kEpiRopeKCache, nullptr, 0},
+                             {L.v, -1, kEpiVCache, nullptr, 0}};
+    launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), segs, 3,
+                      kbase, v_off);
+}
+void enqueue_o(ijb_engine *e, int l, int n, cudaStream_t s, bool x16_ready = false) {
+    const ProjSeg o_segs[1] = {{e->layers[l].o, -1, kEpiAdd, e->x, e->d.dim}};
+    launch_projection(e, s, 0, n, e->attn, e->d.dim, nullptr, o_segs, 1, nullptr, 0, x16_ready);
+}
+void enqueue_gateup(ijb_engine *e, int l, int n, cudaStream_t s) {
+    const auto &L = e->layers[l];
+    const ProjSeg segs[1] = {{L.gate, L.up, kEpiSiluPair, e->h, e->d.hidden}};
+    launch_projection(e, s, 0, n, e->x, e->d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), segs, 1,
+                      nullptr, 0);
+}
+void enqueue_down(ijb_engine *e, int l, int n, cudaStream_t s) {
+    const ProjSeg segs[1] = {{e->layers[l].down, -1, kEpiAdd, e->x, e->d.dim}};
+    launch_projection(e, s, 0, n, e->h, e->d.hidden, nullptr, segs, 1, nullptr, 0);
+}
+
 void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool traced = false) {
     const ijb_model_desc &d = e->d;
     const int *tok = e->meta_dev;
@@ -352,13 +380,7 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool t
         if (traced)
             enqueue_trace_quant(e, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), d.dim, l, 0,
                                 s);
-        {
-            const ProjSeg segs[3] = {{L.q, -1, kEpiRopeQ, e->q, d.dim},
-                                     {L.k, -1, kEpiRopeKCache, nullptr, 0},
-                                     {L.v, -1, kEpiVCache, nullptr, 0}};
-            launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), segs,
-                              3, kbase, v_off);
-        }
+        enqueue_qkv(e, l, n, s);
         AttnParams a;
         std::memset(&a, 0, sizeof(a));
         a.q = e->q;
@@ -406,20 +428,13 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool t
         ck(attention_launch(a, s, e->pdl || (n >= e->mma_min_batch && e->attn_pdl)), "attention launch");
         g_launches += attention_kernels(a);
         if (traced) enqueue_trace_quant(e, n, e->attn, d.dim, nullptr, d.dim, l, d.dim, s);
-        launch_projection(e, s, 0, n, e->attn, d.dim, nullptr, o_segs, 1, nullptr, 0, o_fused && !traced);
+        enqueue_o(e, l, n, s, o_fused && !traced);
         if (traced)
             enqueue_trace_quant(e, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), d.dim, l,
                                 2L * d.dim, s);
-        {
-            const ProjSeg segs[1] = {{L.gate, L.up, kEpiSiluPair, e->h, d.hidden}};
-            launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.ffn_norm].data), segs,
-                              1, nullptr, 0);
-        }
+        enqueue_gateup(e, l, n, s);
         if (traced) enqueue_trace_quant(e, n, e->h, d.hidden, nullptr, d.hidden, l, 3L * d.dim, s);
-        {
-            const ProjSeg segs[1] = {{L.down, -1, kEpiAdd, e->x, d.dim}};
-            launch_projection(e, s, 0, n, e->h, d.hidden, nullptr, segs, 1, nullptr, 0);
-        }
+        enqueue_down(e, l, n, s);
         if (traced)  // residual after the layer -> trace_x[token][l]
             ck(cudaMemcpy2DAsync(e->trace_x + static_cast<long>(l) * d.dim, static_cast<size_t>(d.layers) * d.dim * 4,
                                  e->x, static_cast<size_t>(d.dim) * 4, static_cast<size_t>(d.dim) * 4, n,
@@ -945,6 +960,66 @@ int ijb_prefill_traced(ijb_engine *e, const int *tokens, int n, int *next_token,
 
 int ijb_last_step_size(const ijb_engine *e) { return e ? e->last_n : -1; }
 
+int ijb_time_layer_projections(ijb_engine *e, int n, int reps, float *ms_per_layer) {
+    try {
+        require(e != nullptr && ms_per_layer != nullptr, "bad arguments");
+        require(n >= 1 && n <= e->d.max_batch && n <= e->d.context, "n must be 1..max_batch");
+        require(reps >= 1 && reps <= 1000, "reps must be 1..1000");
+        require(e->seq_len[0] == 0 && e->seq_pages[0].empty(),
+                "sequence 0 must be empty (its KV pages receive the timed K/V writes)");
+        ck(cudaSetDevice(e->d.device), "cudaSetDevice");
+        // tokens 0..n-1 of sequence 0 at positions 0..n-1 (their K/V slots are sequence 0's pages)
+        const ijb_model_desc &d = e->d;
+        int *mt = e->meta_host;
+        for (int i = 0; i < n; ++i) {
+            mt[i] = i % d.vocab;
+            mt[d.max_batch + i] = 0;
+            mt[2 * d.max_batch + i] = i;
+            mt[3 * d.max_batch + i] = slot_for(e, 0, i);
+        }
+        ck(cudaMemcpyAsync(e->meta_dev, e->meta_host, 4 * d.max_batch * sizeof(int), cudaMemcpyHostToDevice, e->stream),
+           "meta H2D");
+        cudaGraph_t graph;
+        cudaGraphExec_t exec = nullptr;
+        const uint64_t before = g_launches.load();
+        ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        try {
+            for (int r = 0; r < reps; ++r) {
+                enqueue_qkv(e, 0, n, e->stream);
+                enqueue_o(e, 0, n, e->stream);
+                enqueue_gateup(e, 0, n, e->stream);
+                enqueue_down(e, 0, n, e->stream);
+            }
+        } catch (...) {
+            cudaStreamEndCapture(e->stream, &graph);
+            throw;
+        }
+        ck(cudaStreamEndCapture(e->stream, &graph), "end capture");
+        const uint64_t launches = g_launches.load() - before;
+        cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        ck(ie, "graph instantiate");
+        float ms = 0.f;
+        cudaError_t le = cudaGraphLaunch(exec, e->stream);  // warm-up
+        if (le == cudaSuccess) le = cudaEventRecord(e->ev_start, e->stream);
+        if (le == cudaSuccess) le = cudaGraphLaunch(exec, e->stream);
+        if (le == cudaSuccess) le = cudaEventRecord(e->ev_end, e->stream);
+        if (le == cudaSuccess) le = cudaStreamSynchronize(e->stream);
+        if (le == cudaSuccess) le = cudaEventElapsedTime(&ms, e->ev_start, e->ev_end);
+        cudaGraphExecDestroy(exec);
+        ck(le, "layer timing");
+        g_launches += launches;  // the second replay (the capture counted the first)
+        check_device_status(e);
+        // the timed K/V writes leave sequence 0 holding n positions of no meaning
+        for (int p : e->seq_pages[0]) e->free_pages.push_back(p);
+        e->seq_pages[0].clear();
+        *ms_per_layer = ms / reps;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
 int ijb_seq_prefill(ijb_engine *e, int seq, const int *tokens, int n, int *next_token) {
     try {
         require(e != nullptr && tokens != nullptr && n >= 1, "bad arguments");
@@ -1128,6 +1203,156 @@ int ijb_probe_wait_timeout(ijb_engine *e, uint64_t limit_ns) {
         return IJB_OK;
     } catch (const std::exception &ex) {
         return fail(e, ex);
+    }
+}
+
+}  // extern "C"
+
+struct ijb_weight {
+    int type = 0, rows = 0, cols = 0, device = 0;
+    MmaWeight mma{};
+    uint8_t *x16 = nullptr;
+    float *x_inv = nullptr;
+    uint32_t *status = nullptr;
+};
+
+extern "C" {
+
+int ijb_weight_create(int type, const void *w_dev, int rows, int cols, int device, ijb_weight **out) {
+    std::unique_ptr<ijb_weight> w(new ijb_weight());
+    uint8_t *unit = nullptr;
+    try {
+        require(out != nullptr && w_dev != nullptr, "null argument");
+        require(type == IJB_TYPE_Q4_K || type == IJB_TYPE_Q6_K, "type must be Q4_K or Q6_K");
+        require(rows >= 1 && cols > 0 && cols % 256 == 0 && cols <= kMaxCols, "bad matrix shape");
+        require(reinterpret_cast<uintptr_t>(w_dev) % 16 == 0, "weights must be 16-byte aligned");
+        ck(cudaSetDevice(device), "cudaSetDevice");
+        ck(mma_prepare(), "tensor-core GEMM attributes");
+        w->type = type;
+        w->rows = rows;
+        w->cols = cols;
+        w->device = device;
+        // power-of-two scale from the GGUF blocks, as ijb_create does
+        int *bits = dev_alloc<int>(1, "scale scan");
+        cudaError_t se = mma_scale_scan_launch(type, static_cast<const uint8_t *>(w_dev),
+                                               static_cast<long>(rows) * (cols / 256), bits, nullptr);
+        unsigned int hb = 0;
+        if (se == cudaSuccess) se = cudaMemcpy(&hb, bits, 4, cudaMemcpyDeviceToHost);
+        cudaFree(bits);
+        ck(se, "weight scale scan");
+        float maxw;
+        std::memcpy(&maxw, &hb, 4);
+        int ex = 0;
+        if (maxw > 0.f) std::frexp(maxw, &ex);
+        w->mma.scale_exp = maxw > 0.f ? std::max(-60, std::min(60, 15 - ex)) : 0;
+        w->mma.nblocks = cols / 256;
+        const uint8_t *src = static_cast<const uint8_t *>(w_dev);
+        long row_bytes = cols / 256 * kQ4Bytes;
+        if (type == IJB_TYPE_Q6_K) {  // the chunked copy reads the Q6_K unit layout
+            row_bytes = q6_planar_row_bytes(cols);
+            unit = dev_alloc<uint8_t>(static_cast<size_t>(rows) * row_bytes, "Q6_K unit layout");
+            ck(repack_q6_launch(w_dev, unit, rows, cols, nullptr), "Q6_K repack");
+            src = unit;
+        }
+        uint8_t *c = dev_alloc<uint8_t>(static_cast<size_t>(mma_tile_bytes(type, rows, cols)), "tensor-core weight copy");
+        w->mma.chunks = c;
+        ck(mma_tile_repack_launch(type, src, row_bytes, rows, cols, c, nullptr), "tensor-core weight copy");
+        ck(cudaDeviceSynchronize(), "weight prepare");
+        cudaFree(unit);
+        unit = nullptr;
+        w->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
+        ck(cudaMemset(w->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
+        w->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
+        w->status = dev_alloc<uint32_t>(1, "status");
+        ck(cudaMemset(w->status, 0, 4), "status clear");
+        g_launches += 3 + (type == IJB_TYPE_Q6_K ? 1 : 0);
+        *out = w.release();
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        cudaFree(unit);
+        ijb_weight_destroy(w.release());
+        return fail(nullptr, ex);
+    }
+}
+
+void ijb_weight_destroy(ijb_weight *w) {
+    if (!w) return;
+    cudaSetDevice(w->device);
+    cudaFree(const_cast<uint8_t *>(w->mma.chunks));
+    cudaFree(w->x16);
+    cudaFree(w->x_inv);
+    cudaFree(w->status);
+    delete w;
+}
+
+int ijb_weight_matmul(ijb_weight *w, const float *x_dev, int n, const float *norm_w_dev, float eps, int use_dp4a,
+                      float *y_dev, long y_stride, int key_offset, unsigned long long *keys_dev, void *stream) {
+    try {
+        require(w != nullptr && x_dev != nullptr && y_dev != nullptr, "null argument");
+        require(n >= 1 && y_stride >= w->rows && key_offset >= 0, "bad matmul arguments");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (keys_dev) ck(cudaMemsetAsync(keys_dev, 0, static_cast<size_t>(n) * 8, s), "keys clear");
+        const int nb = w->cols / 256;
+        for (int t0 = 0; t0 < n; t0 += kMmaMaxN) {
+            const int tn = std::min(kMmaMaxN, n - t0);
+            const int n_pad = (tn + 15) / 16 * 16;
+            ck(mma_prep_launch(x_dev + static_cast<long>(t0) * w->cols, w->cols, norm_w_dev, eps, w->cols, tn, n_pad,
+                               use_dp4a ? 1 : 0, w->x16, w->x_inv, s, false),
+               "activation prep launch");
+            MmaParams m;
+            std::memset(&m, 0, sizeof(m));
+            m.w[0] = w->mma;
+            MmaSeg &sg = m.seg[0];
+            sg.w0 = 0;
+            sg.w1 = -1;
+            sg.type = w->type;
+            sg.rows = w->rows;
+            sg.tile0 = 0;
+            sg.ntiles = (w->rows + kMmaTileM - 1) / kMmaTileM;
+            sg.epi = keys_dev ? kEpiLogitsArgmax : kEpiStore;
+            sg.out = y_dev + static_cast<long>(t0) * y_stride;
+            sg.out_stride = y_stride;
+            sg.key_offset = key_offset;
+            m.nseg = 1;
+            m.total_tiles = sg.ntiles;
+            m.cols = w->cols;
+            m.batch = tn;
+            m.n_pad = n_pad;
+            m.x16 = w->x16;
+            m.x_inv = w->x_inv;
+            m.argmax_keys = keys_dev ? keys_dev + t0 : nullptr;
+            m.status = w->status;
+            m.ksplit = mma_choose_split(m.total_tiles, nb, 8, 1, &m.bps);
+            ck(mma_gemm_launch(m, s, false), "tensor-core GEMM launch");
+            g_launches += 2;
+        }
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(nullptr, ex);
+    }
+}
+
+int ijb_weight_status(ijb_weight *w) {
+    if (!w) return IJB_ERR_INVALID;
+    uint32_t st = 0;
+    if (cudaMemcpy(&st, w->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return IJB_ERR_CUDA;
+    if (st) {
+        cudaMemset(w->status, 0, 4);
+        set_thread_error("kernel reported device error code " + std::to_string(st));
+        return IJB_ERR_DEVICE;
+    }
+    return IJB_OK;
+}
+
+int ijb_keys_to_tokens(const unsigned long long *keys_dev, int n, int *tokens_dev, void *stream) {
+    try {
+        require(keys_dev && tokens_dev && n >= 1, "bad arguments");
+        ck(keys_to_tokens_launch(keys_dev, n, tokens_dev, static_cast<cudaStream_t>(stream), false),
+           "argmax decode launch");
+        ++g_launches;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(nullptr, ex);
     }
 }
 

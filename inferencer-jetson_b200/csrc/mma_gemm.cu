@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
             epi_rows(p, e, tk, stage, r, t_lo, t_hi, bulk);
             if (sg.epi == kEpiLogitsArgmax) {
                 named_bar_sync(1, 128);
-                epi_argmax(stage, tk, sg.row_offset + row0, count, t_lo, t_hi);
+                epi_argmax(stage, tk, sg.key_offset + sg.row_offset + row0, count, t_lo, t_hi);
             }
             if (bulk) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

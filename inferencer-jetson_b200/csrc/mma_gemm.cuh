@@ -49,6 +49,7 @@ struct MmaSeg {
     float *out;
     long out_stride;
     int row_offset;
+    int key_offset;    // added to the row index of the argmax keys (a row slice of a larger matrix)
 };
 
 struct MmaParams {

@@ -80,6 +80,12 @@ def load():
         "ijb_forward_traced": ([P, I, I, I, IP, P, P], I),
         "ijb_prefill_traced": ([P, IP, I, IP, P, P, P], I),
         "ijb_last_step_size": ([P], I),
+        "ijb_time_layer_projections": ([P, I, I, ctypes.POINTER(ctypes.c_float)], I),
+        "ijb_weight_create": ([I, P, I, I, I, ctypes.POINTER(P)], I),
+        "ijb_weight_destroy": ([P], None),
+        "ijb_weight_matmul": ([P, P, I, P, ctypes.c_float, I, P, L64, I, P, P], I),
+        "ijb_weight_status": ([P], I),
+        "ijb_keys_to_tokens": ([P, I, P, P], I),
         "ijb_kernel_launches": ([], ctypes.c_uint64),
         "ijb_last_step_ms": ([P], ctypes.c_float),
     }
