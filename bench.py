@@ -377,17 +377,22 @@ class RaggedServer:
 
 
 GEMV_CASES = (("q4k_ffn_gate_8192x2048", 12, 8192, 2048), ("q6k_lm_head_128256x2048", 14, 128256, 2048))
+# BASELINE config 1 at batch 8 (the CUDA-core GEMV's largest batch; batch 64 is the vocab projection)
+GEMV_B8_CASE = ("q6k_lm_head_128256x2048_b8", 14, 128256, 2048, 8)
 
 
 def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
     """The CUDA-core GEMV (ijb_gemv_kernel, the batch-1 projection) timed
     alone with CUDA events on its stream: the 1B ffn_gate Q4_K shape (BASELINE
-    config 0) and the Q6_K lm_head (config 1), weights rotated over > 4x L2."""
+    config 0) and the Q6_K lm_head (config 1; a case may give a batch, up to
+    8), weights rotated over > 4x L2."""
     import torch
     L = ijblib.load()
     out = {}
     rng = np.random.default_rng(0)
-    for name, qtype, rows, cols in cases:
+    for case in cases:
+        name, qtype, rows, cols = case[:4]
+        batch = case[4] if len(case) > 4 else 1
         w = synth.quant_matrix(rng, qtype, rows, cols)
         wd = torch.from_numpy(w).to(cuda)
         if qtype == 14:
@@ -398,25 +403,25 @@ def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
         nbytes = wd.numel()
         copies = max(1, int(np.ceil(4 * 126e6 / nbytes)))
         ws = [wd] + [wd.clone() for _ in range(copies - 1)]
-        x = torch.randn(cols, device=cuda)
-        y = torch.empty(rows, device=cuda)
+        x = torch.randn(batch, cols, device=cuda)
+        y = torch.empty(batch, rows, device=cuda)
         stream = torch.cuda.current_stream().cuda_stream
         for i in range(3 * copies):
-            ijblib.check(L.ijb_gemv(qtype, ws[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), cols, rows, 1, 1,
+            ijblib.check(L.ijb_gemv(qtype, ws[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), cols, rows, batch, 1,
                                     ctypes.c_void_p(stream)))
         iters = max(iters_min, 4 * copies)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         a.record()
         for i in range(iters):
-            ijblib.check(L.ijb_gemv(qtype, ws[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), cols, rows, 1, 1,
+            ijblib.check(L.ijb_gemv(qtype, ws[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), cols, rows, batch, 1,
                                     ctypes.c_void_p(stream)))
         b.record()
         torch.cuda.synchronize()
         ms = a.elapsed_time(b) / iters
-        algo = nbytes + cols * 4 + rows * 4
+        algo = nbytes + batch * (cols * 4 + rows * 4)
         out[name] = {"us_per_launch": ms * 1e3, "algorithmic_bytes": algo, "gbs": algo / (ms * 1e-3) / 1e9,
-                     "frac": algo / (ms * 1e-3) / 1e9 / peak, "rotated_copies": copies}
+                     "frac": algo / (ms * 1e-3) / 1e9 / peak, "rotated_copies": copies, "batch": batch}
         del ws, wd
         torch.cuda.empty_cache()
     return out
@@ -878,7 +883,8 @@ def run_ours(args):
     result = None
     if rank == 0:
         extras = args.workload == "ragged64" and not args.no_extras
-        kern = gemv_roofline(cuda, peak) if (extras or not ragged) else None
+        kern = gemv_roofline(cuda, peak, GEMV_CASES + ((GEMV_B8_CASE,) if extras else ())) if (extras or not ragged) \
+            else None
         if big:
             # KV bytes are ~97% of this step: the roofline is the step's own
             dom = {"gbs": step_gbs, "frac": step_gbs / peak, "traffic": None,

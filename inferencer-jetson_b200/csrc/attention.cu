@@ -336,6 +336,13 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 // Byte offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile
 // (1024-byte aligned): the chunk index is XORed with the row's low 3 bits.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
+// The same in a tile of CH rows whose rows are wider than the 128-byte swizzle
+// span (head_dim 128: 256 bytes): it is stored as consecutive 128-byte-wide
+// halves [half][CH rows][128 B], chunk c of a row in half c / 8.
+template <int CH>
+__device__ __forceinline__ uint32_t swz_wide(int r, int c) {
+    return static_cast<uint32_t>((c >> 3) * CH * 128) + swz(r, c & 7);
+}
 // mma.m16n8k16 with all four A registers (rows 8-15 in use).
 __device__ __forceinline__ void mma16816_a4(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -356,22 +363,28 @@ __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
 // One chunk of up to 16*MT positions on the tensor cores with positions as
 // the MMA rows and the group's query heads as its 8 columns (G <= 8):
 //   S^T[pos][head] = K[pos][:] . Q^T           (MT tiles of 16 positions)
-//   O^T[dim][head] += V^T[dim][pos] . P^T      (4 tiles of 16 dims)
+//   O^T[dim][head] += V^T[dim][pos] . P^T      (HD/16 tiles of 16 dims)
 // The lane holds heads 2(lane%4) and 2(lane%4)+1: its online-softmax state
 // m[2], l[2]; the max and sum run over the 8 lanes of equal lane%4.  P^T
 // comes from the score accumulators through movmatrix transposes.  Q and P
 // enter as fp16 hi + lo pairs (two MMAs each), so only the cache's own fp16
 // rounding remains; softmax is fp32 with __expf.  kt / vt: the chunk's
 // 128-byte-swizzled K and V tiles (V rows past cnt are zeroed here).
-template <int MT>
-__device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, float scale, const uint32_t (&qb)[4][2][2],
-                                             float (&o)[4][4], float (&m)[2], float (&l)[2], int lane) {
-    constexpr int CH = 16 * MT;  // positions of the chunk
+template <int HD, int MT>
+__device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, float scale,
+                                             const uint32_t (&qb)[HD / 16][2][2], float (&o)[HD / 16][4],
+                                             float (&m)[2], float (&l)[2], int lane) {
+    constexpr int CH = 16 * MT;   // positions of the chunk
+    constexpr int KS = HD / 16;   // k-steps of the scores, dim tiles of the output
     const int gid = lane >> 2, mi = lane >> 3;
     if (cnt < CH) {  // V rows past the last position: zero (their weights are zero, keep them finite)
         for (int r = cnt + (lane >> 3); r < CH; r += 4)
-            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vt + r * 128 + (lane & 7) * 16), "r"(0u)
-                         : "memory");
+#pragma unroll
+            for (int hf = 0; hf < HD / 64; ++hf)
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vt + hf * CH * 128 + r * 128 +
+                                                                            (lane & 7) * 16),
+                             "r"(0u)
+                             : "memory");
         __syncwarp();
     }
     // ---- scores: sc[mt] = S^T rows 16mt + gid (+8), heads 2(lane%4) (+1)
@@ -380,9 +393,9 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
     for (int mt = 0; mt < MT; ++mt) {
         sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < KS; ++kk) {
             uint32_t ka[4];
-            ldsm_x4(kt + swz(16 * mt + 8 * (mi & 1) + (lane & 7), 2 * kk + (mi >> 1)), ka);
+            ldsm_x4(kt + swz_wide<CH>(16 * mt + 8 * (mi & 1) + (lane & 7), 2 * kk + (mi >> 1)), ka);
             mma16816_a4(sc[mt], ka, qb[kk][0][0], qb[kk][0][1]);
             mma16816_a4(sc[mt], ka, qb[kk][1][0], qb[kk][1][1]);
         }
@@ -424,7 +437,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
         l[e] = fmaf(l[e], alpha[e], rs[e]);
     }
 #pragma unroll
-    for (int md = 0; md < 4; ++md) {
+    for (int md = 0; md < KS; ++md) {
         o[md][0] *= alpha[0];
         o[md][1] *= alpha[1];
         o[md][2] *= alpha[0];
@@ -440,9 +453,9 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
         const uint32_t lt = movm_t(pack_h2(sc[kp][0] - ft.x, sc[kp][1] - ft.y));
         const uint32_t lb = movm_t(pack_h2(sc[kp][2] - fb.x, sc[kp][3] - fb.y));
 #pragma unroll
-        for (int md = 0; md < 4; ++md) {
+        for (int md = 0; md < KS; ++md) {
             uint32_t va[4];
-            ldsm_x4_t(vt + swz(16 * kp + 8 * (mi >> 1) + (lane & 7), 2 * md + (mi & 1)), va);
+            ldsm_x4_t(vt + swz_wide<CH>(16 * kp + 8 * (mi >> 1) + (lane & 7), 2 * md + (mi & 1)), va);
             mma16816_a4(o[md], va, bt, bb);
             mma16816_a4(o[md], va, lt, lb);
         }
@@ -452,7 +465,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 // ------------------------------------------------ streaming variant --
 //
 // fp16 cache, head_dim 64, tensor-core chunks as above, as a persistent
-// kernel: one CTA of kStreamWarps independent warps per SM.  The work is cut
+// kernel: one CTA of stream_warps<HD>() independent warps per SM.  The work is cut
 // into items of up to kAttnItem positions of one (token, kv head): a warp's
 // first item is fixed by its index, the next ones come from a device-wide
 // counter (the request for the following item is in flight while the current
@@ -481,7 +494,19 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 constexpr int kStreamWarps = IJB_STREAM_WARPS;
 constexpr int kStreamStages = IJB_STREAM_STAGES;
 constexpr int kStreamChunk = IJB_STREAM_CHUNK;          // positions per chunk (per stage)
-constexpr int kMmaAttnTile = kStreamChunk * 128;       // one K or V tile: kStreamChunk rows of 64 fp16
+// head_dim 128: a stage's K and V tiles take twice the bytes, so six warps
+// fit the shared memory at two stages each
+constexpr int kStreamWarps128 = 6;
+template <int HD>
+__host__ __device__ constexpr int stream_warps() { return HD == 64 ? kStreamWarps : kStreamWarps128; }
+// one K or V tile: kStreamChunk rows of HD fp16, as HD / 64 swizzled 128-byte-wide halves
+template <int HD>
+__host__ __device__ constexpr int stream_tile() { return kStreamChunk * HD * 2; }
+template <int HD>
+__host__ __device__ constexpr int stream_smem() {
+    return stream_warps<HD>() * IJB_STREAM_STAGES * 2 * stream_tile<HD>() + 1024;  // + alignment slack
+}
+static_assert(stream_smem<128>() + 8 * 1024 <= 227 * 1024, "head_dim-128 streaming attention shared memory");
 constexpr int kStreamQueue = kStreamStages + 1;  // items a warp's in-flight chunks can span, plus the one in use
 #ifndef IJB_ATTN_ITEM
 #define IJB_ATTN_ITEM 128
@@ -491,27 +516,28 @@ constexpr int kItemPages = kAttnItem / 8;        // page ids of an item (page_si
 static_assert(kStreamChunk % 16 == 0 && kStreamChunk <= 64 && kAttnItem % kStreamChunk == 0 && kAttnItem <= 256,
               "streaming attention shape");
 constexpr int kStreamMaxBatch = 256;
-constexpr int kStreamSmem = kStreamWarps * kStreamStages * 2 * kMmaAttnTile + 1024;  // + alignment slack
 
 struct StreamItem {
     int b, h, j, p0, p1, nch, pad0, pad1;
     int pg[kItemPages];
 };
 
-template <int G>
-__global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_kernel(const __grid_constant__ AttnParams p) {
-    constexpr int HD = 64, ST = kStreamStages, QN = kStreamQueue;
+template <int HD, int G>
+__global__ void __launch_bounds__(stream_warps<HD>() * 32, 1)
+    ijb_attention_stream_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int ST = kStreamStages, QN = kStreamQueue, SW = stream_warps<HD>(), TILE = stream_tile<HD>();
+    constexpr int KS = HD / 16, NH = HD / 64;  // k-steps / dim tiles; 128-byte halves of a row
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;  // swizzled TMA tiles need 1024-byte alignment
-    const uint32_t wtiles = base + static_cast<uint32_t>(warp * ST * 2 * kMmaAttnTile);  // [ST][K, V]
+    const uint32_t wtiles = base + static_cast<uint32_t>(warp * ST * 2 * TILE);  // [ST][K, V]
     __shared__ int first_s[kStreamMaxBatch + 1];  // first work item of each token (prefix sums)
     __shared__ int nj_s[kStreamMaxBatch];         // items per kv head of each token
     __shared__ int seq_s[kStreamMaxBatch];
     __shared__ int npos_s[kStreamMaxBatch];
-    __shared__ StreamItem q_s[kStreamWarps][QN];
-    __shared__ __align__(8) uint64_t bar[kStreamWarps][ST];
+    __shared__ StreamItem q_s[SW][QN];
+    __shared__ __align__(8) uint64_t bar[SW][ST];
     __shared__ uint32_t cta_abort;
 
     if (threadIdx.x == 0) cta_abort = 0u;
@@ -551,13 +577,13 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
     const int ps = p.page_size;
 
     // this warp's next item into queue slot `slot` (warp-uniform)
-    const int nwarps = static_cast<int>(gridDim.x) * kStreamWarps;
+    const int nwarps = static_cast<int>(gridDim.x) * SW;
     bool first = true;
     int pending = 0;  // lane 0: the counter value for the following item (request in flight)
     auto grab = [&](int slot) -> bool {
         int id;
         if (first) {
-            id = static_cast<int>(blockIdx.x) * kStreamWarps + warp;
+            id = static_cast<int>(blockIdx.x) * SW + warp;
             first = false;
         } else {
             id = __shfl_sync(0xffffffffu, pending, 0) + nwarps;
@@ -590,14 +616,17 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
     auto issue = [&](const StreamItem &it, int c, int stage) {
         const int t0 = it.p0 + c * kStreamChunk;
         const int npg = (min(kStreamChunk, it.p1 - t0) + ps - 1) / ps;
-        const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
+        const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * TILE), vt = kt + TILE;
         uint64_t *bb = &bar[warp][stage];
-        if (lane == 0) mbar_arrive_expect_tx(bb, 2u * npg * ps * 128u);
+        if (lane == 0) mbar_arrive_expect_tx(bb, 2u * npg * ps * 128u * NH);
         __syncwarp();
-        if (lane < 2 * npg) {  // one copy per lane: page lane/2, K (even lanes) or V (odd)
-            const int j = lane >> 1, page = it.pg[(t0 - it.p0) / ps + j];
-            if (lane & 1) tma_load_3d(vt + j * ps * 128, &p.kv_map, 0, (p.kv_heads + it.h) * ps, page, bb);
-            else tma_load_3d(kt + j * ps * 128, &p.kv_map, 0, it.h * ps, page, bb);
+        if (lane < 2 * npg * NH) {
+            // one copy per lane: the 128-byte-wide half lane % NH of page (lane / NH) / 2,
+            // K (even (lane / NH)) or V (odd)
+            const int hf = lane % NH, kv = (lane / NH) & 1, j = lane / (2 * NH);
+            const int page = it.pg[(t0 - it.p0) / ps + j];
+            const uint32_t dst = (kv ? vt : kt) + static_cast<uint32_t>(hf * kStreamChunk * 128 + j * ps * 128);
+            tma_load_3d(dst, &p.kv_map, 64 * hf, (kv ? p.kv_heads + it.h : it.h) * ps, page, bb);
         }
     };
 
@@ -605,8 +634,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
     int is_item = 0, is_ch = 0;  // issue cursor
     int issued = 0, done = 0, cc = 0;
     bool exhausted = false;
-    uint32_t qa[4][2][2];
-    float o[4][4];  // O^T: dims 16md + gid (+8), heads 2tig (+1)
+    uint32_t qa[KS][2][2];
+    float o[KS][4];  // O^T: dims 16md + gid (+8), heads 2tig (+1)
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     // keep ST chunks of the warp's stream in flight (warp-uniform)
     auto refill = [&]() {
@@ -631,13 +660,13 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
         }
     };
     // the query of queued item k, raw (the MMA fragments are built when it starts)
-    float qv[4][4];
+    float qv[KS][4];
     int qv_item = -1;
     auto load_q = [&](int k) {
         const StreamItem &it = q_s[warp][k % QN];
         const float *q = p.q + static_cast<long>(it.b) * p.q_stride + static_cast<long>(it.h) * G * HD;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < KS; ++kk) {
             float2 v0 = make_float2(0.f, 0.f), v1 = v0;
             if (gid < G) {
                 v0 = *reinterpret_cast<const float2 *>(q + gid * HD + 16 * kk + 2 * tig);
@@ -658,7 +687,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
             // column gid = head gid (zero for gid >= G), [k-step][hi, lo][b0, b1]
             if (qv_item != q_head) load_q(q_head);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
+            for (int kk = 0; kk < KS; ++kk) {
                 const __half2 h0 = __floats2half2_rn(qv[kk][0], qv[kk][1]), h1 = __floats2half2_rn(qv[kk][2], qv[kk][3]);
                 const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
                 qa[kk][0][0] = *reinterpret_cast<const uint32_t *>(&h0);
@@ -667,15 +696,15 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
                 qa[kk][1][1] = pack_h2(qv[kk][2] - f1.x, qv[kk][3] - f1.y);
             }
 #pragma unroll
-            for (int md = 0; md < 4; ++md) o[md][0] = o[md][1] = o[md][2] = o[md][3] = 0.f;
+            for (int md = 0; md < KS; ++md) o[md][0] = o[md][1] = o[md][2] = o[md][3] = 0.f;
             m[0] = m[1] = -INFINITY;
             l[0] = l[1] = 0.f;
         }
         const int stage = done % ST;
         mbar_wait_bounded(&bar[warp][stage], (done / ST) & 1, p.status, &cta_abort);
-        const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * kMmaAttnTile), vt = kt + kMmaAttnTile;
+        const uint32_t kt = wtiles + static_cast<uint32_t>(stage * 2 * TILE), vt = kt + TILE;
         const int t0 = it.p0 + cc * kStreamChunk;
-        attn_chunk_t<kStreamChunk / 16>(kt, vt, min(kStreamChunk, it.p1 - t0), p.scale, qa, o, m, l, lane);
+        attn_chunk_t<HD, kStreamChunk / 16>(kt, vt, min(kStreamChunk, it.p1 - t0), p.scale, qa, o, m, l, lane);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic accesses before TMA refills the stage
         __syncwarp();
         ++done;
@@ -694,7 +723,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
                 float *out = p.out + static_cast<long>(b) * p.out_stride + (static_cast<long>(h) * G + 2 * tig + e) * HD;
                 const float inv = 1.f / l[e];
 #pragma unroll
-                for (int md = 0; md < 4; ++md) {
+                for (int md = 0; md < KS; ++md) {
                     out[16 * md + gid] = o[md][e] * inv;
                     out[16 * md + gid + 8] = o[md][2 + e] * inv;
                 }
@@ -711,7 +740,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
                 rec[1] = l[e];
             }
 #pragma unroll
-            for (int md = 0; md < 4; ++md) {
+            for (int md = 0; md < KS; ++md) {
                 rec[2 + 16 * md + gid] = o[md][e];
                 rec[2 + 16 * md + gid + 8] = o[md][2 + e];
             }
@@ -731,15 +760,15 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) ijb_attention_stream_ker
 }
 
 // One CTA per token.  Each warp merges the items of one kv head of a token
-// whose sequence spans more than one item: lane s holds item s's max and sum
-// (at most 32 items), the weights exp(m_s - M) come from a warp max, then each
+// whose sequence spans more than one item: lane s holds the max and sum of
+// items s and s + 32 (at most 64 items), the weights exp(m_s - M) come from a warp max, then each
 // lane sums two output dims over the items, KB items of every head per round
 // of loads.  When the O projection runs on the tensor cores (x16 set), the CTA
 // then builds the token's fp16 activation row for it (mma_prep_token), which
 // takes the place of the projection's own prep launch.
-template <int G>
+template <int HD, int G>
 __global__ void __launch_bounds__(256) ijb_attention_finish_kernel(const __grid_constant__ AttnParams p) {
-    constexpr int HD = 64, KB = G >= 8 ? 4 : 8;
+    constexpr int KB = G * HD >= 512 ? 4 : 8, NH = HD / 64;  // items per round of loads; dim pairs per lane
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -747,40 +776,55 @@ __global__ void __launch_bounds__(256) ijb_attention_finish_kernel(const __grid_
     const int nsplit = b < p.batch ? (p.tok_pos[b] + kAttnItem) / kAttnItem : 0;
     for (int h = warp; nsplit > 1 && h < p.kv_heads; h += 8) {
         const float *part = p.partial + ((static_cast<long>(b) * p.heads + h * G) * p.max_splits) * (HD + 2);
-        float fg[G], Lg[G];
-        float2 O[G];
+        // lane s holds items s and s + 32 (up to 64 items)
+        float fg[G], fg2[G], Lg[G];
+        float2 O[G][NH];  // dims 2 lane + 64 hf (+1)
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             const float *recs = part + static_cast<long>(g) * p.max_splits * (HD + 2);
             const float ms = lane < nsplit ? recs[lane * (HD + 2)] : -INFINITY;
             const float ls = lane < nsplit ? recs[lane * (HD + 2) + 1] : 0.f;
-            const float M = warp_max(ms);
+            const float ms2 = lane + 32 < nsplit ? recs[(lane + 32) * (HD + 2)] : -INFINITY;
+            const float ls2 = lane + 32 < nsplit ? recs[(lane + 32) * (HD + 2) + 1] : 0.f;
+            const float M = warp_max(fmaxf(ms, ms2));
             fg[g] = lane < nsplit ? __expf(ms - M) : 0.f;
-            Lg[g] = warp_sum(fg[g] * ls);
-            O[g] = make_float2(0.f, 0.f);
+            fg2[g] = lane + 32 < nsplit ? __expf(ms2 - M) : 0.f;
+            Lg[g] = warp_sum(fg[g] * ls + fg2[g] * ls2);
+#pragma unroll
+            for (int hf = 0; hf < NH; ++hf) O[g][hf] = make_float2(0.f, 0.f);
         }
         for (int k0 = 0; k0 < nsplit; k0 += KB) {
-            float2 v[G][KB];
+            float2 v[G][KB][NH];
 #pragma unroll
             for (int g = 0; g < G; ++g)
 #pragma unroll
                 for (int k = 0; k < KB; ++k)
-                    v[g][k] = k0 + k < nsplit ? reinterpret_cast<const float2 *>(
-                                                    part + (static_cast<long>(g) * p.max_splits + k0 + k) * (HD + 2) + 2)[lane]
-                                              : make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int hf = 0; hf < NH; ++hf)
+                        v[g][k][hf] = k0 + k < nsplit
+                                          ? reinterpret_cast<const float2 *>(
+                                                part + (static_cast<long>(g) * p.max_splits + k0 + k) * (HD + 2) + 2)
+                                                [lane + 32 * hf]
+                                          : make_float2(0.f, 0.f);
 #pragma unroll
             for (int g = 0; g < G; ++g)
 #pragma unroll
                 for (int k = 0; k < KB; ++k) {
-                    const float fk = __shfl_sync(0xffffffffu, fg[g], (k0 + k) & 31);
-                    O[g].x = fmaf(v[g][k].x, fk, O[g].x);
-                    O[g].y = fmaf(v[g][k].y, fk, O[g].y);
+                    const float fk = __shfl_sync(0xffffffffu, k0 + k < 32 ? fg[g] : fg2[g], (k0 + k) & 31);
+#pragma unroll
+                    for (int hf = 0; hf < NH; ++hf) {
+                        O[g][hf].x = fmaf(v[g][k][hf].x, fk, O[g][hf].x);
+                        O[g][hf].y = fmaf(v[g][k][hf].y, fk, O[g][hf].y);
+                    }
                 }
         }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             float *out = p.out + static_cast<long>(b) * p.out_stride + (static_cast<long>(h) * G + g) * HD;
-            *reinterpret_cast<float2 *>(out + 2 * lane) = make_float2(O[g].x / Lg[g], O[g].y / Lg[g]);
+#pragma unroll
+            for (int hf = 0; hf < NH; ++hf)
+                *reinterpret_cast<float2 *>(out + 2 * lane + 64 * hf) =
+                    make_float2(O[g][hf].x / Lg[g], O[g][hf].y / Lg[g]);
         }
     }
     if (p.x16) {
@@ -789,24 +833,24 @@ __global__ void __launch_bounds__(256) ijb_attention_finish_kernel(const __grid_
     }
 }
 
-template <int G>
+template <int HD, int G>
 static cudaError_t launch_attn_stream(const AttnParams &p, cudaStream_t stream, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.num_ctas);
-    cfg.blockDim = dim3(kStreamWarps * 32);
-    cfg.dynamicSmemBytes = kStreamSmem;
+    cfg.blockDim = dim3(stream_warps<HD>() * 32);
+    cfg.dynamicSmemBytes = stream_smem<HD>();
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, ijb_attention_stream_kernel<G>, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, ijb_attention_stream_kernel<HD, G>, p);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(p.x16 ? p.n_pad : p.batch);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&cfg, ijb_attention_finish_kernel<G>, p);
+    return cudaLaunchKernelEx(&cfg, ijb_attention_finish_kernel<HD, G>, p);
 }
 
 typedef CUresult (*EncodeTiledFnA)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -815,7 +859,7 @@ typedef CUresult (*EncodeTiledFnA)(CUtensorMap *, CUtensorMapDataType, cuuint32_
 
 int attention_make_kv_map(CUtensorMap *map, const void *layer_base, int head_dim, int kv_heads, int page_size,
                           long page_stride_elems, long num_pages) {
-    if (head_dim != 64 || (reinterpret_cast<uintptr_t>(layer_base) & 15)) return -1;
+    if ((head_dim != 64 && head_dim != 128) || (reinterpret_cast<uintptr_t>(layer_base) & 15)) return -1;
     static EncodeTiledFnA fn = nullptr;
     if (!fn) {
         void *ptr = nullptr;
@@ -828,7 +872,9 @@ int attention_make_kv_map(CUtensorMap *map, const void *layer_base, int head_dim
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(2 * kv_heads * page_size),
                           static_cast<cuuint64_t>(num_pages)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * 2), static_cast<cuuint64_t>(page_stride_elems * 2)};
-    cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(page_size), 1};
+    // one 128-byte-wide box (64 fp16) per copy: the 128-byte swizzle span; a
+    // head_dim-128 row is fetched as two boxes at x = 0 and x = 64
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(page_size), 1};
     cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(layer_base), dims, strides, box,
                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -873,13 +919,13 @@ static cudaError_t attention_launch_t(const AttnParams &p, dim3 grid, cudaStream
     return cudaErrorInvalidValue;
 }
 
-// The streaming kernel serves fp16 caches with head_dim 64 up to 32 work items
-// (4096 positions) per sequence and kStreamMaxBatch tokens; anything else, or a
+// The streaming kernel serves fp16 caches with head_dim 64 or 128 up to 64 work items
+// (8192 positions) per sequence and kStreamMaxBatch tokens; anything else, or a
 // G it is not built for, goes to the CUDA-core split kernel.
 static bool stream_path(const AttnParams &p) {
     const int G = p.kv_heads > 0 ? p.heads / p.kv_heads : 0;
-    return p.has_map && p.head_dim == 64 && !p.kv_f32 && p.work && p.num_ctas >= 1 && p.batch <= kStreamMaxBatch &&
-           p.max_splits <= 32 && (G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8) && G * p.kv_heads == p.heads &&
+    return p.has_map && (p.head_dim == 64 || p.head_dim == 128) && !p.kv_f32 && p.work && p.num_ctas >= 1 && p.batch <= kStreamMaxBatch &&
+           p.max_splits <= 64 && (G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8) && G * p.kv_heads == p.heads &&
            p.page_size <= kStreamChunk && kStreamChunk % p.page_size == 0;  // a chunk is whole pages
 }
 
@@ -906,15 +952,23 @@ static cudaError_t set_attrs_t() {
     return cudaSuccess;
 }
 
+template <int HD>
+static cudaError_t set_stream_attrs() {
+    cudaError_t e;
+    const int smem = stream_smem<HD>();
+    if ((e = cudaFuncSetAttribute(ijb_attention_stream_kernel<HD, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<HD, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<HD, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+        return e;
+    return cudaSuccess;
+}
+
 cudaError_t attention_prepare() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(ijb_attention_stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)) ||
-        (e = cudaFuncSetAttribute(ijb_attention_stream_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem)))
-        return e;
+    if ((e = set_stream_attrs<64>()) || (e = set_stream_attrs<128>())) return e;
     e = set_attrs_t<__half>();
     return e != cudaSuccess ? e : set_attrs_t<float>();
 }
@@ -924,15 +978,24 @@ cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
         return cudaErrorInvalidValue;
     if (p.max_splits * kAttnItem < 1) return cudaErrorInvalidValue;
     if (stream_path(p)) {
-        if (p.x16 && (p.n_pad < p.batch || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.heads * 64 > kMaxCols))
+        if (p.x16 && (p.n_pad < p.batch || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.heads * p.head_dim > kMaxCols))
             return cudaErrorInvalidValue;
         const int G = p.heads / p.kv_heads;
-        if (G == 4) return launch_attn_stream<4>(p, stream, pdl);
-        if (G == 8) return launch_attn_stream<8>(p, stream, pdl);
-        if (G == 2) return launch_attn_stream<2>(p, stream, pdl);
-        if (G == 1) return launch_attn_stream<1>(p, stream, pdl);
-        if (G == 3) return launch_attn_stream<3>(p, stream, pdl);
-        if (G == 6) return launch_attn_stream<6>(p, stream, pdl);
+        if (p.head_dim == 64) {
+            if (G == 4) return launch_attn_stream<64, 4>(p, stream, pdl);
+            if (G == 8) return launch_attn_stream<64, 8>(p, stream, pdl);
+            if (G == 2) return launch_attn_stream<64, 2>(p, stream, pdl);
+            if (G == 1) return launch_attn_stream<64, 1>(p, stream, pdl);
+            if (G == 3) return launch_attn_stream<64, 3>(p, stream, pdl);
+            if (G == 6) return launch_attn_stream<64, 6>(p, stream, pdl);
+        } else {
+            if (G == 3) return launch_attn_stream<128, 3>(p, stream, pdl);
+            if (G == 4) return launch_attn_stream<128, 4>(p, stream, pdl);
+            if (G == 8) return launch_attn_stream<128, 8>(p, stream, pdl);
+            if (G == 2) return launch_attn_stream<128, 2>(p, stream, pdl);
+            if (G == 1) return launch_attn_stream<128, 1>(p, stream, pdl);
+            if (G == 6) return launch_attn_stream<128, 6>(p, stream, pdl);
+        }
     }
     // one CTA per split of kAttnSplit positions (the partial records are kept
     // at kAttnItem granularity, so max_splits counts items)

@@ -778,7 +778,7 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         const size_t kv_bytes = static_cast<size_t>(d.layers) * e->num_pages * e->page_stride * e->kv_elem;
         e->kv = dev_alloc<char>(kv_bytes, "KV pool");
         ck(cudaMemset(e->kv, 0, kv_bytes), "KV clear");
-        if (!e->kv_f32 && e->head_dim == 64) {
+        if (!e->kv_f32 && (e->head_dim == 64 || e->head_dim == 128)) {
             const long layer_pool = e->num_pages * e->page_stride;
             e->kv_maps.resize(d.layers);
             for (int l = 0; l < d.layers && !e->kv_maps.empty(); ++l)

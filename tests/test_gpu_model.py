@@ -108,7 +108,7 @@ def test_1b_width_model_128_steps(cuda):
         assert agree >= 0.99, (kv_f32, agree)
 
 
-@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_G3], ids=lambda c: c.name)
+@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_G3, synth.TINY_HD128_G3], ids=lambda c: c.name)
 @pytest.mark.parametrize("prompts,context", [((3, 40), 128), ((150, 300), 512)], ids=["one-item", "multi-item"])
 def test_ragged_step_matches_single_sequence_runs(cuda, prompts, context, cfg):
     """Each sequence of a packed step matches the same sequence decoded alone
@@ -143,15 +143,42 @@ def test_ragged_step_matches_single_sequence_runs(cuda, prompts, context, cfg):
 
 
 def test_long_context_engine_uses_split_kernel(cuda):
-    """An fp16-cache, head_dim-64 engine whose context exceeds the streaming
-    attention's 32 work items (4096 positions) decodes through the CUDA-core
-    split kernel and still meets the logits and greedy bars."""
+    """An fp16-cache engine whose context exceeds the streaming attention's 64
+    work items (8192 positions) decodes through the CUDA-core split kernel and
+    still meets the logits and greedy bars."""
     cfg = synth.TINY
     weights = synth.make_model(cfg, seed=13)
     prompt = synth.prompt_tokens(96, seed=4, vocab_limit=cfg.vocab)
-    errs, agree = _run_pair(cfg, weights, prompt, 8, context=4608)
+    errs, agree = _run_pair(cfg, weights, prompt, 8, context=8320)
     assert errs.max() <= logits_bar(True), errs
     assert agree >= 0.99
+
+
+@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_HD128], ids=lambda c: c.name)
+def test_long_sequence_streaming_merge(cuda, cfg):
+    """A 4200-position sequence spans 33 of the streaming attention's
+    128-position work items, so its merge takes the second item per lane
+    (items 32 and up); both head dims, FP32 activation path, fp16 cache, against
+    the oracle with the same cache format."""
+    weights = synth.make_model(cfg, seed=14)
+    prompt = synth.prompt_tokens(4200, seed=6, vocab_limit=cfg.vocab)
+    O.set_threads(8)
+    om = O.OracleModel(cfg, weights, 4300, False, False, kv_fp16=True)
+    st = om.new_state()
+    tok = om.prefill(st, prompt)
+    eng = Engine(cfg, weights, context=4300, max_batch=8, max_seqs=2, use_dp4a=False, use_q6_dp4a=False)
+    got = eng.prefill(prompt)
+    errs, agree = [], 0
+    for s in range(6):
+        errs.append(rel_l2(eng.logits(8)[(len(prompt) - 1) % 8] if s == 0 else eng.logits(1)[0], st.logits()))
+        agree += int(got == tok)
+        pos = len(prompt) + s
+        nxt = st.forward(int(tok), pos, True)
+        got = eng.forward(int(tok), pos, True)
+        tok = nxt
+    eng.close()
+    assert max(errs) <= FP32_LOGITS_BAR, errs
+    assert agree >= 5, agree
 
 
 def test_prefill_chunks_match_token_by_token(cuda):
