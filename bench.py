@@ -85,6 +85,9 @@ def parse(argv=None):
     ap.add_argument("--no-extras", action="store_true",
                     help="ragged64: skip the decode1 record, kernel timings and reference CUDA timings")
     ap.add_argument("--prompt", type=int, default=512, help="decode1 prompt length")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="ragged workloads: live sequences (0 = the BASELINE config's 64 / 256; smaller for "
+                         "profiling captures)")
     ap.add_argument("--prompt-max", type=int, default=1024,
                     help="ragged64 longest prompt (1024 in the BASELINE config; smaller for profiling captures)")
     ap.add_argument("--nvtx-step", action="store_true",
@@ -807,12 +810,12 @@ def run_ours(args):
     weights = synth.make_model(cfg, seed=0)
     from ijb200.engine import Engine
     if args.workload == "ragged64":
-        batch, context = 64, args.prompt_max + 256 + 16
+        batch, context = args.batch or 64, args.prompt_max + 256 + 16
         eng = Engine(cfg, weights, context=context, max_batch=batch, max_seqs=batch + 1, device=local)
         server = RaggedServer(eng, batch, seed=1000 + rank, prompt_max=args.prompt_max)
     elif big:
         pmax = min(args.prompt_max * 4, 4096)  # 4096 by default
-        batch, context = 256, pmax + 512 + 16
+        batch, context = args.batch or 256, pmax + 512 + 16
         eng = Engine(cfg, weights, context=context, max_batch=batch, max_seqs=batch + 1, device=local)
         server = RaggedServer(eng, batch, seed=2000 + rank, prompt_max=pmax, prompt_min=64, out_range=(64, 512))
     else:
@@ -917,11 +920,11 @@ def run_ours(args):
                                                   "sample": f"one decode token at each context {used1}"},
                              "gemv_1_thread": cpu_gemv(1), f"gemv_{nthreads}_threads": cpu_gemv(nthreads)}
         h2d = 4 * batch * 4  # token, seq, position, KV slot per entry (int32)
-        metric = ("decode tokens/s (3B Q4_K_M, batch 256)" if big else
-                  "decode tokens/s (1B Q4_K_M, batch 64)" if ragged else "decode tokens/s (1B Q4_K_M, batch 1)")
-        workload = (f"llama-3.2-3b Q4_K_M ragged decode, 256 seqs, prompts U[64,{server.prompt_max}], outputs "
+        metric = (f"decode tokens/s (3B Q4_K_M, batch {batch})" if big else
+                  f"decode tokens/s (1B Q4_K_M, batch {batch})" if ragged else "decode tokens/s (1B Q4_K_M, batch 1)")
+        workload = (f"llama-3.2-3b Q4_K_M ragged decode, {batch} seqs, prompts U[64,{server.prompt_max}], outputs "
                     "U[64,512], replacement, pre-aged population" if big else
-                    f"llama-3.2-1b Q4_K_M ragged decode, 64 seqs, prompts U[16,{args.prompt_max}], "
+                    f"llama-3.2-1b Q4_K_M ragged decode, {batch} seqs, prompts U[16,{args.prompt_max}], "
                     "outputs U[32,256], replacement, pre-aged population" if ragged
                     else f"llama-3.2-1b Q4_K_M decode, batch 1, {args.prompt}-token prompt")
         result = {
