@@ -68,7 +68,12 @@ constexpr int kMaxCluster = 8;
 constexpr int kStage = kMmaTileM + 4;
 constexpr int kRedBytes = kMmaMaxN * kStage * 4;
 constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kXWarp = 6, kConvWarp0 = 7, kConvWarps = 16;
-constexpr int kMmaThreads = (kConvWarp0 + kConvWarps) * 32;
+constexpr int kMma2Warp = kConvWarp0 + kConvWarps;  // second MMA issuer of CTAs with several tiles
+constexpr int kMmaThreads = (kMma2Warp + 1) * 32;
+constexpr int kEpiThreadsSingle = (4 + kConvWarps) * 32;  // epilogue + converter warps of a one-tile CTA
+// TMEM column of accumulator chain g (0..3) of a one-tile CTA: chains 0 and 1
+// sit where a several-tile CTA keeps its double-buffered chains 0 and 1
+__host__ __device__ constexpr uint32_t chain_col_single(int g) { return ((g & 1) ? 384u : 0u) + ((g & 2) ? 64u : 0u); }
 constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 2;
 
 struct MmaSmem {
@@ -160,6 +165,18 @@ __device__ __forceinline__ void tmem_wait16(uint32_t *r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
                    "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+// 8 columns without waiting, and the matching wait (see tmem_ld16_nw).
+__device__ __forceinline__ void tmem_ld8_nw(uint32_t taddr, uint32_t *r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait8(uint32_t *r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
                  :
                  : "memory");
 }
@@ -452,24 +469,26 @@ __device__ __forceinline__ long kv_offset(const MmaParams &p, const EpiRow &e, c
 }
 
 // Phase B of the epilogue: stage[n][r] holds the finished GEMM value of tile
-// lane r for tokens [t_lo, t_hi); apply the row operation in place (SiLU pairs,
-// RoPE), write the KV cache, or (no bulk path) store the outputs directly.
-// Every thread of the 128 calls this; per-token loops are warp-uniform.
-__device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, float *stage, int r, int t_lo, int t_hi,
-                         bool bulk) {
+// lane r for the tokens of this part's slice (below t_hi); apply the row
+// operation in place (SiLU pairs, RoPE), write the KV cache, or (no bulk path)
+// store the outputs directly.  The calling thread handles row r for tokens
+// n0, n0 + step, ... (step = threads / 128); per-token loops are warp-uniform.
+__device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, float *stage, int r, int n0, int step,
+                         int t_hi, bool bulk) {
     float *col = stage + r;  // token n at col[n * kStage]
     switch (e.epi) {
         case kEpiSiluPair: {
-            // gate row r & 63 of every other token (both halves of the 128 threads
-            // work); silu(g) * u with the fast division (2 ulp)
+            // gate row r & 63 of every other token of the thread's phase (both halves
+            // of each 128 work); silu(g) * u with the fast division (2 ulp)
             float *gcol = stage + (r & 63);
             const bool valid = r < 64 ? e.valid : e.valid_pair;
+            float *out = r < 64 ? e.out : e.out_pair;
 #pragma unroll 4
-            for (int n = t_lo + (r >> 6); n < t_hi; n += 2) {
+            for (int n = n0 + step * (r >> 6); n < t_hi; n += 2 * step) {
                 const float g = gcol[n * kStage], u = gcol[n * kStage + 64];
                 const float v = __fdividef(g, 1.f + __expf(-g)) * u;
                 if (bulk) gcol[n * kStage] = v;
-                else if (valid) e.out_pair[n * e.stride] = v;
+                else if (valid) out[n * e.stride] = v;
             }
             break;
         }
@@ -477,11 +496,11 @@ __device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, 
         case kEpiRopeKCache: {
             // rope_cuda (inferencer.cu:906-917); the partner row r ^ 1 is the neighbouring lane
             const float *pc = p.rope_cos + e.f, *ps = p.rope_sin + e.f;
-            for (int n0 = t_lo; n0 < t_hi; n0 += 8) {
+            for (int nb = n0; nb < t_hi; nb += 8 * step) {
                 float y[8], z[8], c[8], sn[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    const int n = min(n0 + k, t_hi - 1);
+                    const int n = min(nb + k * step, t_hi - 1);
                     y[k] = col[n * kStage];
                     z[k] = stage[n * kStage + (r ^ 1)];
                     const int pos = tk.pos[n] * p.half_head;
@@ -491,14 +510,15 @@ __device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, 
                 __syncwarp();
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    if (n0 + k >= t_hi) break;
+                    const int n = nb + k * step;
+                    if (n >= t_hi) break;
                     const float a = e.even ? y[k] : z[k], b = e.even ? z[k] : y[k];
                     const float v = e.even ? a * c[k] - b * sn[k] : a * sn[k] + b * c[k];
                     if (e.epi == kEpiRopeQ) {
-                        if (bulk) col[(n0 + k) * kStage] = v;
-                        else if (e.valid) e.out[(n0 + k) * e.stride] = v;
+                        if (bulk) col[n * kStage] = v;
+                        else if (e.valid) e.out[n * e.stride] = v;
                     } else if (e.valid) {
-                        const long off = kv_offset(p, e, tk, n0 + k);
+                        const long off = kv_offset(p, e, tk, n);
                         if (p.kv_f32) static_cast<float *>(p.k_cache)[off] = v;
                         else static_cast<__half *>(p.k_cache)[off] = __float2half_rn(v);
                     }
@@ -509,25 +529,22 @@ __device__ void epi_rows(const MmaParams &p, const EpiRow &e, const EpiTok &tk, 
         }
         case kEpiVCache:
             if (e.valid)
-                for (int n = t_lo; n < t_hi; ++n) {
+                for (int n = n0; n < t_hi; n += step) {
                     const long off = kv_offset(p, e, tk, n);
                     if (p.kv_f32) static_cast<float *>(p.v_cache)[off] = col[n * kStage];
                     else static_cast<__half *>(p.v_cache)[off] = __float2half_rn(col[n * kStage]);
                 }
             break;
         case kEpiStore:
+        case kEpiLogitsArgmax:
             if (!bulk && e.valid)
-                for (int n = t_lo; n < t_hi; ++n) e.out[n * e.stride] = col[n * kStage];
+                for (int n = n0; n < t_hi; n += step) e.out[n * e.stride] = col[n * kStage];
             break;
         case kEpiAdd:
             if (!bulk && e.valid)
-                for (int n = t_lo; n < t_hi; ++n)
+                for (int n = n0; n < t_hi; n += step)
                     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + n * e.stride), "f"(col[n * kStage])
                                  : "memory");
-            break;
-        case kEpiLogitsArgmax:
-            if (!bulk && e.valid)
-                for (int n = t_lo; n < t_hi; ++n) e.out[n * e.stride] = col[n * kStage];
             break;
         default:
             break;
@@ -564,6 +581,9 @@ __device__ void epi_argmax(const float *stage, const EpiTok &tk, int row_base, i
 
 // ----------------------------------------------------------------- kernel --
 
+// The kernel declares no static shared memory: with a static block in front of
+// the dynamic one, results came out wrong on B200 (cause not identified), so
+// every shared buffer is carved from the dynamic block (mma_smem).
 __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __grid_constant__ MmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr MmaSmem L = mma_smem();
@@ -610,7 +630,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
             mbar_init(empty + i, 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(acc_full + i, single ? 2 : 1);  // a commit from each issuing thread
+            mbar_init(acc_full + i, single ? 4 : 2);  // a commit from each issuing thread
             mbar_init(acc_empty + i, 4);
         }
         mbar_init(part_ready, ksplit);
@@ -630,13 +650,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
     pdl_trigger();
 
     // MMA issue for the 64-wide groups in `mask` of every block column: D (fp32)
-    // [128 x n_pad] = A (fp16 weights in TMEM) * B (fp16 activation, K-major)^T.
-    // Even groups accumulate into chain 0, odd groups into chain 1 (summed by the
-    // epilogue).  One thread issues a tcgen05.mma about every 100 cycles
-    // whatever N, so a CTA with a single tile lets two epilogue warps, idle
-    // until then, issue one chain each; otherwise warp 1 issues both and the
-    // accumulators are double-buffered across tiles.
-    auto mma_loop = [&](uint32_t mask) {
+    // [128 x n_pad] = A (fp16 weights in TMEM) * B (fp16 activation, K-major)^T,
+    // into one accumulator chain per issuing thread (summed by the epilogue).
+    // A thread issues a tcgen05.mma only every ~130 cycles whatever N, while
+    // several threads issuing into separate accumulators share the tensor core
+    // (four reach ~43 cycles per M=128 N=64 K=16 MMA), so a CTA with a single
+    // tile has its four epilogue warps, idle until then, issue one group's chain
+    // each; a CTA with several tiles issues from warps 1 (even groups) and 23
+    // (odd groups) with the accumulators double-buffered across tiles.
+    auto mma_loop = [&](uint32_t mask, uint32_t chain_col) {
         const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(n_pad >> 3) << 17) | (8u << 24);
         const uint64_t b_desc0 = umma_desc(smem_u32(smem + L.x16), kCoreStride, kGroupStride);
         uint32_t blk = 0, i = 0;
@@ -644,8 +666,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
             const int a = i & 1;
             if (i >= 2) mbar_wait_bounded(acc_empty + a, ((i >> 1) - 1) & 1, p.status, cta_abort);
             tc_fence_after();
-            const uint32_t dcol0 = tmem_base + static_cast<uint32_t>(a * n_pad), dcol1 = dcol0 + kTmemAcc1;
-            uint32_t acc0 = 0, acc1 = 0;
+            const uint32_t dcol = tmem_base + chain_col + static_cast<uint32_t>(single ? 0 : a * n_pad);
+            uint32_t acc = 0;
             for (int b = b0; b < b1; ++b, ++blk) {
                 const uint32_t ph = (blk >> 1) & 1;
 #pragma unroll
@@ -660,13 +682,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                     const uint64_t bd = b_desc0 + static_cast<uint64_t>(st * (kX16Bytes >> 4));
 #pragma unroll
                     for (int kk = 0; kk < kKChunk / 16; ++kk) {
-                        if (g & 1) {
-                            umma_f16_ta(dcol1, ta + kk * 8, bd + kk * 16, idesc, acc1);
-                            acc1 = 1u;
-                        } else {
-                            umma_f16_ta(dcol0, ta + kk * 8, bd + kk * 16, idesc, acc0);
-                            acc0 = 1u;
-                        }
+                        umma_f16_ta(dcol, ta + kk * 8, bd + kk * 16, idesc, acc);
+                        acc = 1u;
                     }
                     umma_commit(empty + st);
                 }
@@ -729,176 +746,217 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                 }
             }
         }
-    } else if (warp == kMmaWarp) {
-        if (lane == 0 && !single) mma_loop(0xFu);
-    } else if (warp < kXWarp) {
-        // ---------------------------------------------------------- epilogue
-        const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
-        const int r = quad * 32 + lane;
-        if (single && warp < kEpiWarp0 + 2) {  // first issue one accumulation chain's MMAs
-            if (lane == 0) mma_loop(warp == kEpiWarp0 ? 0x5u : 0xAu);
-            __syncwarp();
-        }
-        pdl_wait();
-        float *xinv_s = reinterpret_cast<float *>(smem + L.tok);
-        int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxN), *slot_s = pos_s + kMmaMaxN;
-        unsigned long long *keys_s = reinterpret_cast<unsigned long long *>(slot_s + kMmaMaxN);
-        if (r < n_pad) {
-            xinv_s[r] = p.x_inv[r];
-            pos_s[r] = p.tok_pos && r < p.batch ? p.tok_pos[r] : 0;
-            slot_s[r] = p.tok_slot && r < p.batch ? p.tok_slot[r] : 0;
-            keys_s[r] = 0ull;
-        }
-        named_bar_sync(1, 128);
-        const EpiTok tk{xinv_s, pos_s, slot_s, keys_s};
-        bool any_logits = false;
-        const int per = split_per(p.batch, ksplit);  // tokens of each part's epilogue slice
-        uint32_t i = 0;
-        for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
-            const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
-            const int lt = t - sg.tile0;
-            const int a = i & 1;
-            // the tile's row bookkeeping, done while its accumulator is still being summed
-            bool valid;
-            const int row = tile_row(sg, lt, r, valid);
-            EpiRow e = make_epi_row(p, sg, row, valid);
-            if (sg.w1 >= 0 && r >= 64) {  // up-row threads also finish gate row r - 64 (SiLU pass)
-                bool v2;
-                const int row2 = tile_row(sg, lt, r - 64, v2);
-                e.out_pair = sg.out + sg.row_offset + row2;
-                e.valid_pair = v2;
-            }
-            any_logits |= sg.epi == kEpiLogitsArgmax;
-            const float wscale = ldexpf(1.0f, -wexp_s[r >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * n_pad;
-            // the bulk stores of the previous tile have finished reading the staging tile
-            if (i > 0) {
-                if (warp == kEpiWarp0) bulk_wait_read();
-                named_bar_sync(1, 128);
-            }
-            // ... and (split K) every part has read its slice of this CTA's previous tile
-            if (ksplit > 1 && i > 0) mbar_wait_cluster_bounded(part_free, (i - 1) & 1, p.status, cta_abort);
-            mbar_wait_bounded(acc_full + a, (i >> 1) & 1, p.status, cta_abort);
-            tc_fence_after();
-            // accumulator (chain 0 + chain 1) -> stage[token][row], scaled
-            float *stage = red;
-            for (int c0 = 0; c0 < n_pad; c0 += 16) {
-                uint32_t v[16], w[16];
-                tmem_ld16_nw(taddr + c0, v);
-                tmem_ld16_nw(taddr + kTmemAcc1 + c0, w);
-                tmem_wait16(v);
-                tmem_wait16(w);
-#pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    stage[(c0 + k) * kStage + r] = (__uint_as_float(v[k]) + __uint_as_float(w[k])) * wscale * xinv_s[c0 + k];
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty + a);
-            int t_lo = 0, t_hi = p.batch;
-            if (ksplit > 1) {
-                // the parts signal each other that their partial tiles are staged, then
-                // part s sums its token slice of every part's tile over the cluster's
-                // shared memory (DSMEM), in part order, so the result does not depend on
-                // timing; the sums overwrite the slice in this CTA's own tile
-                named_bar_sync(1, 128);
-                if (warp == kEpiWarp0 && lane < ksplit) {
-                    asm volatile("fence.acq_rel.cluster;" ::: "memory");
-                    mbar_arrive_remote(part_ready, lane);
+    } else if (warp == kMmaWarp || warp == kMma2Warp) {
+        if (lane == 0 && !single) mma_loop(warp == kMmaWarp ? 0x5u : 0xAu, warp == kMmaWarp ? 0u : kTmemAcc1);
+    } else {
+        const bool conv = warp >= kConvWarp0;
+        if (conv) {
+            // ---------------------------------------------------------- dequant
+            // four groups of four warps; group g converts group g of every block
+            // column, warp w covers the rows of TMEM lane quadrant w % 4
+            const int g = (warp - kConvWarp0) / 4;
+            const int row = (warp & 3) * 32 + lane;
+            const uint32_t tmem_lane = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + kTmemA;
+            uint32_t blk = 0;
+            int r = 0;
+            for (int t = tile_first; t < p.total_tiles; t += tile_step) {
+                const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
+                const float scale = ldexpf(1.0f, wexp_s[row >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
+                for (int b = b0; b < b1; ++b, ++blk) {
+                    const int st = (blk & 1) * kGroups + g;
+                    const uint32_t use = blk >> 1;
+                    const uint32_t tmem_row = tmem_lane + static_cast<uint32_t>(st * 32);
+                    mbar_wait_bounded(full_raw + r, (blk / kRawStages) & 1, p.status, cta_abort);
+                    if (use) mbar_wait_bounded(empty + st, (use - 1) & 1, p.status, cta_abort);
+                    tc_fence_after();
+                    const uint8_t *raw = smem + L.raw + r * kRawStageBytes;
+                    if (sg.type == kQ4K) convert_q4(raw, tmem_row, row, g, scale);
+                    else convert_q6(raw, tmem_row, row, g, scale);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(full + st);
+                        mbar_arrive(empty_raw + r);
+                    }
+                    if (++r == kRawStages) r = 0;
                 }
-                const bool ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort);
-                t_lo = min(p.batch, rank * per);
-                t_hi = ok ? min(p.batch, t_lo + per) : t_lo;
-                // items of four rows x one token, a warp covering one token's 128 rows
-                const int items = (t_hi - t_lo) * 32;
-                const uint32_t base = smem_u32(stage);
-                for (int it = threadIdx.x - kEpiWarp0 * 32; it < items; it += 128) {
-                    const uint32_t off = static_cast<uint32_t>(((t_lo + (it >> 5)) * kStage + (it & 31) * 4) * 4);
-                    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int q0 = 0; q0 < ksplit; q0 += 4) {  // four loads in flight, summed in part order
-                        float4 v[4];
+            }
+        }
+        if (!conv || single) {
+            // ---------------------------------------------------------- epilogue
+            // Run by the four epilogue warps, joined by the sixteen converter warps
+            // (then idle) when the CTA has a single tile: E threads, e = 0..E-1.
+            const int E = single ? kEpiThreadsSingle : 128;
+            const int bar_id = single ? 2 : 1;
+            const int e = conv ? (4 + warp - kConvWarp0) * 32 + lane : (warp - kEpiWarp0) * 32 + lane;
+            const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+            const int dr = quad * 32 + lane;  // the tile row this thread drains from TMEM
+            // drain: 16-column blocks of the accumulators; with one tile the four
+            // converter warps of a quadrant take one block each, else the epilogue
+            // warp of the quadrant takes all
+            const int jq = conv ? (warp - kConvWarp0) / 4 : -1;
+            const int cb_first = single ? jq : 0, cb_step = single ? 4 : 1;
+            if (!conv) {
+                if (single) {  // first issue group (warp - 2)'s accumulation chain
+                    if (lane == 0) mma_loop(1u << (warp - kEpiWarp0), chain_col_single(warp - kEpiWarp0));
+                    __syncwarp();
+                }
+                pdl_wait();
+            }
+            float *xinv_s = reinterpret_cast<float *>(smem + L.tok);
+            int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxN), *slot_s = pos_s + kMmaMaxN;
+            unsigned long long *keys_s = reinterpret_cast<unsigned long long *>(slot_s + kMmaMaxN);
+            if (!conv && dr < n_pad) {
+                xinv_s[dr] = p.x_inv[dr];
+                pos_s[dr] = p.tok_pos && dr < p.batch ? p.tok_pos[dr] : 0;
+                slot_s[dr] = p.tok_slot && dr < p.batch ? p.tok_slot[dr] : 0;
+                keys_s[dr] = 0ull;
+            }
+            named_bar_sync(bar_id, E);
+            const EpiTok tk{xinv_s, pos_s, slot_s, keys_s};
+            bool any_logits = false;
+            const int per = split_per(p.batch, ksplit);  // tokens of each part's epilogue slice
+            const int r = e & 127, ph = e >> 7, nph = E >> 7;  // row and token phase of the row work
+            uint32_t i = 0;
+            for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
+                const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
+                const int lt = t - sg.tile0;
+                const int a = i & 1;
+                // the tile's row bookkeeping, done while its accumulator is still being summed
+                bool valid;
+                const int row = tile_row(sg, lt, r, valid);
+                EpiRow er = make_epi_row(p, sg, row, valid);
+                if (sg.w1 >= 0 && r >= 64) {  // up-row threads also finish gate row r - 64 (SiLU pass)
+                    bool v2;
+                    const int row2 = tile_row(sg, lt, r - 64, v2);
+                    er.out_pair = sg.out + sg.row_offset + row2;
+                    er.valid_pair = v2;
+                }
+                any_logits |= sg.epi == kEpiLogitsArgmax;
+                const float wscale = ldexpf(1.0f, -wexp_s[dr >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+                // the bulk stores of the previous tile have finished reading the staging tile
+                if (i > 0) {
+                    if (warp == kEpiWarp0) bulk_wait_read();
+                    named_bar_sync(bar_id, E);
+                }
+                // ... and (split K) every part has read its slice of this CTA's previous tile
+                if (ksplit > 1 && i > 0) mbar_wait_cluster_bounded(part_free, (i - 1) & 1, p.status, cta_abort);
+                mbar_wait_bounded(acc_full + a, (i >> 1) & 1, p.status, cta_abort);
+                tc_fence_after();
+                // accumulator chains -> stage[token][row], summed in a fixed order and scaled
+                float *stage = red;
+                if (cb_first >= 0) {
+                    // 8 columns at a time: (chain 0 + chain 1) [+ (chain 2 + chain 3)]
+                    for (int c0 = cb_first * 16; c0 < n_pad; c0 += cb_step * 16) {
+#pragma unroll 1
+                        for (int h = 0; h < 16; h += 8) {
+                            const int c = c0 + h;
+                            uint32_t v[8], w[8], v2[8], w2[8];
+                            float sum[8];
+                            if (single) {
+                                tmem_ld8_nw(taddr + chain_col_single(0) + c, v);
+                                tmem_ld8_nw(taddr + chain_col_single(1) + c, w);
+                                tmem_ld8_nw(taddr + chain_col_single(2) + c, v2);
+                                tmem_ld8_nw(taddr + chain_col_single(3) + c, w2);
+                                tmem_wait8(v);
+                                tmem_wait8(w);
+                                tmem_wait8(v2);
+                                tmem_wait8(w2);
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            if (q0 + q < ksplit) v[q] = dsmem_ld4(dsmem_addr(base + off, q0 + q));
+                                for (int k = 0; k < 8; ++k)
+                                    sum[k] = (__uint_as_float(v[k]) + __uint_as_float(w[k])) +
+                                             (__uint_as_float(v2[k]) + __uint_as_float(w2[k]));
+                            } else {
+                                tmem_ld8_nw(taddr + a * n_pad + c, v);
+                                tmem_ld8_nw(taddr + kTmemAcc1 + a * n_pad + c, w);
+                                tmem_wait8(v);
+                                tmem_wait8(w);
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            if (q0 + q < ksplit) {
-                                y.x += v[q].x; y.y += v[q].y; y.z += v[q].z; y.w += v[q].w;
+                                for (int k = 0; k < 8; ++k) sum[k] = __uint_as_float(v[k]) + __uint_as_float(w[k]);
                             }
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) stage[(c + k) * kStage + dr] = sum[k] * wscale * xinv_s[c + k];
                         }
                     }
-                    *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(stage) + off) = y;
                 }
-                // the peers may refill their tiles once every part has read its slice
-                if (t + tile_step < p.total_tiles) {
-                    named_bar_sync(1, 128);
-                    if (warp == kEpiWarp0 && lane < ksplit) {
-                        asm volatile("fence.acq_rel.cluster;" ::: "memory");
-                        mbar_arrive_remote(part_free, lane);
-                    }
-                }
-            }
-            named_bar_sync(1, 128);
-            // rows this tile writes and whether whole token rows can go out as bulk stores
-            const int row0 = sg.w1 >= 0 ? lt * 64 : lt * 128;
-            const int count = min(sg.w1 >= 0 ? 64 : 128, sg.rows - row0);
-            float *gbase = sg.out + sg.row_offset + row0;
-            const bool bulk_kind = sg.epi == kEpiStore || sg.epi == kEpiAdd || sg.epi == kEpiSiluPair ||
-                                   sg.epi == kEpiRopeQ || sg.epi == kEpiLogitsArgmax;
-            const bool bulk = p.bulk_out && bulk_kind && count > 0 && (count & 3) == 0 && (sg.out_stride & 3) == 0 &&
-                              (reinterpret_cast<uintptr_t>(gbase) & 15) == 0;
-            epi_rows(p, e, tk, stage, r, t_lo, t_hi, bulk);
-            if (sg.epi == kEpiLogitsArgmax) {
-                named_bar_sync(1, 128);
-                epi_argmax(stage, tk, sg.key_offset + sg.row_offset + row0, count, t_lo, t_hi);
-            }
-            if (bulk) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                named_bar_sync(1, 128);
-                if (warp == kEpiWarp0) {  // one token row per lane at a time
-                    for (int n = t_lo + lane; n < t_hi; n += 32) {
-                        if (sg.epi == kEpiAdd) bulk_s2g_add(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
-                        else bulk_s2g(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
-                    }
-                    bulk_commit();
-                }
-            }
-        }
-        if (warp == kEpiWarp0) bulk_wait_read();  // the writes complete with the grid
-        if (any_logits) {  // this CTA's best key per token, one global atomic each
-            named_bar_sync(1, 128);
-            if (r < p.batch && keys_s[r]) atomicMax(p.argmax_keys + r, keys_s[r]);
-        }
-    } else {
-        // ---------------------------------------------------------- dequant
-        // four groups of four warps; group g converts group g of every block
-        // column, warp w covers the rows of TMEM lane quadrant w % 4
-        const int g = (warp - kConvWarp0) / 4;
-        const int row = (warp & 3) * 32 + lane;
-        const uint32_t tmem_lane = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + kTmemA;
-        uint32_t blk = 0;
-        int r = 0;
-        for (int t = tile_first; t < p.total_tiles; t += tile_step) {
-            const MmaSeg sg = seg_s[mma_seg_of_tile(p, t)];
-            const float scale = ldexpf(1.0f, wexp_s[row >= 64 && sg.w1 >= 0 ? sg.w1 : sg.w0]);
-            for (int b = b0; b < b1; ++b, ++blk) {
-                const int st = (blk & 1) * kGroups + g;
-                const uint32_t use = blk >> 1;
-                const uint32_t tmem_row = tmem_lane + static_cast<uint32_t>(st * 32);
-                mbar_wait_bounded(full_raw + r, (blk / kRawStages) & 1, p.status, cta_abort);
-                if (use) mbar_wait_bounded(empty + st, (use - 1) & 1, p.status, cta_abort);
-                tc_fence_after();
-                const uint8_t *raw = smem + L.raw + r * kRawStageBytes;
-                if (sg.type == kQ4K) convert_q4(raw, tmem_row, row, g, scale);
-                else convert_q6(raw, tmem_row, row, g, scale);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(full + st);
-                    mbar_arrive(empty_raw + r);
+                if (!single && lane == 0) mbar_arrive(acc_empty + a);
+                int t_lo = 0, t_hi = p.batch;
+                if (ksplit > 1) {
+                    // the parts signal each other that their partial tiles are staged, then
+                    // part s sums its token slice of every part's tile over the cluster's
+                    // shared memory (DSMEM), in part order, so the result does not depend on
+                    // timing; the sums overwrite the slice in this CTA's own tile
+                    named_bar_sync(bar_id, E);
+                    if (warp == kEpiWarp0 && lane < ksplit) {
+                        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                        mbar_arrive_remote(part_ready, lane);
+                    }
+                    const bool ok = mbar_wait_cluster_bounded(part_ready, i & 1, p.status, cta_abort);
+                    t_lo = min(p.batch, rank * per);
+                    t_hi = ok ? min(p.batch, t_lo + per) : t_lo;
+                    // items of four rows x one token, a warp covering one token's 128 rows
+                    const int items = (t_hi - t_lo) * 32;
+                    const uint32_t base = smem_u32(stage);
+                    for (int it = e; it < items; it += E) {
+                        const uint32_t off = static_cast<uint32_t>(((t_lo + (it >> 5)) * kStage + (it & 31) * 4) * 4);
+                        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int q0 = 0; q0 < ksplit; q0 += 4) {  // four loads in flight, summed in part order
+                            float4 v[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                if (q0 + q < ksplit) v[q] = dsmem_ld4(dsmem_addr(base + off, q0 + q));
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                if (q0 + q < ksplit) {
+                                    y.x += v[q].x; y.y += v[q].y; y.z += v[q].z; y.w += v[q].w;
+                                }
+                            }
+                        }
+                        *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(stage) + off) = y;
+                    }
+                    // the peers may refill their tiles once every part has read its slice
+                    if (t + tile_step < p.total_tiles) {
+                        named_bar_sync(bar_id, E);
+                        if (warp == kEpiWarp0 && lane < ksplit) {
+                            asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                            mbar_arrive_remote(part_free, lane);
+                        }
+                    }
                 }
-                if (++r == kRawStages) r = 0;
+                named_bar_sync(bar_id, E);
+                // rows this tile writes and whether whole token rows can go out as bulk stores
+                const int row0 = sg.w1 >= 0 ? lt * 64 : lt * 128;
+                const int count = min(sg.w1 >= 0 ? 64 : 128, sg.rows - row0);
+                float *gbase = sg.out + sg.row_offset + row0;
+                const bool bulk_kind = sg.epi == kEpiStore || sg.epi == kEpiAdd || sg.epi == kEpiSiluPair ||
+                                       sg.epi == kEpiRopeQ || sg.epi == kEpiLogitsArgmax;
+                const bool bulk = p.bulk_out && bulk_kind && count > 0 && (count & 3) == 0 &&
+                                  (sg.out_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(gbase) & 15) == 0;
+                epi_rows(p, er, tk, stage, r, t_lo + ph, nph, t_hi, bulk);
+                if (sg.epi == kEpiLogitsArgmax) {
+                    named_bar_sync(bar_id, E);
+                    if (!conv) epi_argmax(stage, tk, sg.key_offset + sg.row_offset + row0, count, t_lo, t_hi);
+                }
+                if (bulk) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    named_bar_sync(bar_id, E);
+                    if (warp == kEpiWarp0) {  // one token row per lane at a time
+                        for (int n = t_lo + lane; n < t_hi; n += 32) {
+                            if (sg.epi == kEpiAdd) bulk_s2g_add(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
+                            else bulk_s2g(gbase + n * sg.out_stride, stage + n * kStage, count * 4);
+                        }
+                        bulk_commit();
+                    }
+                }
+            }
+            if (warp == kEpiWarp0) bulk_wait_read();  // the writes complete with the grid
+            if (any_logits && !conv) {  // this CTA's best key per token, one global atomic each
+                named_bar_sync(1, 128);
+                if (dr < p.batch && keys_s[dr]) atomicMax(p.argmax_keys + dr, keys_s[dr]);
             }
         }
     }
@@ -914,35 +972,58 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
 
 // --------------------------------------------------------- activation prep --
 
-// One CTA per token: the GEMV prologue's arithmetic (RMSNorm, the reference's
-// per-32 int8 quantisation) then x^ = q * scale (DP4A semantics) or x (FP32
-// semantics), times 2^kx so that max|x^| lies in [2^14, 2^15), rounded to
-// fp16 into the MMA layout: chunk c (64 wide) is [n/8][core j][n%8][8 values]
-// with core j holding 64c + 4j + {0,2,1,3} and 64c + 32 + 4j + {0,2,1,3}.
-// Each thread owns cores; the 8 cores of a chunk sit on 8 adjacent lanes, so
-// a 32-wide quantisation group is an 8-lane shuffle reduction.
-__device__ void mma_prep_token(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch, int n,
-                               int n_pad, int use_dp4a, uint8_t *x16, float *x_inv) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float part_s[8], amax_s[8];
+// One token by NT threads (tid 0..NT-1, synchronising on named barrier bar_id;
+// part_s/amax_s: 2 * NT/32 floats of shared memory each, double-buffered by
+// `parity` so that consecutive tokens need no extra barrier): the GEMV
+// prologue's arithmetic (RMSNorm, the reference's per-32 int8 quantisation)
+// then x^ = q * scale (DP4A semantics) or x (FP32 semantics), times 2^kx so
+// that max|x^| lies in [2^14, 2^15), rounded to fp16 into the MMA layout:
+// chunk c (64 wide) is [n/8][core j][n%8][8 values] with core j holding
+// 64c + 4j + {0,2,1,3} and 64c + 32 + 4j + {0,2,1,3}.  Each thread owns cores;
+// the 8 cores of a chunk sit on 8 adjacent lanes, so a 32-wide quantisation
+// group is an 8-lane shuffle reduction.  With wait_pdl the norm weights are
+// read before griddepcontrol.wait (they do not depend on the previous kernel)
+// and everything else after it.
+template <int NT>
+__device__ void mma_prep_token_t(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
+                                 int n, int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, int tid, int bar_id,
+                                 float *part_s, float *amax_s, int parity, bool wait_pdl) {
+    constexpr int W = NT / 32;
+    constexpr int kPer = kMaxCols / (NT * 8);
+    const int lane = tid & 31, warp = tid >> 5;
+    part_s += parity * W;
+    amax_s += parity * W;
     const long chunk_bytes = static_cast<long>(n_pad) * kKChunk * 2;
     const int cores = cols / 8;
     auto dst_of = [&](int core) -> uint8_t * {
         return x16 + (core >> 3) * chunk_bytes + (n >> 3) * kGroupStride + (core & 7) * kCoreStride + (n & 7) * 16;
     };
+    // the norm weight of every value this thread owns
+    float wv[kPer][8];
+    if (norm_w && n < batch) {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int core = tid + NT * j;
+            if (core >= cores) continue;
+            const int k0 = (core >> 3) * 64 + (core & 7) * 4;
+            const float4 wa = __ldg(reinterpret_cast<const float4 *>(norm_w + k0));
+            const float4 wb = __ldg(reinterpret_cast<const float4 *>(norm_w + k0 + 32));
+            wv[j][0] = wa.x; wv[j][1] = wa.y; wv[j][2] = wa.z; wv[j][3] = wa.w;
+            wv[j][4] = wb.x; wv[j][5] = wb.y; wv[j][6] = wb.z; wv[j][7] = wb.w;
+        }
+    }
+    if (wait_pdl) pdl_wait();
     if (n >= batch) {
-        for (int c = tid; c < cores; c += 256) *reinterpret_cast<uint4 *>(dst_of(c)) = make_uint4(0, 0, 0, 0);
+        for (int c = tid; c < cores; c += NT) *reinterpret_cast<uint4 *>(dst_of(c)) = make_uint4(0, 0, 0, 0);
         if (tid == 0) x_inv[n] = 0.f;
         return;
     }
     const float *xr = x + n * x_stride;
-    // every value this thread needs, loaded once (activation and norm weight together)
-    constexpr int kPer = kMaxCols / (256 * 8);
     float vals[kPer][8];
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-        const int core = tid + 256 * j;
+        const int core = tid + NT * j;
         if (core >= cores) continue;
         const int k0 = (core >> 3) * 64 + (core & 7) * 4;  // first of the low four; +32 for the high four
         const float4 a = *reinterpret_cast<const float4 *>(xr + k0);
@@ -953,28 +1034,24 @@ __device__ void mma_prep_token(const float *x, long x_stride, const float *norm_
         for (int e = 0; e < 8; ++e) ss = fmaf(vals[j][e], vals[j][e], ss);
     }
     float r = 1.f;
-    if (norm_w) {  // RMSNorm: warp sums, then the 8 warp partials in a fixed order
+    if (norm_w) {  // RMSNorm: warp sums, then the warp partials in a fixed order
         ss = warp_sum(ss);
         if (lane == 0) part_s[warp] = ss;
-        __syncthreads();
+        named_bar_sync(bar_id, NT);
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) tot += part_s[w];
+        for (int w = 0; w < W; ++w) tot += part_s[w];
         r = rsqrtf(tot / static_cast<float>(cols) + eps);
     }
     float local_max = 0.f;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-        const int core = tid + 256 * j;
+        const int core = tid + NT * j;
         if (core >= cores) continue;  // warp-uniform: cores is a multiple of 32
         float *v = vals[j];
         if (norm_w) {
-            const int k0 = (core >> 3) * 64 + (core & 7) * 4;
-            const float4 wa = *reinterpret_cast<const float4 *>(norm_w + k0);
-            const float4 wb = *reinterpret_cast<const float4 *>(norm_w + k0 + 32);
-            const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], r), w8[e]);
+            for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], r), wv[j][e]);
         }
         if (use_dp4a) {
             // quantize_x32_cuda (inferencer.cu:544-556): groups 64c..64c+31 (v[0..3] of
@@ -1004,17 +1081,17 @@ __device__ void mma_prep_token(const float *x, long x_stride, const float *norm_
     }
     local_max = warp_max(local_max);
     if (lane == 0) amax_s[warp] = local_max;
-    __syncthreads();
+    named_bar_sync(bar_id, NT);
     float amax = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) amax = fmaxf(amax, amax_s[w]);
+    for (int w = 0; w < W; ++w) amax = fmaxf(amax, amax_s[w]);
     int e2 = 0;
     if (amax > 0.f) frexpf(amax, &e2);
     const int kx = amax > 0.f ? 15 - e2 : 0;  // amax * 2^kx in [2^14, 2^15)
     const float up = ldexpf(1.0f, kx);
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-        const int core = tid + 256 * j;
+        const int core = tid + NT * j;
         if (core >= cores) continue;
         const float *v = vals[j];
         const uint4 o = make_uint4(pack_half2(v[0] * up, v[2] * up), pack_half2(v[1] * up, v[3] * up),
@@ -1024,12 +1101,24 @@ __device__ void mma_prep_token(const float *x, long x_stride, const float *norm_
     if (tid == 0) x_inv[n] = ldexpf(1.0f, -kx);
 }
 
-__global__ void __launch_bounds__(256) ijb_mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
-                                                       int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
-                                                       float *x_inv) {
+__device__ void mma_prep_token(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch, int n,
+                               int n_pad, int use_dp4a, uint8_t *x16, float *x_inv) {
+    __shared__ float part_s[16], amax_s[16];
+    mma_prep_token_t<256>(x, x_stride, norm_w, eps, cols, batch, n, n_pad, use_dp4a, x16, x_inv,
+                          static_cast<int>(threadIdx.x), 0, part_s, amax_s, 0, false);
+}
+
+// One CTA of NT threads per token; NT is chosen so that each thread owns one
+// or two 8-wide cores (the prep is a chain of dependent steps, so more threads
+// per token shorten it).
+template <int NT>
+__global__ void __launch_bounds__(NT) ijb_mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
+                                                          int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
+                                                          float *x_inv) {
+    __shared__ float part_s[2 * (NT / 32)], amax_s[2 * (NT / 32)];
     pdl_trigger();
-    pdl_wait();
-    mma_prep_token(x, x_stride, norm_w, eps, cols, batch, static_cast<int>(blockIdx.x), n_pad, use_dp4a, x16, x_inv);
+    mma_prep_token_t<NT>(x, x_stride, norm_w, eps, cols, batch, static_cast<int>(blockIdx.x), n_pad, use_dp4a, x16,
+                         x_inv, static_cast<int>(threadIdx.x), 0, part_s, amax_s, 0, true);
 }
 
 // Bound of max|w| over GGUF blocks: Q4_K |d|*63*15 + |dmin|*63, Q6_K
@@ -1063,15 +1152,24 @@ cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, 
                             int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl) {
     if (cols % 256 || cols > kMaxCols || batch < 1 || n_pad > kMmaMaxN || n_pad % 16) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
+    const int cores = cols / 8;
+    const int nt = cores <= 256 ? 256 : (cores <= 512 ? 512 : 1024);
     cfg.gridDim = dim3(n_pad);
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(nt);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a, x16, x_inv);
+    if (nt == 256)
+        return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<256>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a,
+                                  x16, x_inv);
+    if (nt == 512)
+        return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<512>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a,
+                                  x16, x_inv);
+    return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<1024>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a,
+                              x16, x_inv);
 }
 
 cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks, int *out_max_bits, cudaStream_t stream) {
