@@ -388,10 +388,12 @@ def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
     """The CUDA-core GEMV (ijb_gemv_kernel, the batch-1 projection) timed
     alone: the 1B ffn_gate Q4_K shape and the Q6_K lm_head
     (config 1; a case may give a batch, up to 8), weights rotated over > 4x L2.
-    The launches are captured into one CUDA graph and the graph's replay is
-    timed with CUDA events (a 9.5 MB GEMV takes ~1.5 us at peak bandwidth, less
-    than a host launch, so a host loop would time the host); the host-loop time
-    is reported beside it."""
+    The launches are captured into one CUDA graph, chained with programmatic
+    dependent launch (IJB_GEMV_PDL: each GEMV's weight prefetch overlaps the
+    previous one's tail), and the graph's replay is timed with CUDA events (a
+    9.5 MB GEMV takes ~1.5 us at peak bandwidth, less than a host launch, so a
+    host loop would time the host); the graph without PDL and the host loop are
+    reported beside it."""
     import torch
     L = ijblib.load()
     out = {}
@@ -425,24 +427,28 @@ def gemv_roofline(cuda, peak, cases=GEMV_CASES, iters_min=20):
         b.record()
         torch.cuda.synchronize()
         ms_loop = a.elapsed_time(b) / iters
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            gs = torch.cuda.current_stream().cuda_stream
-            for i in range(iters):
-                ijblib.check(L.ijb_gemv(qtype, ws[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), cols, rows,
-                                        batch, 1, ctypes.c_void_p(gs)))
-        graph.replay()
-        torch.cuda.synchronize()
-        a.record()
-        graph.replay()
-        b.record()
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / iters
-        del graph
+        def graph_ms(flags):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                gs = torch.cuda.current_stream().cuda_stream
+                for i in range(iters):
+                    ijblib.check(L.ijb_gemv(qtype, ws[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), cols, rows,
+                                            batch, flags, ctypes.c_void_p(gs)))
+            graph.replay()
+            torch.cuda.synchronize()
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            del graph
+            return a.elapsed_time(b) / iters
+        ms_plain = graph_ms(1)
+        ms = graph_ms(1 | ijblib.GEMV_PDL)
         algo = nbytes + batch * (cols * 4 + rows * 4)
         out[name] = {"us_per_launch": ms * 1e3, "algorithmic_bytes": algo, "gbs": algo / (ms * 1e-3) / 1e9,
                      "frac": algo / (ms * 1e-3) / 1e9 / peak, "rotated_copies": copies, "batch": batch,
-                     "method": f"CUDA graph of {iters} launches", "us_per_launch_host_loop": ms_loop * 1e3}
+                     "method": f"CUDA graph of {iters} launches chained with programmatic dependent launch",
+                     "us_per_launch_graph_no_pdl": ms_plain * 1e3, "us_per_launch_host_loop": ms_loop * 1e3}
         del ws, wd
         torch.cuda.empty_cache()
     return out

@@ -180,9 +180,14 @@ long ijb_q6k_planar_row_bytes(int cols);
 int ijb_repack_q6k(const void *src_dev, void *dst_dev, int rows, int cols, void *stream);
 
 /* Standalone GEMV over one matrix: w_dev is GGUF layout for Q4_K, plane
- * layout (ijb_repack_q6k) for Q6_K; use_dp4a selects the INT8 activation path
- * (quantize_x32_cuda + gemv_q4_dp4a / gemv_q6_dp4a) or the FP32 path
- * (gemv_quant<T>), inferencer.cu:544-674.  batch <= 8. */
+ * layout (ijb_repack_q6k) for Q6_K; bit 0 of use_dp4a selects the INT8
+ * activation path (quantize_x32_cuda + gemv_q4_dp4a / gemv_q6_dp4a) or the
+ * FP32 path (gemv_quant<T>), inferencer.cu:544-674.  With IJB_GEMV_PDL also
+ * set, the kernel is launched with programmatic dependent launch: in a stream
+ * or graph of consecutive GEMVs each one's weight prefetch overlaps the tail of
+ * the one before (its activation is read only after that one completed).
+ * batch <= 8. */
+#define IJB_GEMV_PDL 2
 int ijb_gemv(int type, const void *w_dev, const float *x_dev, float *y_dev, int cols, int rows, int batch,
              int use_dp4a, void *stream);
 

@@ -116,8 +116,14 @@ struct ijb_engine {
     int *next_host = nullptr;  // pinned
     float *attn_partial = nullptr;
     int *attn_counters = nullptr;
-    uint8_t *x16 = nullptr;  // fp16 activation tile of the tensor-core path
+    uint8_t *x16 = nullptr;  // fp16 activation tiles of the tensor-core path, one per 64-token chunk
     float *x_inv = nullptr;
+    // steps wider than one tensor-core chunk run their chunks' launches on
+    // parallel branches: chunk c > 0 on side[(c - 1) % nside]
+    static constexpr int kMaxSide = 7;
+    int nside = 0;
+    cudaStream_t side[kMaxSide] = {};
+    cudaEvent_t ev_fork = nullptr, ev_join[kMaxSide] = {};
     int mma_max_split = 8, mma_split_cost = 1;
     int mma_bulk_out = 0;  // thread stores measured faster than per-row bulk copies
     int mma_min_batch = kMmaMinBatch;
@@ -162,6 +168,9 @@ int fail(ijb_engine *e, const std::exception &ex) {
 }
 
 cudaStream_t pick(ijb_engine *e, void *s) { return s ? static_cast<cudaStream_t>(s) : e->stream; }
+
+// Bytes of one 64-token fp16 activation tile (the widest row, kMaxCols).
+constexpr size_t kX16ChunkBytes = static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256;
 
 // ------------------------------------------------------------ GEMV params --
 
@@ -253,12 +262,25 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
     require(!x16_ready || (mma_ok && gn <= kMmaMaxN), "prepared activation without a single tensor-core chunk");
     const int cols = e->w[segs[0].w0].cols;
     if (mma_ok) {
+        // the chunks are independent (their own tokens, activation tile and outputs)
+        // and read the same weights, so they run side by side and the later reads
+        // of each weight tile hit L2
+        const int nchunks = (gn + kMmaMaxN - 1) / kMmaMaxN;
+        const int nbranch = std::min(nchunks - 1, e->nside);
+        if (nbranch > 0) {
+            ck(cudaEventRecord(e->ev_fork, s), "chunk fork");
+            for (int i = 0; i < nbranch; ++i) ck(cudaStreamWaitEvent(e->side[i], e->ev_fork, 0), "chunk fork");
+        }
         for (int t0 = 0; t0 < gn; t0 += kMmaMaxN) {
             const int tn = std::min(kMmaMaxN, gn - t0);
             const int n_pad = (tn + 15) / 16 * 16;
+            const int c = t0 / kMmaMaxN;
+            cudaStream_t cs = c == 0 || nbranch == 0 ? s : e->side[(c - 1) % nbranch];
+            uint8_t *x16 = e->x16 + static_cast<size_t>(c) * kX16ChunkBytes;
+            float *x_inv = e->x_inv + c * kMmaMaxN;
             if (!x16_ready) {
                 ck(mma_prep_launch(x + static_cast<long>(t0) * x_stride, x_stride, norm_w, d.eps, cols, tn, n_pad, dp,
-                                   e->x16, e->x_inv, s, e->mma_pdl),
+                                   x16, x_inv, cs, e->mma_pdl),
                    "activation prep launch");
                 ++g_launches;
             }
@@ -288,8 +310,8 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.cols = cols;
             m.batch = tn;
             m.n_pad = n_pad;
-            m.x16 = e->x16;
-            m.x_inv = e->x_inv;
+            m.x16 = x16;
+            m.x_inv = x_inv;
             m.rope_cos = e->rope_cos;
             m.rope_sin = e->rope_sin;
             m.half_head = e->head_dim / 2;
@@ -306,8 +328,12 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.status = e->status;
             m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->mma_max_split, e->mma_split_cost, &m.bps);
             m.bulk_out = e->mma_bulk_out;
-            ck(mma_gemm_launch(m, s, e->mma_pdl), "tensor-core GEMM launch");
+            ck(mma_gemm_launch(m, cs, e->mma_pdl), "tensor-core GEMM launch");
             ++g_launches;
+        }
+        for (int i = 0; i < nbranch; ++i) {
+            ck(cudaEventRecord(e->ev_join[i], e->side[i]), "chunk join");
+            ck(cudaStreamWaitEvent(s, e->ev_join[i], 0), "chunk join");
         }
         return;
     }
@@ -742,9 +768,16 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
                 w.has_mma = true;
             }
             ck(cudaStreamSynchronize(e->stream), "tensor-core weight copy");
-            e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256, "fp16 activation");
-            ck(cudaMemset(e->x16, 0, static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256), "fp16 activation clear");
-            e->x_inv = dev_alloc<float>(kMmaMaxN, "activation scales");
+            const int nchunks = (d.max_batch + kMmaMaxN - 1) / kMmaMaxN;
+            e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(nchunks) * kX16ChunkBytes, "fp16 activation");
+            ck(cudaMemset(e->x16, 0, static_cast<size_t>(nchunks) * kX16ChunkBytes), "fp16 activation clear");
+            e->x_inv = dev_alloc<float>(static_cast<size_t>(nchunks) * kMmaMaxN, "activation scales");
+            e->nside = std::min(nchunks - 1, ijb_engine::kMaxSide);
+            if (e->nside > 0) ck(cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming), "event");
+            for (int i = 0; i < e->nside; ++i) {
+                ck(cudaStreamCreateWithFlags(&e->side[i], cudaStreamNonBlocking), "stream");
+                ck(cudaEventCreateWithFlags(&e->ev_join[i], cudaEventDisableTiming), "event");
+            }
             const char *env = std::getenv("IJB_MMA_MIN_BATCH");  // diagnostic: path switch-over point
             if (env) e->mma_min_batch = std::max(1, std::atoi(env));
             // split-K tuning: most parts per tile, and the exchange's cost in block columns
@@ -865,6 +898,11 @@ void ijb_destroy(ijb_engine *e) {
     cudaFree(e->trace_q);
     if (e->ev_start) cudaEventDestroy(e->ev_start);
     if (e->ev_end) cudaEventDestroy(e->ev_end);
+    if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+    for (int i = 0; i < e->nside; ++i) {
+        if (e->ev_join[i]) cudaEventDestroy(e->ev_join[i]);
+        if (e->side[i]) cudaStreamDestroy(e->side[i]);
+    }
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
 }
@@ -1174,8 +1212,8 @@ int ijb_gemv(int type, const void *w, const float *x, float *y, int cols, int ro
         wt.data = static_cast<const uint8_t *>(w);
         wt.row_bytes = type == IJB_TYPE_Q4_K ? cols / 256 * kQ4Bytes : static_cast<int>(q6_planar_row_bytes(cols));
         ijb_model_desc d{};
-        d.use_dp4a = use_dp4a;
-        d.use_q6_dp4a = use_dp4a;
+        d.use_dp4a = use_dp4a & 1;
+        d.use_q6_dp4a = use_dp4a & 1;
         GemvParams p;
         std::memset(&p, 0, sizeof(p));
         p.cols = cols;
@@ -1183,7 +1221,7 @@ int ijb_gemv(int type, const void *w, const float *x, float *y, int cols, int ro
         p.x = x;
         p.x_stride = cols;
         add_seg(p, wt, nullptr, kEpiStore, y, rows, 0, d);
-        ck(gemv_launch(p, sms, static_cast<cudaStream_t>(stream), false), "GEMV launch");
+        ck(gemv_launch(p, sms, static_cast<cudaStream_t>(stream), (use_dp4a & IJB_GEMV_PDL) != 0), "GEMV launch");
         ++g_launches;
         return IJB_OK;
     } catch (const std::exception &ex) {

@@ -13,6 +13,7 @@ HEADER = os.path.join(REPO_ROOT, "include", "ijb200.h")
 
 OK = 0
 ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_CAPACITY, ERR_DEVICE = 1, 2, 3, 4, 5
+GEMV_PDL = 2  # IJB_GEMV_PDL: ijb_gemv flag bit
 
 _lib = None
 

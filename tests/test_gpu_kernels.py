@@ -152,3 +152,36 @@ def test_argmax_tie_rule(cuda, ties):
     idx = torch.zeros(1, dtype=torch.int32, device=cuda)
     lib.check(lib.load().ijb_argmax(vt.data_ptr(), v.size, idx.data_ptr(), None))
     assert int(idx.item()) == O.argmax(v)
+
+
+@pytest.mark.parametrize("dp4a", [1, 0])
+def test_gemv_pdl_chain_reads_previous_output(cuda, dp4a):
+    """IJB_GEMV_PDL: a chain y1 = W1 x, y2 = W2 y1, y3 = W1 y2 ... launched with
+    programmatic dependent launch on one stream, each GEMV reading the output
+    of the one before, matches the same chain launched without PDL (bit for
+    bit) and the oracle."""
+    import torch
+    L = lib.load()
+    rng = np.random.default_rng(21)
+    n = 2048
+    w1 = synth.quant_matrix(rng, 12, n, n)
+    w2 = synth.quant_matrix(rng, 12, n, n)
+    d1, d2 = _t(w1, cuda), _t(w2, cuda)
+    x = rng.standard_normal(n).astype(np.float32)
+    outs = {}
+    for flags in (dp4a, dp4a | lib.GEMV_PDL):
+        bufs = [_t(x[None, :], cuda)] + [torch.empty((1, n), dtype=torch.float32, device=cuda) for _ in range(6)]
+        s = torch.cuda.current_stream().cuda_stream
+        for i in range(6):
+            w = d1 if i % 2 == 0 else d2
+            lib.check(L.ijb_gemv(12, w.data_ptr(), bufs[i].data_ptr(), bufs[i + 1].data_ptr(), n, n, 1, flags,
+                                 ctypes.c_void_p(s)))
+        torch.cuda.synchronize()
+        outs[flags] = [b.cpu().numpy()[0] for b in bufs[1:]]
+    for a, b in zip(outs[dp4a], outs[dp4a | lib.GEMV_PDL]):
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+    prev = x
+    for i in range(6):  # each link against the oracle on the GPU's own input to it
+        ref = O.matvec(12, w1 if i % 2 == 0 else w2, prev, n, n, bool(dp4a), bool(dp4a))
+        assert rel_l2(outs[dp4a][i], ref) < 1e-5, i
+        prev = outs[dp4a][i]

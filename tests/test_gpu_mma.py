@@ -146,3 +146,35 @@ def test_ragged_step_tensor_core_vs_oracle(cuda, dp4a):
     else:
         assert errs.max() <= 1e-2, errs.max()
     assert agree / total >= 0.99, agree / total
+
+
+@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_HD128_G3], ids=lambda c: c.name)
+def test_wide_step_chunks_match_narrow_steps(cuda, cfg):
+    """A 150-token step runs its three 64-token tensor-core chunks on parallel
+    graph branches (own activation tiles, same weights).  Its logits and next
+    tokens equal, bit for bit, those of an engine with max_batch 64 that
+    decodes the same sequences in three steps of 64, 64 and 22 tokens (the same
+    chunks through the same kernels), over three steps with prefill."""
+    weights = synth.make_model(cfg, seed=12)
+    reqs = synth.ragged_requests(150, prompt_range=(3, 40), output_range=(8, 16), seed=4, vocab_limit=cfg.vocab)
+    wide = Engine(cfg, weights, context=64, max_batch=160, max_seqs=151)
+    narrow = Engine(cfg, weights, context=64, max_batch=64, max_seqs=151)
+    ws = [wide.seq_open() for _ in reqs]
+    ns = [narrow.seq_open() for _ in reqs]
+    cw = [wide.seq_prefill(s, r.prompt) for s, r in zip(ws, reqs)]
+    cn = [narrow.seq_prefill(s, r.prompt) for s, r in zip(ns, reqs)]
+    assert cw == cn
+    cuts = [(0, 64), (64, 128), (128, 150)]
+    for step in range(3):
+        out_w = list(wide.decode_step(ws, cw))
+        lw = wide.logits(150)
+        out_n, ln = [], []
+        for a, b in cuts:
+            out_n += list(narrow.decode_step(ns[a:b], cn[a:b]))
+            ln.append(narrow.logits(b - a))
+        ln = np.concatenate(ln)
+        assert out_w == out_n, step
+        assert np.array_equal(lw.view(np.uint32), ln.view(np.uint32)), step
+        cw, cn = out_w, out_n
+    wide.close()
+    narrow.close()
