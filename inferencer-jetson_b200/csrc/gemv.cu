@@ -29,7 +29,10 @@ namespace ijb {
 
 constexpr int kWarps = 8;          // 2 CTAs fit per SM, so the next kernel's CTA prefetches alongside
 constexpr int kThreads = kWarps * 32;
-constexpr int kDepth = 3;          // units in flight per warp
+#ifndef IJB_GEMV_DEPTH
+#define IJB_GEMV_DEPTH 3
+#endif
+constexpr int kDepth = IJB_GEMV_DEPTH;  // units in flight per warp
 constexpr int kSlotBytes = 1680;   // largest unit: 8 Q6_K blocks (8 Q4_K blocks: 1152)
 constexpr int kNormThreads = 256;  // the reference's RMSNorm reduction width
 
@@ -515,7 +518,13 @@ __device__ void epilogue(const GemvParams &p, const GemvSeg &s, int li, int b, f
 
 // ----------------------------------------------------------------- kernel --
 
-template <int B>
+// kLean: the launch is one segment of single-row items whose epilogue is a
+// store, a residual add or logits + argmax key (the lm_head, O and down
+// projections, standalone GEMVs); its loop keeps the segment's constants in
+// registers and steps its cursors without the general bookkeeping (item rows,
+// segment changes, pair epilogues), which otherwise costs more instructions per
+// unit than the dot products.
+template <int B, bool kLean>
 __global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) ijb_gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t cta_abort;
@@ -550,6 +559,74 @@ __global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) ijb_gemv_kernel(co
     pdl_wait();
     build_activation(p, L, smem);
     __syncthreads();
+
+    if constexpr (kLean) {
+        const GemvSeg &s0 = p.seg[0];
+        const int type = s0.type, dp4a = s0.dp4a, epi = s0.epi, rows = p.total_items;
+        const uint8_t *w0 = s0.w0;
+        const long row_bytes = s0.row_bytes, out_stride = s0.out_stride;
+        float *out = s0.out + s0.row_offset;
+        const int unit_full = type == kQ4K ? kUnitBlocks * kQ4Bytes : q6_unit_bytes(kUnitBlocks);
+        const int last_nb = nb - (upr - 1) * kUnitBlocks;
+        const uint32_t last_bytes = static_cast<uint32_t>(type == kQ4K ? last_nb * kQ4Bytes : q6_unit_bytes(last_nb));
+        int prow = pf.item, pu = pf.u;  // the next unit to fetch (the prologue fetched kDepth)
+        float acc[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] = 0.f;
+        unsigned long long best = 0ull;  // lane b: best argmax key of token b
+        int slot = 0, u = 0;
+        uint32_t phase = 0;
+        for (int row = gw; row < rows;) {
+            mbar_wait_bounded(bars + slot, phase, p.status, &cta_abort);
+            const uint8_t *unit = ring + slot * kSlotBytes;
+            const int nb_u = u == upr - 1 ? last_nb : kUnitBlocks;
+            if (type == kQ4K)
+                q4_unit<B>(unit, nb_u, u, lane, p, L, smem, dp4a, acc);
+            else
+                q6_unit<B>(unit, nb_u, u, lane, p, L, smem, dp4a, acc);
+            __syncwarp();
+            if (prow < rows) {  // refill this slot with the unit kDepth ahead
+                if (lane == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    const uint32_t bytes = pu == upr - 1 ? last_bytes : static_cast<uint32_t>(unit_full);
+                    mbar_arrive_expect_tx(bars + slot, bytes);
+                    bulk_g2s(ring + slot * kSlotBytes, w0 + prow * row_bytes + static_cast<long>(pu) * unit_full, bytes,
+                             bars + slot);
+                }
+                if (++pu == upr) {
+                    pu = 0;
+                    prow += GW;
+                }
+            }
+            if (++u == upr) {  // last unit of the row: reduce and write it
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const float y = warp_sum(acc[b]);
+                    acc[b] = 0.f;
+                    if (lane == b && b < p.batch) {
+                        float *o = out + b * out_stride + row;
+                        if (epi == kEpiAdd) {
+                            *o += y;
+                        } else {
+                            *o = y;
+                            if (epi == kEpiLogitsArgmax) {
+                                const unsigned long long key = argmax_key(y, s0.row_offset + row);
+                                best = key > best ? key : best;
+                            }
+                        }
+                    }
+                }
+                u = 0;
+                row += GW;
+            }
+            if (++slot == kDepth) {
+                slot = 0;
+                phase ^= 1u;
+            }
+        }
+        if (best && p.argmax_keys && lane < p.batch) atomicMax(p.argmax_keys + lane, best);
+        return;
+    }
 
     Cursor cur;
     cursor_start(p, gw, cur);
@@ -621,10 +698,12 @@ static cudaError_t prepare_attributes() {
     int optin = 0;
     e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
-    const void *fns[4] = {(const void *)ijb_gemv_kernel<1>, (const void *)ijb_gemv_kernel<2>, (const void *)ijb_gemv_kernel<4>,
-                          (const void *)ijb_gemv_kernel<8>};
+    const void *fns[8] = {(const void *)ijb_gemv_kernel<1, false>, (const void *)ijb_gemv_kernel<2, false>,
+                          (const void *)ijb_gemv_kernel<4, false>, (const void *)ijb_gemv_kernel<8, false>,
+                          (const void *)ijb_gemv_kernel<1, true>,  (const void *)ijb_gemv_kernel<2, true>,
+                          (const void *)ijb_gemv_kernel<4, true>,  (const void *)ijb_gemv_kernel<8, true>};
     int limit = optin;
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
         cudaFuncAttributes fa;
         e = cudaFuncGetAttributes(&fa, fns[i]);
         if (e != cudaSuccess) return e;
@@ -632,7 +711,7 @@ static cudaError_t prepare_attributes() {
         limit = lim < limit ? lim : limit;
     }
     limit &= ~127;
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
         e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
         if (e != cudaSuccess) return e;
     }
@@ -641,6 +720,13 @@ static cudaError_t prepare_attributes() {
 }
 
 cudaError_t gemv_prepare() { return prepare_attributes(); }
+
+// The lean loop's conditions (see ijb_gemv_kernel).
+static bool lean_launch(const GemvParams &p) {
+    const GemvSeg &s = p.seg[0];
+    return p.nseg == 1 && s.item0 == 0 && s.item_rows == 1 && s.w1 == nullptr &&
+           (s.epi == kEpiStore || s.epi == kEpiAdd || s.epi == kEpiLogitsArgmax);
+}
 
 template <int B>
 static cudaError_t launch_b(const GemvParams &p, int grid, int smem, cudaStream_t stream, bool pdl) {
@@ -654,7 +740,8 @@ static cudaError_t launch_b(const GemvParams &p, int grid, int smem, cudaStream_
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, ijb_gemv_kernel<B>, p);
+    if (lean_launch(p)) return cudaLaunchKernelEx(&cfg, ijb_gemv_kernel<B, true>, p);
+    return cudaLaunchKernelEx(&cfg, ijb_gemv_kernel<B, false>, p);
 }
 
 // Tokens the kernel instance is compiled for: the smallest of 1, 2, 4, 8
