@@ -444,6 +444,44 @@ __device__ __forceinline__ const uint8_t *unit_src(const GemvParams &p, const Cu
     return base + static_cast<long>(row) * s.row_bytes + c.u * q6_unit_bytes(kUnitBlocks);
 }
 
+// A segment's fields that the main loop needs per unit, held in registers:
+// what the prefetching cursor needs to address a unit ...
+struct FetchSeg {
+    const uint8_t *w0, *w1;
+    long row_bytes;
+    int item0, item_end, item_rows;
+    uint32_t unit_bytes, last_bytes;
+    __device__ __forceinline__ void load(const GemvParams &p, int si, int last_nb) {
+        const GemvSeg &s = p.seg[si];
+        w0 = s.w0;
+        w1 = s.w1;
+        row_bytes = s.row_bytes;
+        item0 = s.item0;
+        item_end = s.item0 + s.nitems;
+        item_rows = s.item_rows;
+        unit_bytes = static_cast<uint32_t>(s.type == kQ4K ? kUnitBlocks * kQ4Bytes : q6_unit_bytes(kUnitBlocks));
+        last_bytes = static_cast<uint32_t>(s.type == kQ4K ? last_nb * kQ4Bytes : q6_unit_bytes(last_nb));
+    }
+    // Row r of item `item` (a pair's second row is the same row of w1, else the next row).
+    __device__ __forceinline__ const uint8_t *row_ptr(int item, int r) const {
+        const int li = item - item0;
+        if (w1) return (r ? w1 : w0) + static_cast<long>(li) * row_bytes;
+        return w0 + static_cast<long>(li * item_rows + r) * row_bytes;
+    }
+};
+// ... and what the consuming cursor needs to compute and finish it.
+struct UseSeg {
+    int item0, item_end, item_rows, type, dp4a;
+    __device__ __forceinline__ void load(const GemvParams &p, int si) {
+        const GemvSeg &s = p.seg[si];
+        item0 = s.item0;
+        item_end = s.item0 + s.nitems;
+        item_rows = s.item_rows;
+        type = s.type;
+        dp4a = s.dp4a;
+    }
+};
+
 // ----------------------------------------------------------- epilogue --
 
 // Writes one finished item (1 or 2 rows) for token b; y0/y1 are the rows' dots.
@@ -628,56 +666,87 @@ __global__ void __launch_bounds__(kThreads, (B == 1 ? 4 : 2)) ijb_gemv_kernel(co
         return;
     }
 
-    Cursor cur;
-    cursor_start(p, gw, cur);
+    // General loop: several segments, two-row items (RoPE pairs, gate/up
+    // pairs).  Each cursor keeps its segment's fields in registers and reloads
+    // them only when it crosses into the next segment.
+    const int last_nb = nb - (upr - 1) * kUnitBlocks;
+    UseSeg cs;    // the consuming cursor's segment
+    FetchSeg ps;  // the prefetching cursor's segment
+    int cseg = seg_of_item(p, gw), item = gw, r = 0, u = 0;
+    cs.load(p, cseg);
+    int pseg = pf.seg, pitem = pf.item, pr = pf.r, pu = pf.u;
+    ps.load(p, pseg, last_nb);
     float acc[B];
     float res0[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[b] = res0[b] = 0.f;
     unsigned long long best = 0ull;  // lane b: best argmax key of token b
-    for (uint32_t k = 0; cur.item < p.total_items; ++k) {
-        const int slot = k % kDepth;
-        mbar_wait_bounded(bars + slot, (k / kDepth) & 1, p.status, &cta_abort);
-        const GemvSeg &sg = p.seg[cur.seg];
-        const int nb_u = min(kUnitBlocks, nb - cur.u * kUnitBlocks);
+    const int total = p.total_items;
+    int slot = 0;
+    uint32_t phase = 0;
+    while (item < total) {
+        mbar_wait_bounded(bars + slot, phase, p.status, &cta_abort);
+        const int nb_u = u == upr - 1 ? last_nb : kUnitBlocks;
         const uint8_t *unit = ring + slot * kSlotBytes;
-        if (sg.type == kQ4K)
-            q4_unit<B>(unit, nb_u, cur.u, lane, p, L, smem, sg.dp4a, acc);
+        if (cs.type == kQ4K)
+            q4_unit<B>(unit, nb_u, u, lane, p, L, smem, cs.dp4a, acc);
         else
-            q6_unit<B>(unit, nb_u, cur.u, lane, p, L, smem, sg.dp4a, acc);
+            q6_unit<B>(unit, nb_u, u, lane, p, L, smem, cs.dp4a, acc);
         __syncwarp();
         // refill this slot with the unit kDepth ahead
-        if (pf.item < p.total_items) {
+        if (pitem < total) {
             if (lane == 0) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                uint32_t bytes;
-                const uint8_t *src = unit_src(p, pf, nb, bytes);
+                const uint32_t bytes = pu == upr - 1 ? ps.last_bytes : ps.unit_bytes;
+                const uint8_t *src = ps.row_ptr(pitem, pr) + static_cast<long>(pu) * ps.unit_bytes;
                 mbar_arrive_expect_tx(bars + slot, bytes);
                 bulk_g2s(ring + slot * kSlotBytes, src, bytes, bars + slot);
             }
-            cursor_next(p, GW, upr, pf);
+            if (++pu == upr) {
+                pu = 0;
+                if (++pr == ps.item_rows) {
+                    pr = 0;
+                    pitem += GW;
+                    if (pitem >= ps.item_end && pitem < total) {  // items only grow
+                        while (pseg + 1 < p.nseg && pitem >= p.seg[pseg + 1].item0) ++pseg;
+                        ps.load(p, pseg, last_nb);
+                    }
+                }
+            }
         }
-        if (cur.u == upr - 1) {  // last unit of a row: reduce it
+        if (++u == upr) {  // last unit of a row: reduce it
+            u = 0;
             float y[B];
 #pragma unroll
             for (int b = 0; b < B; ++b) {
                 y[b] = warp_sum(acc[b]);
                 acc[b] = 0.f;
             }
-            if (cur.r + 1 < sg.item_rows) {
+            if (r + 1 < cs.item_rows) {
 #pragma unroll
                 for (int b = 0; b < B; ++b) res0[b] = y[b];
+                ++r;
             } else {
-                const int li = cur.item - sg.item0;
+                const GemvSeg &sg = p.seg[cseg];
+                const int li = item - cs.item0;
 #pragma unroll
                 for (int b = 0; b < B; ++b)
                     if (lane == b && b < p.batch) {
-                        if (sg.item_rows == 2) epilogue(p, sg, li, b, res0[b], y[b], best);
+                        if (cs.item_rows == 2) epilogue(p, sg, li, b, res0[b], y[b], best);
                         else epilogue(p, sg, li, b, y[b], 0.f, best);
                     }
+                r = 0;
+                item += GW;
+                if (item >= cs.item_end && item < total) {
+                    while (cseg + 1 < p.nseg && item >= p.seg[cseg + 1].item0) ++cseg;
+                    cs.load(p, cseg);
+                }
             }
         }
-        cursor_next(p, GW, upr, cur);
+        if (++slot == kDepth) {
+            slot = 0;
+            phase ^= 1u;
+        }
     }
     if (best && p.argmax_keys && lane < p.batch) atomicMax(p.argmax_keys + lane, best);
 }
