@@ -257,22 +257,23 @@ __device__ __forceinline__ void q4_unit(const uint8_t *unit, int nb_u, int u, in
             const int bu = b * U + u;
             const uint4 *xl = reinterpret_cast<const uint4 *>(smem + L.q4x) + bu * 128 + lane;
             const uint4 l0 = xl[0], l1 = xl[32], h0 = xl[64], h1 = xl[96];
-            int dl = dp4a(lo[0], l0.x, 0);
+            // four independent chains of four (integer sums: the order is free)
+            int dl = dp4a(lo[0], l0.x, 0), dl2 = dp4a(lo[4], l1.x, 0);
+            int dh = dp4a(hi[0], h0.x, 0), dh2 = dp4a(hi[4], h1.x, 0);
             dl = dp4a(lo[1], l0.y, dl);
-            dl = dp4a(lo[2], l0.z, dl);
-            dl = dp4a(lo[3], l0.w, dl);
-            dl = dp4a(lo[4], l1.x, dl);
-            dl = dp4a(lo[5], l1.y, dl);
-            dl = dp4a(lo[6], l1.z, dl);
-            dl = dp4a(lo[7], l1.w, dl);
-            int dh = dp4a(hi[0], h0.x, 0);
+            dl2 = dp4a(lo[5], l1.y, dl2);
             dh = dp4a(hi[1], h0.y, dh);
+            dh2 = dp4a(hi[5], h1.y, dh2);
+            dl = dp4a(lo[2], l0.z, dl);
+            dl2 = dp4a(lo[6], l1.z, dl2);
             dh = dp4a(hi[2], h0.z, dh);
+            dh2 = dp4a(hi[6], h1.z, dh2);
+            dl = dp4a(lo[3], l0.w, dl);
+            dl2 = dp4a(lo[7], l1.w, dl2);
             dh = dp4a(hi[3], h0.w, dh);
-            dh = dp4a(hi[4], h1.x, dh);
-            dh = dp4a(hi[5], h1.y, dh);
-            dh = dp4a(hi[6], h1.z, dh);
-            dh = dp4a(hi[7], h1.w, dh);
+            dh2 = dp4a(hi[7], h1.w, dh2);
+            dl += dl2;
+            dh += dh2;
             const int4 s4 = reinterpret_cast<const int4 *>(smem + L.q4s)[bu * 32 + lane];
             const float2 sx = reinterpret_cast<const float2 *>(smem + L.q4f)[bu * 32 + lane];
             float t = fmaf(a_lo, static_cast<float>(dl), -b_lo * static_cast<float>(s4.x + s4.y)) * sx.x;
@@ -822,7 +823,15 @@ static cudaError_t launch_group(const GemvParams &p, int num_sms, cudaStream_t s
     const int smem = smem_layout(p.cols, inst, p.need_q4, p.need_q6, p.need_f).total;
     if (p.total_items < 1) return cudaSuccess;
     switch (inst) {
-        case 1: return launch_b<1>(p, 2 * num_sms, smem, stream, pdl);
+        case 1: {
+            // two CTAs per SM leave room for the next kernel's CTAs; a long
+            // stream (>= 32 units per warp at two per SM, e.g. the lm_head) runs
+            // four, whose extra copies in flight lift it from ~0.61 to ~0.70 of
+            // HBM bandwidth on B200 (short ones lose to the extra prologues)
+            const long units = static_cast<long>(p.total_items) * p.seg[0].item_rows * ((p.cols / 256 + kUnitBlocks - 1) / kUnitBlocks);
+            const int per_sm = units >= 32L * 2 * num_sms * kWarps ? 4 : 2;
+            return launch_b<1>(p, per_sm * num_sms, smem, stream, pdl);
+        }
         case 2: return launch_b<2>(p, num_sms, smem, stream, pdl);
         case 4: return launch_b<4>(p, num_sms, smem, stream, pdl);
         default: return launch_b<8>(p, num_sms, smem, stream, pdl);
