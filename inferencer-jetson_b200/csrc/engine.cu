@@ -128,6 +128,7 @@ struct ijb_engine {
     int mma_bulk_out = 0;  // thread stores measured faster than per-row bulk copies
     int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
+    int attn_stream_min = 1;  // smallest step that uses the streaming attention
     uint32_t *status = nullptr;
     unsigned long long *scratch_key = nullptr;
 
@@ -434,7 +435,7 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool t
         a.work = e->attn_counters + d.max_batch * d.kv_heads;
         a.num_ctas = e->num_sms;
         a.status = e->status;
-        if (!e->kv_maps.empty()) {
+        if (!e->kv_maps.empty() && n >= e->attn_stream_min) {
             a.kv_map = e->kv_maps[l];
             a.has_map = 1;
         }
@@ -654,6 +655,11 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->attn_pdl = env2 && env2[0] == '1';
             env2 = std::getenv("IJB_ATTN_PREP");
             e->attn_prep = env2 && env2[0] == '1';
+            // IJB_ATTN_STREAM_MIN: steps of fewer tokens use the CUDA-core split
+            // kernel (measured on B200: a 1B batch-1 step 0.81 ms with the
+            // streaming kernel, 0.88 ms with the split kernel)
+            env2 = std::getenv("IJB_ATTN_STREAM_MIN");
+            if (env2) e->attn_stream_min = std::max(1, std::atoi(env2));
         }
         ck(attention_prepare(), "attention attributes");
         ck(cudaEventCreate(&e->ev_start), "event");
