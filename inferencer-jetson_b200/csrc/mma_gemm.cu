@@ -1108,9 +1108,11 @@ __device__ void mma_prep_token(const float *x, long x_stride, const float *norm_
                           static_cast<int>(threadIdx.x), 0, part_s, amax_s, 0, false);
 }
 
-// One CTA of NT threads per token; NT is chosen so that each thread owns one
-// or two 8-wide cores (the prep is a chain of dependent steps, so more threads
-// per token shorten it).
+// One CTA of NT threads per token.  256 for every row width: wider CTAs for
+// the 8192-wide input of the down projection shorten the prep alone but make the
+// step slower (measured on B200, ragged64: 1.794 ms with 1024 threads for it,
+// 1.784 ms with 256), presumably because they hold whole SMs that the next
+// GEMM's CTAs wait for.
 template <int NT>
 __global__ void __launch_bounds__(NT) ijb_mma_prep_kernel(const float *x, long x_stride, const float *norm_w, float eps,
                                                           int cols, int batch, int n_pad, int use_dp4a, uint8_t *x16,
@@ -1152,8 +1154,7 @@ cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, 
                             int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl) {
     if (cols % 256 || cols > kMaxCols || batch < 1 || n_pad > kMmaMaxN || n_pad % 16) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    const int cores = cols / 8;
-    const int nt = cores <= 256 ? 256 : (cores <= 512 ? 512 : 1024);
+    const int nt = 256;
     cfg.gridDim = dim3(n_pad);
     cfg.blockDim = dim3(nt);
     cfg.stream = stream;
