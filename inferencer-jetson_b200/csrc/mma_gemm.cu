@@ -1154,23 +1154,16 @@ cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, 
                             int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl) {
     if (cols % 256 || cols > kMaxCols || batch < 1 || n_pad > kMmaMaxN || n_pad % 16) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    const int nt = 256;
     cfg.gridDim = dim3(n_pad);
-    cfg.blockDim = dim3(nt);
+    cfg.blockDim = dim3(256);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (nt == 256)
-        return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<256>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a,
-                                  x16, x_inv);
-    if (nt == 512)
-        return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<512>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a,
-                                  x16, x_inv);
-    return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<1024>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a,
-                              x16, x_inv);
+    return cudaLaunchKernelEx(&cfg, ijb_mma_prep_kernel<256>, x, x_stride, norm_w, eps, cols, batch, n_pad, use_dp4a, x16,
+                              x_inv);
 }
 
 cudaError_t mma_scale_scan_launch(int type, const uint8_t *w, long nblocks, int *out_max_bits, cudaStream_t stream) {
