@@ -158,6 +158,21 @@ int ijb_seq_length(const ijb_engine *engine, int seq_id);
  * copied to the host; the call returns after the step completed. */
 int ijb_decode_step(ijb_engine *engine, int n, const int *seq_ids, const int *tokens, int *next_tokens);
 
+/* Greedy generation of one sequence with the token feedback on the device:
+ * the reference's decode loop (main, inferencer.cu:1870-1883) from `next`
+ * (first_token, the prefill's argmax) at the sequence's next position.  A
+ * token equal to one of stop_ids (n_stop <= 16) ends the loop and is not
+ * emitted; otherwise it is emitted, and the loop ends after max_tokens
+ * emitted tokens or when the position to feed it at reaches the context.
+ * out_tokens (room for max_tokens) receives the emitted tokens, *n_out their
+ * count; the sequence's cached length grows by the positions fed.  Each step
+ * is the batch-1 step graph followed by a one-thread kernel that turns its
+ * argmax into the next step's token, position and KV slot, so steps are
+ * queued without a host round trip (the host checks the state once per 8
+ * steps; steps queued past the end recompute the last position). */
+int ijb_generate(ijb_engine *engine, int seq_id, int first_token, int max_tokens, const int *stop_ids, int n_stop,
+                 int *out_tokens, int *n_out);
+
 /* Prefill one sequence with n tokens (chunks of max_batch); *next_token is
  * the argmax after the last token. */
 int ijb_seq_prefill(ijb_engine *engine, int seq_id, const int *tokens, int n, int *next_token);

@@ -133,6 +133,11 @@ struct ijb_engine {
     unsigned long long *scratch_key = nullptr;
 
     std::unordered_map<int, StepGraph> graphs;  // key: (n * 2 + need_logits) * 2 + traced
+    // device-side greedy loop (ijb_generate): its step graph, state, outputs, stop ids
+    StepGraph gen_graph;
+    GenState *gen_state = nullptr;
+    int *gen_out = nullptr;
+    int *gen_stop = nullptr;
     // debug traces of traced steps (allocated on first use): the residual after
     // every layer [max_batch][layers][dim] and the four int8 activations the
     // INT8 path quantises per layer [max_batch][layers][trace_q_stride]
@@ -169,6 +174,9 @@ int fail(ijb_engine *e, const std::exception &ex) {
 }
 
 cudaStream_t pick(ijb_engine *e, void *s) { return s ? static_cast<cudaStream_t>(s) : e->stream; }
+
+constexpr int kGenMaxStop = 16;  // stop ids of ijb_generate
+constexpr int kGenRound = 8;     // ijb_generate steps queued per host check
 
 // Bytes of one 64-token fp16 activation tile (the widest row, kMaxCols).
 constexpr size_t kX16ChunkBytes = static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256;
@@ -875,6 +883,10 @@ void ijb_destroy(ijb_engine *e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     for (auto &kv : e->graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (e->gen_graph.exec) cudaGraphExecDestroy(e->gen_graph.exec);
+    cudaFree(e->gen_state);
+    cudaFree(e->gen_out);
+    cudaFree(e->gen_stop);
     for (auto &w : e->w) {
         if (w.owned) cudaFree(w.owned);
         if (w.mma_owned) cudaFree(w.mma_owned);
@@ -1132,6 +1144,111 @@ int ijb_seq_close(ijb_engine *e, int seq) {
 int ijb_seq_length(const ijb_engine *e, int seq) {
     if (!e || seq < 0 || seq >= e->d.max_seqs || !e->seq_used[seq]) return -1;
     return e->seq_len[seq];
+}
+
+int ijb_generate(ijb_engine *e, int seq, int first_token, int max_tokens, const int *stop_ids, int n_stop,
+                 int *out_tokens, int *n_out) {
+    try {
+        require(e != nullptr && out_tokens != nullptr && n_out != nullptr, "bad arguments");
+        const ijb_model_desc &d = e->d;
+        require(seq >= 0 && seq < d.max_seqs && e->seq_used[seq], "unknown sequence id");
+        require(first_token >= 0 && first_token < d.vocab, "Token or position outside model context");
+        require(max_tokens >= 0 && n_stop >= 0 && n_stop <= kGenMaxStop && (n_stop == 0 || stop_ids),
+                "bad generate limits (stop ids: at most 16)");
+        *n_out = 0;
+        const int pos0 = e->seq_len[seq];
+        // the reference loop's first iteration, on the host: `next` from the prefill
+        for (int i = 0; i < n_stop; ++i)
+            if (first_token == stop_ids[i]) return IJB_OK;
+        if (max_tokens == 0) return IJB_OK;
+        out_tokens[0] = first_token;
+        *n_out = 1;
+        if (max_tokens == 1 || pos0 >= d.context) return IJB_OK;
+        // at most this many steps feed a new position; their pages are allocated now
+        const int steps = std::min(max_tokens - 1, d.context - pos0);
+        int *mt = e->meta_host;
+        std::memset(mt, 0, 4 * d.max_batch * sizeof(int));
+        for (int k = steps - 1; k >= 0; --k) slot_for(e, seq, pos0 + k);
+        mt[0] = first_token;
+        mt[d.max_batch] = seq;
+        mt[2 * d.max_batch] = pos0;
+        mt[3 * d.max_batch] = slot_for(e, seq, pos0);
+        if (!e->gen_state) {
+            e->gen_state = dev_alloc<GenState>(1, "generate state");
+            e->gen_out = dev_alloc<int>(d.context + 1, "generate output");
+            e->gen_stop = dev_alloc<int>(kGenMaxStop, "generate stop ids");
+        }
+        GenState g{};
+        g.count = 1;
+        g.max_tokens = max_tokens;
+        g.context = d.context;
+        g.n_stop = n_stop;
+        g.seq = seq;
+        g.page_size = d.page_size;
+        g.max_pages_per_seq = e->max_pages_per_seq;
+        cudaStream_t s = e->stream;
+        ck(cudaMemcpyAsync(e->meta_dev, mt, 4 * d.max_batch * sizeof(int), cudaMemcpyHostToDevice, s), "meta H2D");
+        ck(cudaMemcpyAsync(e->gen_state, &g, sizeof(g), cudaMemcpyHostToDevice, s), "generate state H2D");
+        if (n_stop) ck(cudaMemcpyAsync(e->gen_stop, stop_ids, n_stop * sizeof(int), cudaMemcpyHostToDevice, s), "stop H2D");
+        ck(cudaStreamSynchronize(s), "generate setup");  // the host buffers above are stack / staging memory
+        if (!e->gen_graph.exec) {
+            // one batch-1 step reading its inputs from meta_dev, then the advance kernel
+            cudaGraph_t graph;
+            const uint64_t before = g_launches.load();
+            ck(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+            try {
+                enqueue_step(e, 1, true, s, false);
+                ck(gen_advance_launch(e->gen_state, e->next_dev, e->meta_dev, d.max_batch, e->page_table_dev,
+                                      e->gen_stop, e->gen_out, s),
+                   "generate advance launch");
+                ++g_launches;
+            } catch (...) {
+                cudaStreamEndCapture(s, &graph);
+                throw;
+            }
+            ck(cudaStreamEndCapture(s, &graph), "end capture");
+            e->gen_graph.launches = g_launches.load() - before;
+            g_launches.store(before);
+            cudaError_t ie = cudaGraphInstantiate(&e->gen_graph.exec, graph, 0);
+            cudaGraphDestroy(graph);
+            ck(ie, "graph instantiate");
+        }
+        // steps are queued in rounds without waiting for their tokens; the host
+        // reads the state once per round (steps queued past the end recompute the
+        // last position, see the advance kernel)
+        ck(cudaEventRecord(e->ev_start, s), "generate timer start");
+        int queued = 0;
+        while (queued < steps) {
+            const int round = std::min(kGenRound, steps - queued);
+            for (int k = 0; k < round; ++k) ck(cudaGraphLaunch(e->gen_graph.exec, s), "graph launch");
+            g_launches += e->gen_graph.launches * round;
+            queued += round;
+            ck(cudaMemcpyAsync(&g, e->gen_state, sizeof(g), cudaMemcpyDeviceToHost, s), "generate state D2H");
+            ck(cudaStreamSynchronize(s), "generate synchronize");
+            if (g.done) break;
+        }
+        ck(cudaEventRecord(e->ev_end, s), "generate timer end");
+        ck(cudaMemcpyAsync(out_tokens + 1, e->gen_out + 1, (g.count - 1) * sizeof(int), cudaMemcpyDeviceToHost, s),
+           "generate output D2H");
+        ck(cudaStreamSynchronize(s), "generate synchronize");
+        float ms = 0.f;
+        ck(cudaEventElapsedTime(&ms, e->ev_start, e->ev_end), "generate timer");
+        e->last_step_ms = ms / static_cast<float>(queued);
+        e->last_n = 1;
+        check_device_status(e);
+        *n_out = g.count;
+        e->seq_len[seq] = pos0 + g.processed;
+        // pages allocated for positions the loop did not reach go back to the pool
+        auto &pages = e->seq_pages[seq];
+        const size_t keep = (e->seq_len[seq] + d.page_size - 1) / d.page_size;
+        while (pages.size() > keep) {
+            e->free_pages.push_back(pages.back());
+            pages.pop_back();
+        }
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
 }
 
 int ijb_decode_step(ijb_engine *e, int n, const int *seq_ids, const int *tokens, int *next_tokens) {

@@ -247,6 +247,45 @@ cudaError_t wait_probe_launch(uint32_t *status, uint64_t limit_ns, cudaStream_t 
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------- device-side greedy loop --
+
+// After one batch-1 step of ijb_generate: the step's next token (next[0]) is
+// the reference generate loop's `next` (inferencer.cu:1870-1883): a stop id
+// ends the loop unemitted; otherwise it is emitted, and the loop ends after
+// max_tokens emitted tokens or when the position to feed it at reaches the
+// context; otherwise it becomes the next step's input at the next position,
+// whose KV slot comes from the sequence's page table (pages allocated by the
+// host beforehand).  Once done, the step's inputs stay as they are, so any
+// step already queued recomputes the last position: the same K/V, written to
+// the same slot.
+__global__ void ijb_gen_advance_kernel(GenState *g, const int *next, int *meta, int max_batch, const int *page_table,
+                                       const int *stop_ids, int *out) {
+    if (threadIdx.x != 0 || g->done) return;
+    const int t = next[0];
+    ++g->processed;  // the token in meta was fed at its position
+    for (int i = 0; i < g->n_stop; ++i)
+        if (t == stop_ids[i]) {
+            g->done = 1;
+            return;
+        }
+    out[g->count++] = t;
+    const int pos = meta[2 * max_batch] + 1;
+    if (g->count >= g->max_tokens || pos >= g->context) {
+        g->done = 1;
+        return;
+    }
+    const int ps = g->page_size;
+    meta[0] = t;
+    meta[2 * max_batch] = pos;
+    meta[3 * max_batch] = page_table[static_cast<long>(g->seq) * g->max_pages_per_seq + pos / ps] * ps + pos % ps;
+}
+
+cudaError_t gen_advance_launch(GenState *g, const int *next, int *meta, int max_batch, const int *page_table,
+                               const int *stop_ids, int *out, cudaStream_t stream) {
+    ijb_gen_advance_kernel<<<1, 32, 0, stream>>>(g, next, meta, max_batch, page_table, stop_ids, out);
+    return cudaGetLastError();
+}
+
 cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *tokens, cudaStream_t stream,
                                   bool pdl) {
     cudaLaunchAttribute attr[1];

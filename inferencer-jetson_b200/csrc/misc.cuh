@@ -29,4 +29,16 @@ cudaError_t wait_probe_launch(uint32_t *status, uint64_t limit_ns, cudaStream_t 
 
 cudaError_t keys_to_tokens_launch(const unsigned long long *keys, int n, int *tokens, cudaStream_t stream, bool pdl);
 
+// State of the device-side greedy loop of one sequence (ijb_generate).
+struct GenState {
+    int done;       // the loop has ended (stop id, max_tokens or context)
+    int count;      // tokens emitted so far
+    int processed;  // positions fed to the model by the loop's steps
+    int max_tokens, context, n_stop, seq, page_size, max_pages_per_seq;
+};
+// One thread: consumes the step's next token and sets up the next step's meta
+// (token, position, KV slot) in place, or ends the loop.
+cudaError_t gen_advance_launch(GenState *g, const int *next, int *meta, int max_batch, const int *page_table,
+                               const int *stop_ids, int *out, cudaStream_t stream);
+
 }  // namespace ijb

@@ -160,6 +160,16 @@ class Engine:
         _L.check(self.lib.ijb_decode_step(self.h, n, s, t, out), self.h)
         return np.frombuffer(out, dtype=np.int32).copy()
 
+    def generate(self, seq_id: int, first_token: int, max_tokens: int, stop_ids=()) -> list:
+        """ijb_generate: greedy tokens from first_token on, fed back on the device
+        (the reference's decode loop: stop ids end it unemitted)."""
+        out = (ctypes.c_int * max(1, max_tokens))()
+        stops = (ctypes.c_int * max(1, len(stop_ids)))(*[int(v) for v in stop_ids])
+        n = ctypes.c_int()
+        _L.check(self.lib.ijb_generate(self.h, int(seq_id), int(first_token), int(max_tokens), stops, len(stop_ids),
+                                       out, ctypes.byref(n)), self.h)
+        return [int(v) for v in out[:n.value]]
+
     def probe_wait_timeout(self, limit_ns: int) -> int:
         """ijb_probe_wait_timeout: the status code of a step whose bounded wait expired."""
         return int(self.lib.ijb_probe_wait_timeout(self.h, int(limit_ns)))

@@ -70,6 +70,7 @@ def load():
         "ijb_seq_close": ([P, I], I),
         "ijb_seq_length": ([P, I], I),
         "ijb_decode_step": ([P, I, IP, IP, IP], I),
+        "ijb_generate": ([P, I, I, I, IP, I, IP, IP], I),
         "ijb_seq_prefill": ([P, I, IP, I, IP], I),
         "ijb_argmax": ([P, I, P, P], I),
         "ijb_argmax_noalloc": ([P, I, P, P], I),
