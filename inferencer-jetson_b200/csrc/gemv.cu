@@ -84,6 +84,13 @@ __host__ __device__ inline SmemLayout smem_layout(int cols, int batch, int need_
     return L;
 }
 
+// Lane of quarter j (0..3) of block blk (0..7) of a Q6_K unit, and back: blocks
+// b and b + 4 share each 8-lane phase of a warp's 16-byte shared-memory loads,
+// and as the unit's block bodies are 208 bytes apart their 64-byte pieces fall
+// in opposite halves of the banks (blocks b and b + 1 would overlap in 4 banks).
+__device__ __forceinline__ int q6_lane(int blk, int j) { return 8 * (blk & 3) + 4 * (blk >> 2) + j; }
+__device__ __forceinline__ int q6_blk(int lane) { return ((lane >> 3) & 3) + 4 * ((lane >> 2) & 1); }
+
 // ---------------------------------------------------------------- prologue --
 
 // Builds the activation of every token in shared memory.  RMSNorm follows
@@ -177,7 +184,7 @@ __device__ void build_activation(const GemvParams &p, const SmemLayout &L, uint8
                     const int bu = b * U + u;
                     if (p.need_q6) {
                         const int g = i / 128, pt = (i % 128) / 32, l = i % 32, h = l / 16;
-                        const int lane = 4 * blk + 2 * g + h;
+                        const int lane = q6_lane(blk, 2 * g + h);
                         *reinterpret_cast<uint2 *>(smem + L.q6x + ((bu * 4 + pt) * 32 + lane) * 16 + (l % 16)) =
                             make_uint2(packed[0], packed[1]);
                         if ((l % 16) == 0) reinterpret_cast<int *>(smem + L.q6s)[(bu * 32 + lane) * 4 + pt] = hs;
@@ -309,7 +316,7 @@ __device__ __forceinline__ void q4_unit(const uint8_t *unit, int nb_u, int u, in
     }
 }
 
-// One Q6_K unit in the unit layout (gemv.cuh).  Lane -> block lane/4,
+// One Q6_K unit in the unit layout (gemv.cuh).  Lane -> block q6_blk(lane),
 // 128-weight group g = (lane/2)%2 and 16 positions l0 = (lane%2)*16: 64
 // weights, one scale per part.  Weight (g, part, l) is
 // d * scale[g*8+part*2+l/16] * (q - 32), q assembled as in q6_value
@@ -317,7 +324,7 @@ __device__ __forceinline__ void q4_unit(const uint8_t *unit, int nb_u, int u, in
 template <int B>
 __device__ __forceinline__ void q6_unit(const uint8_t *unit, int nb_u, int u, int lane, const GemvParams &p,
                                         const SmemLayout &L, const uint8_t *smem, int use_dp4a, float (&acc)[B]) {
-    const int blk = lane >> 2;
+    const int blk = q6_blk(lane);
     if (blk >= nb_u) return;
     const int gblk0 = u * kUnitBlocks;
     const int g = (lane >> 1) & 1, l0 = (lane & 1) * 16;
