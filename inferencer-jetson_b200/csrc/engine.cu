@@ -148,6 +148,7 @@ struct ijb_engine {
     bool pdl = false;      // programmatic dependent launch between the step's kernels
     bool mma_pdl = true;   // the same for the tensor-core path's prep and GEMM launches
     bool attn_pdl = false;   // the same for the attention launches of tensor-core steps
+    bool small_attn_pdl = true;  // the same for the attention and O launches of CUDA-core steps
     bool attn_prep = false;  // the attention finish kernel builds the O projection's activation tile
     float last_step_ms = 0.f;
     std::string err;
@@ -229,8 +230,8 @@ GemvParams base_params(ijb_engine *e, int cols, int batch, const float *x, long 
     return p;
 }
 
-void launch_gemv(ijb_engine *e, const GemvParams &p, cudaStream_t s, bool pdl) {
-    ck(gemv_launch(p, e->num_sms, s, pdl && e->pdl), "GEMV launch");
+void launch_gemv(ijb_engine *e, const GemvParams &p, cudaStream_t s, bool pdl, bool force_pdl = false) {
+    ck(gemv_launch(p, e->num_sms, s, (pdl && e->pdl) || force_pdl), "GEMV launch");
     ++g_launches;
 }
 
@@ -260,9 +261,11 @@ bool proj_uses_mma(const ijb_engine *e, int gn, const ProjSeg *segs, int nsegs, 
 
 // x16_ready: the activation tile of the (single, <= kMmaMaxN-token) tensor-core
 // chunk has already been built by the previous kernel.
+// gemv_pdl: the CUDA-core launch uses programmatic dependent launch even when
+// the engine's IJB_PDL is off.
 void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const float *x, long x_stride,
                        const float *norm_w, const ProjSeg *segs, int nsegs, char *kbase, long v_off,
-                       bool x16_ready = false) {
+                       bool x16_ready = false, bool gemv_pdl = false) {
     const ijb_model_desc &d = e->d;
     const int *tpos = e->meta_dev + 2 * d.max_batch;
     const int *tslot = e->meta_dev + 3 * d.max_batch;
@@ -358,7 +361,7 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             add_seg(p, e->w[segs[i].w0], segs[i].w1 >= 0 ? &e->w[segs[i].w1] : nullptr, segs[i].epi,
                     segs[i].out ? segs[i].out + static_cast<long>(g0 + q0) * segs[i].out_stride : nullptr,
                     segs[i].out_stride, 0, d);
-        launch_gemv(e, p, s, true);
+        launch_gemv(e, p, s, true, gemv_pdl);
     }
 }
 
@@ -386,7 +389,8 @@ void enqueue_qkv(ijb_engine *e, int l, int n, cudaStream_t s) {
 }
 void enqueue_o(ijb_engine *e, int l, int n, cudaStream_t s, bool x16_ready = false) {
     const ProjSeg o_segs[1] = {{e->layers[l].o, -1, kEpiAdd, e->x, e->d.dim}};
-    launch_projection(e, s, 0, n, e->attn, e->d.dim, nullptr, o_segs, 1, nullptr, 0, x16_ready);
+    launch_projection(e, s, 0, n, e->attn, e->d.dim, nullptr, o_segs, 1, nullptr, 0, x16_ready,
+                      n < e->mma_min_batch && e->small_attn_pdl);
 }
 void enqueue_gateup(ijb_engine *e, int l, int n, cudaStream_t s) {
     const auto &L = e->layers[l];
@@ -460,7 +464,8 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool t
             a.use_dp4a = o_dp;
         }
         // tensor-core steps chain their launches with programmatic dependent launch
-        ck(attention_launch(a, s, e->pdl || (n >= e->mma_min_batch && e->attn_pdl)), "attention launch");
+        ck(attention_launch(a, s, e->pdl || (n >= e->mma_min_batch ? e->attn_pdl : e->small_attn_pdl)),
+           "attention launch");
         g_launches += attention_kernels(a);
         if (traced) enqueue_trace_quant(e, n, e->attn, d.dim, nullptr, d.dim, l, d.dim, s);
         enqueue_o(e, l, n, s, o_fused && !traced);
@@ -663,6 +668,11 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->attn_pdl = env2 && env2[0] == '1';
             env2 = std::getenv("IJB_ATTN_PREP");
             e->attn_prep = env2 && env2[0] == '1';
+            // IJB_SMALL_ATTN_PDL=0: steps of 1-15 tokens launch their attention and O
+            // projection without PDL (with it, measured on B200: a 1B batch-1 step
+            // 0.830 -> 0.793 ms; PDL for every kernel of those steps is slower, 0.89 ms)
+            env2 = std::getenv("IJB_SMALL_ATTN_PDL");
+            e->small_attn_pdl = !(env2 && env2[0] == '0');
             // IJB_ATTN_STREAM_MIN: steps of fewer tokens use the CUDA-core split
             // kernel (measured on B200: a 1B batch-1 step 0.81 ms with the
             // streaming kernel, 0.88 ms with the split kernel)
