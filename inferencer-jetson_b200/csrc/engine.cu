@@ -148,7 +148,7 @@ struct ijb_engine {
     bool pdl = false;      // programmatic dependent launch between the step's kernels
     bool mma_pdl = true;   // the same for the tensor-core path's prep and GEMM launches
     bool attn_pdl = false;   // the same for the attention launches of tensor-core steps
-    bool small_attn_pdl = true;  // the same for the attention and O launches of CUDA-core steps
+    bool small_attn_pdl = true;  // the same for the QKV, attention and O launches of CUDA-core steps
     bool attn_prep = false;  // the attention finish kernel builds the O projection's activation tile
     float last_step_ms = 0.f;
     std::string err;
@@ -385,7 +385,7 @@ void enqueue_qkv(ijb_engine *e, int l, int n, cudaStream_t s) {
                              {L.k, -1, kEpiRopeKCache, nullptr, 0},
                              {L.v, -1, kEpiVCache, nullptr, 0}};
     launch_projection(e, s, 0, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), segs, 3,
-                      kbase, v_off);
+                      kbase, v_off, false, n < e->mma_min_batch && e->small_attn_pdl);
 }
 void enqueue_o(ijb_engine *e, int l, int n, cudaStream_t s, bool x16_ready = false) {
     const ProjSeg o_segs[1] = {{e->layers[l].o, -1, kEpiAdd, e->x, e->d.dim}};
@@ -668,9 +668,10 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->attn_pdl = env2 && env2[0] == '1';
             env2 = std::getenv("IJB_ATTN_PREP");
             e->attn_prep = env2 && env2[0] == '1';
-            // IJB_SMALL_ATTN_PDL=0: steps of 1-15 tokens launch their attention and O
-            // projection without PDL (with it, measured on B200: a 1B batch-1 step
-            // 0.830 -> 0.793 ms; PDL for every kernel of those steps is slower, 0.89 ms)
+            // IJB_SMALL_ATTN_PDL=0: steps of 1-15 tokens launch their QKV projection,
+            // attention and O projection without PDL (with it, measured on B200: a 1B
+            // batch-1 step 0.830 -> 0.786 ms; PDL on the gate/up or down launch as well
+            // makes it slower, 0.821 / 0.831 ms, and on every kernel 0.89 ms)
             env2 = std::getenv("IJB_SMALL_ATTN_PDL");
             e->small_attn_pdl = !(env2 && env2[0] == '0');
             // IJB_ATTN_STREAM_MIN: steps of fewer tokens use the CUDA-core split
