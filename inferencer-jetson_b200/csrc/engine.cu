@@ -3,12 +3,13 @@
 // graphs with programmatic dependent launch between kernels.
 //
 // It takes the place of FastGPU (inferencer.cu:1101-1180) and FastRunner
-// (:1182-1532).  Per layer a step of 1-15 tokens launches five kernels where
-// the reference launches 13-17 (QKV + RoPE + KV write, attention, O +
-// residual, gate/up + SiLU, down + residual), plus the streaming attention's
-// finish kernel for an fp16, head_dim-64 cache; steps of 16-64 tokens add an
-// activation-prep launch before each tensor-core projection.  The whole step
-// is one CUDA graph.
+// (:1182-1532).  Per layer a step on the CUDA-core GEMV (1-2 tokens, or any
+// step of an engine with max_batch < 16) launches five kernels where the
+// reference launches 13-17 (QKV + RoPE + KV write, attention, O + residual,
+// gate/up + SiLU, down + residual), plus the streaming attention's finish
+// kernel for an fp16, head_dim-64 cache; tensor-core steps (3 or more tokens)
+// add an activation-prep launch before each projection.  The whole step is one
+// CUDA graph.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -668,7 +669,7 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             e->attn_pdl = env2 && env2[0] == '1';
             env2 = std::getenv("IJB_ATTN_PREP");
             e->attn_prep = env2 && env2[0] == '1';
-            // IJB_SMALL_ATTN_PDL=0: steps of 1-15 tokens launch their QKV projection,
+            // IJB_SMALL_ATTN_PDL=0: CUDA-core steps launch their QKV projection,
             // attention and O projection without PDL (with it, measured on B200: a 1B
             // batch-1 step 0.830 -> 0.786 ms; PDL on the gate/up or down launch as well
             // makes it slower, 0.821 / 0.831 ms, and on every kernel 0.89 ms)
@@ -778,7 +779,7 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
 
         // chunked weight copies of the tensor-core path ([64-row group][block
         // column] chunks, so that each stage of a tile is a few plain bulk copies)
-        if (d.max_batch >= kMmaMinBatch) {
+        if (d.max_batch >= kMmaEngineMinBatch) {
             ck(mma_prepare(), "tensor-core GEMM attributes");
             for (size_t i = 0; i < e->w.size(); ++i) {
                 Weight &w = e->w[i];

@@ -11,7 +11,13 @@ namespace ijb {
 
 constexpr int kMmaTileM = 128;    // weight rows per tile (TMEM lanes)
 constexpr int kMmaMaxN = 64;      // tokens per launch (MMA N, padded to 16)
-constexpr int kMmaMinBatch = 16;  // below this the CUDA-core GEMV is used
+// Engines with max_batch >= kMmaEngineMinBatch hold the tensor-core weight copy
+// and run steps of kMmaMinBatch or more tokens on it (measured on B200, 1B decode
+// steps: 2 tokens 1.01 ms on CUDA cores / 1.20 ms on the tensor cores; 3 tokens
+// 1.37 / 1.23; 8 tokens 3.03 / 1.26; 12 tokens 4.38 / 1.27); smaller engines
+// run every step on the CUDA-core GEMV.
+constexpr int kMmaMinBatch = 3;
+constexpr int kMmaEngineMinBatch = 16;
 
 // Row groups of the tensor-core path's weight layout.
 constexpr int kMmaRowGroup = 64;
