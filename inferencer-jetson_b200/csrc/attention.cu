@@ -930,6 +930,7 @@ static bool stream_path(const AttnParams &p) {
 }
 
 int attention_split_len() { return kAttnSplit; }
+int attention_split_len_min() { return kAttnItem; }
 int attention_kernels(const AttnParams &p) { return stream_path(p) ? 2 : 1; }
 int attention_item_len() { return kAttnItem; }
 
@@ -974,7 +975,10 @@ cudaError_t attention_prepare() {
 }
 
 cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl) {
-    if (p.split_len != kAttnSplit || p.page_size < 8 || p.page_size > 32 || 32 % p.page_size)
+    // the split kernel's split length: kAttnItem..kAttnSplit positions, whole chunks and
+    // pages, so that split indexes stay below max_splits (counted in kAttnItem items)
+    if (p.split_len < kAttnItem || p.split_len > kAttnSplit || p.split_len % kAttnChunk || p.page_size < 8 ||
+        p.page_size > 32 || 32 % p.page_size || p.split_len % p.page_size)
         return cudaErrorInvalidValue;
     if (p.max_splits * kAttnItem < 1) return cudaErrorInvalidValue;
     if (stream_path(p)) {
@@ -999,7 +1003,7 @@ cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
     }
     // one CTA per split of kAttnSplit positions (the partial records are kept
     // at kAttnItem granularity, so max_splits counts items)
-    dim3 grid((p.max_splits * kAttnItem + kAttnSplit - 1) / kAttnSplit, p.kv_heads, p.batch);
+    dim3 grid((p.max_splits * kAttnItem + p.split_len - 1) / p.split_len, p.kv_heads, p.batch);
     return p.kv_f32 ? attention_launch_t<float>(p, grid, stream, pdl) : attention_launch_t<__half>(p, grid, stream, pdl);
 }
 

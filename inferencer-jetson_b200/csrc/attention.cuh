@@ -28,7 +28,7 @@ struct AttnParams {
     const int *tok_pos;    // [batch]: attends to positions 0..pos
     int batch, heads, kv_heads, head_dim;
     float scale;           // 1/sqrt(head_dim)
-    int split_len;         // positions per split (attention_split_len())
+    int split_len;         // positions per split of the split kernel (attention_split_len_min()..attention_split_len())
     int max_splits;        // partial records per (token, head); >= ceil(context / attention_item_len())
     float *partial;        // [batch][heads][max_splits][head_dim + 2] scratch
     int *counters;         // [batch][kv_heads], zero between launches
@@ -50,7 +50,8 @@ int attention_kernels(const AttnParams &p);  // kernels attention_launch launche
 // 0 on success, -1 where the tensor-core kernel does not apply (head_dim != 64).
 int attention_make_kv_map(CUtensorMap *map, const void *layer_base, int head_dim, int kv_heads, int page_size,
                           long page_stride_elems, long num_pages);
-int attention_split_len();  // positions per split the kernel is built for
+int attention_split_len();      // longest split of the split kernel (positions)
+int attention_split_len_min();  // shortest split of the split kernel (positions)
 int attention_item_len();   // positions per work item of the streaming kernel (finest split)
 cudaError_t attention_prepare();  // once per device, before any launch
 

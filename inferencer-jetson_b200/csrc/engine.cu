@@ -441,7 +441,9 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool t
         a.kv_heads = d.kv_heads;
         a.head_dim = e->head_dim;
         a.scale = 1.0f / std::sqrt(static_cast<float>(e->head_dim));
-        a.split_len = e->attn_split_len;
+        // steps below attn_stream_min (batch 1) take the split kernel with short
+        // splits: more CTAs for one sequence's few positions
+        a.split_len = n < e->attn_stream_min ? attention_split_len_min() : e->attn_split_len;
         a.max_splits = e->attn_max_splits;
         a.partial = e->attn_partial;
         a.counters = e->attn_counters;
@@ -676,8 +678,10 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             env2 = std::getenv("IJB_SMALL_ATTN_PDL");
             e->small_attn_pdl = !(env2 && env2[0] == '0');
             // IJB_ATTN_STREAM_MIN: steps of fewer tokens use the CUDA-core split
-            // kernel (measured on B200: a 1B batch-1 step 0.81 ms with the
-            // streaming kernel, 0.88 ms with the split kernel)
+            // kernel with 128-position splits.  Off by default: a 1B batch-1 step
+            // measured 0.767 ms that way against 0.781 ms with the streaming
+            // kernel, but a sequence's tokens would then depend on whether it is
+            // decoded alone or in a batch (the two kernels round differently)
             env2 = std::getenv("IJB_ATTN_STREAM_MIN");
             if (env2) e->attn_stream_min = std::max(1, std::atoi(env2));
         }
