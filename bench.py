@@ -1006,7 +1006,10 @@ def run_ours(args):
             except Exception as ex:  # reported, not fatal
                 result["reference_cuda"]["decode_3b_b1"] = {"error": repr(ex)}
         if ragged:
-            result["prefill"] = {"tokens": server.prefill_tokens, "seconds": server.prefill_s}
+            result["prefill"] = {"tokens": server.prefill_tokens, "seconds": server.prefill_s,
+                                 "tokens_per_s": server.prefill_tokens / max(server.prefill_s, 1e-9),
+                                 "method": "wall time of the population's prefills (ijb_seq_prefill, chunks of "
+                                           "max_batch tokens through the decode kernels), outside the timed steps"}
     if eng is not None:
         eng.close()
     if world > 1:
