@@ -524,6 +524,28 @@ def layer_roofline(cuda, peak, local, iters=20, batch=64):
             "per_matrix_alone": per}
 
 
+def attention_roofline(eng, server, peak, head_dim, iters=20):
+    """Decode attention as a step issues it: layer 0's launch (the streaming
+    kernel ijb_attention_stream_kernel and its merge) for one token of every
+    live sequence at its newest position, replayed `iters` times in one CUDA
+    graph by ijb_time_layer_attention (CUDA events on the engine's stream).
+    Algorithmic bytes per launch: every cached K and V row of those sequences
+    (fp16), read once."""
+    ids = [int(s[0]) for s in server.live]
+    ms, kv_bytes = eng.time_layer_attention(ids, iters)
+    gbs = kv_bytes / (ms * 1e-3) / 1e9
+    prof = f"attention_stream_hd{head_dim}_traffic.md"
+    ratio = profile_figure(prof, "traffic_per_algorithmic_byte")
+    return {"kernel": f"ijb_attention_stream_kernel<{head_dim}, G> + ijb_attention_finish_kernel: one layer's decode "
+                      f"attention for {len(ids)} sequences at their current contexts",
+            "us_per_layer": ms * 1e3, "algorithmic_bytes": kv_bytes, "gbs": gbs, "frac": gbs / peak,
+            "traffic": kv_bytes * ratio if ratio else None,
+            "traffic_source": (f"profiles/{prof}: ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                               f"of a smaller population divided by its K/V bytes ({ratio:.4f}), times this "
+                               f"launch's K/V bytes")
+            if ratio else None}
+
+
 def mma_vocab_roofline(eng, cuda, peak, iters=20, batch=64):
     """The vocab projection (Q6_K 128256x2048, the largest single launch of a
     step) through ijb_matvec for `batch` tokens: activation prep +
@@ -927,12 +949,10 @@ def run_ours(args):
         extras = args.workload == "ragged64" and not args.no_extras
         kern = gemv_roofline(cuda, peak, GEMV_CASES + ((GEMV_B8_CASE,) if extras else ())) if (extras or not ragged) \
             else None
+        att = attention_roofline(eng, server, peak, cfg.head_dim) if ragged else None
         if big:
-            # KV bytes are ~97% of this step: the roofline is the step's own
-            dom = {"gbs": step_gbs, "frac": step_gbs / peak, "traffic": None,
-                   "kernel": "whole decode step (attention over the paged KV cache is ~97% of its bytes)",
-                   "us_per_layer": ms_per_step * 1e3 / cfg.layers, "weight_bytes": w_bytes,
-                   "algorithmic_bytes": step_bytes, "traffic_source": None, "per_matrix_alone": None}
+            # K/V reads are ~97% of this step's bytes: the dominant kernel is the attention
+            dom = dict(att, weight_bytes=None, per_matrix_alone=None)
             vocab = None
         elif ragged:
             dom = layer_roofline(cuda, peak, local)
@@ -993,6 +1013,9 @@ def run_ours(args):
         }
         if vocab:
             result["vocab_projection"] = vocab
+        if att and not big:
+            result["attention"] = {k: att[k] for k in ("kernel", "us_per_layer", "algorithmic_bytes", "gbs", "frac",
+                                                        "traffic", "traffic_source")}
         if kern:
             result["gemv"] = kern
         if d1:

@@ -245,6 +245,19 @@ int ijb_probe_wait_timeout(ijb_engine *engine, uint64_t limit_ns);
  * (a measurement aid for the dominant kernel). */
 int ijb_time_layer_projections(ijb_engine *engine, int n, int reps, float *ms_per_layer);
 
+/* Timing helper: layer 0's decode attention for one query token of each of
+ * the n listed open sequences at its newest position (so each launch reads
+ * every cached K/V row of those sequences, as the next decode step would),
+ * launched as a packed step of n tokens launches it (streaming kernel and
+ * merge, or the split kernel), `reps` times in one CUDA graph.  Writes the
+ * mean device time of one layer's attention in milliseconds (CUDA events on
+ * the engine's stream) and the K/V bytes one launch reads.  The engine's
+ * attention output is overwritten; the cache is only read.  No counterpart
+ * in the reference (a measurement aid; the reference's decode attention is
+ * attention_cuda, inferencer.cu:981-1009). */
+int ijb_time_layer_attention(ijb_engine *engine, int n, const int *seq_ids, int reps, float *ms_per_layer,
+                             long long *kv_bytes);
+
 /* ---- one quantised matrix on the tensor cores, outside an engine ----
  * For callers that hold one matrix or a slice of one, e.g. each rank's
  * row slice of a row-split lm_head (the reference's lm_head GEMV,

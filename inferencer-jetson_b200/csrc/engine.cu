@@ -404,56 +404,64 @@ void enqueue_down(ijb_engine *e, int l, int n, cudaStream_t s) {
     launch_projection(e, s, 0, n, e->h, e->d.hidden, nullptr, segs, 1, nullptr, 0);
 }
 
+// Layer l's attention over the n tokens of the step metadata (meta_dev): the
+// split kernel, or the streaming kernel where the cache has TMA maps.
+AttnParams attn_params(ijb_engine *e, int l, int n) {
+    const ijb_model_desc &d = e->d;
+    const long layer_pool = e->num_pages * e->page_stride;
+    const long v_off = static_cast<long>(d.kv_heads) * d.page_size * e->head_dim;
+    char *kbase = static_cast<char *>(e->kv) + l * layer_pool * e->kv_elem;
+    const int *tseq = e->meta_dev + d.max_batch;
+    const int *tpos = e->meta_dev + 2 * d.max_batch;
+    AttnParams a;
+    std::memset(&a, 0, sizeof(a));
+    a.q = e->q;
+    a.q_stride = d.dim;
+    a.out = e->attn;
+    a.out_stride = d.dim;
+    a.k_cache = kbase;
+    a.v_cache = kbase + v_off * e->kv_elem;
+    a.kv_f32 = e->kv_f32;
+    a.page_stride = e->page_stride;
+    a.page_size = d.page_size;
+    a.page_table = e->page_table_dev;
+    a.max_pages_per_seq = e->max_pages_per_seq;
+    a.tok_seq = tseq;
+    a.tok_pos = tpos;
+    a.batch = n;
+    a.heads = d.heads;
+    a.kv_heads = d.kv_heads;
+    a.head_dim = e->head_dim;
+    a.scale = 1.0f / std::sqrt(static_cast<float>(e->head_dim));
+    // steps below attn_stream_min (batch 1) take the split kernel with short
+    // splits: more CTAs for one sequence's few positions
+    a.split_len = n < e->attn_stream_min ? attention_split_len_min() : e->attn_split_len;
+    a.max_splits = e->attn_max_splits;
+    a.partial = e->attn_partial;
+    a.counters = e->attn_counters;
+    a.work = e->attn_counters + d.max_batch * d.kv_heads;
+    a.num_ctas = e->num_sms;
+    a.status = e->status;
+    if (!e->kv_maps.empty() && n >= e->attn_stream_min) {
+        a.kv_map = e->kv_maps[l];
+        a.has_map = 1;
+    }
+    return a;
+}
+
 void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool traced = false) {
     const ijb_model_desc &d = e->d;
     const int *tok = e->meta_dev;
-    const int *tseq = e->meta_dev + d.max_batch;
-    const int *tpos = e->meta_dev + 2 * d.max_batch;
     const Weight &emb = e->w[e->token_embd];
     ck(embed_launch(emb.data, emb.row_bytes, d.dim, tok, n, e->x, d.dim, e->keys, s, e->pdl), "embedding launch");
     ++g_launches;
-    const long layer_pool = e->num_pages * e->page_stride;
-    const long v_off = static_cast<long>(d.kv_heads) * d.page_size * e->head_dim;
     for (int l = 0; l < d.layers; ++l) {
         const auto &L = e->layers[l];
-        char *kbase = static_cast<char *>(e->kv) + l * layer_pool * e->kv_elem;
         if (traced)
             enqueue_trace_quant(e, n, e->x, d.dim, reinterpret_cast<const float *>(e->w[L.attn_norm].data), d.dim, l, 0,
                                 s);
         enqueue_qkv(e, l, n, s);
-        AttnParams a;
-        std::memset(&a, 0, sizeof(a));
-        a.q = e->q;
-        a.q_stride = d.dim;
-        a.out = e->attn;
-        a.out_stride = d.dim;
-        a.k_cache = kbase;
-        a.v_cache = kbase + v_off * e->kv_elem;
-        a.kv_f32 = e->kv_f32;
-        a.page_stride = e->page_stride;
-        a.page_size = d.page_size;
-        a.page_table = e->page_table_dev;
-        a.max_pages_per_seq = e->max_pages_per_seq;
-        a.tok_seq = tseq;
-        a.tok_pos = tpos;
-        a.batch = n;
-        a.heads = d.heads;
-        a.kv_heads = d.kv_heads;
-        a.head_dim = e->head_dim;
-        a.scale = 1.0f / std::sqrt(static_cast<float>(e->head_dim));
-        // steps below attn_stream_min (batch 1) take the split kernel with short
-        // splits: more CTAs for one sequence's few positions
-        a.split_len = n < e->attn_stream_min ? attention_split_len_min() : e->attn_split_len;
-        a.max_splits = e->attn_max_splits;
-        a.partial = e->attn_partial;
-        a.counters = e->attn_counters;
-        a.work = e->attn_counters + d.max_batch * d.kv_heads;
-        a.num_ctas = e->num_sms;
-        a.status = e->status;
-        if (!e->kv_maps.empty() && n >= e->attn_stream_min) {
-            a.kv_map = e->kv_maps[l];
-            a.has_map = 1;
-        }
+        AttnParams a = attn_params(e, l, n);
         // the streaming attention's finish kernel also builds the O projection's
         // activation tile when that projection is one tensor-core chunk
         const ProjSeg o_segs[1] = {{L.o, -1, kEpiAdd, e->x, d.dim}};
@@ -1086,6 +1094,64 @@ int ijb_time_layer_projections(ijb_engine *e, int n, int reps, float *ms_per_lay
         for (int p : e->seq_pages[0]) e->free_pages.push_back(p);
         e->seq_pages[0].clear();
         *ms_per_layer = ms / reps;
+        return IJB_OK;
+    } catch (const std::exception &ex) {
+        return fail(e, ex);
+    }
+}
+
+int ijb_time_layer_attention(ijb_engine *e, int n, const int *seq_ids, int reps, float *ms_per_layer,
+                              long long *kv_bytes) {
+    try {
+        require(e != nullptr && seq_ids != nullptr && ms_per_layer != nullptr && kv_bytes != nullptr, "bad arguments");
+        const ijb_model_desc &d = e->d;
+        require(n >= 1 && n <= d.max_batch, "n must be 1..max_batch");
+        require(reps >= 1 && reps <= 1000, "reps must be 1..1000");
+        ck(cudaSetDevice(d.device), "cudaSetDevice");
+        // one query token per sequence at its newest position: the launch reads
+        // the sequence's whole cached context, as the next decode step would
+        int *mt = e->meta_host;
+        long long positions = 0;
+        for (int i = 0; i < n; ++i) {
+            const int sq = seq_ids[i];
+            require(sq >= 0 && sq < d.max_seqs && e->seq_used[sq], "unknown sequence id");
+            const int len = e->seq_len[sq];
+            require(len >= 1, "sequence holds no positions");
+            mt[i] = 0;
+            mt[d.max_batch + i] = sq;
+            mt[2 * d.max_batch + i] = len - 1;
+            mt[3 * d.max_batch + i] = slot_for(e, sq, len - 1);  // an existing slot: no page is taken
+            positions += len;
+        }
+        ck(cudaMemcpyAsync(e->meta_dev, e->meta_host, 4 * d.max_batch * sizeof(int), cudaMemcpyHostToDevice, e->stream),
+           "meta H2D");
+        const AttnParams a = attn_params(e, 0, n);
+        const bool pdl = e->pdl || (n >= e->mma_min_batch ? e->attn_pdl : e->small_attn_pdl);
+        cudaGraph_t graph;
+        cudaGraphExec_t exec = nullptr;
+        ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        cudaError_t ce = cudaSuccess;
+        for (int r = 0; r < reps && ce == cudaSuccess; ++r) ce = attention_launch(a, e->stream, pdl);
+        const cudaError_t ee = cudaStreamEndCapture(e->stream, &graph);
+        if (ee == cudaSuccess && ce != cudaSuccess) cudaGraphDestroy(graph);
+        ck(ce, "attention launch");
+        ck(ee, "end capture");
+        cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        ck(ie, "graph instantiate");
+        float ms = 0.f;
+        cudaError_t le = cudaGraphLaunch(exec, e->stream);  // warm-up
+        if (le == cudaSuccess) le = cudaEventRecord(e->ev_start, e->stream);
+        if (le == cudaSuccess) le = cudaGraphLaunch(exec, e->stream);
+        if (le == cudaSuccess) le = cudaEventRecord(e->ev_end, e->stream);
+        if (le == cudaSuccess) le = cudaStreamSynchronize(e->stream);
+        if (le == cudaSuccess) le = cudaEventElapsedTime(&ms, e->ev_start, e->ev_end);
+        cudaGraphExecDestroy(exec);
+        ck(le, "attention timing");
+        g_launches += 2ull * reps * attention_kernels(a);
+        check_device_status(e);
+        *ms_per_layer = ms / reps;
+        *kv_bytes = positions * d.kv_heads * 2LL * e->head_dim * e->kv_elem;
         return IJB_OK;
     } catch (const std::exception &ex) {
         return fail(e, ex);

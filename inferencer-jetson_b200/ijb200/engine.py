@@ -170,6 +170,17 @@ class Engine:
                                        out, ctypes.byref(n)), self.h)
         return [int(v) for v in out[:n.value]]
 
+    def time_layer_attention(self, seq_ids, reps: int = 20):
+        """ijb_time_layer_attention: (ms per layer, K/V bytes per launch) of layer 0's
+        attention for one token of each listed sequence at its newest position."""
+        n = len(seq_ids)
+        s = (ctypes.c_int * n)(*[int(v) for v in seq_ids])
+        ms = ctypes.c_float()
+        kvb = ctypes.c_longlong()
+        _L.check(self.lib.ijb_time_layer_attention(self.h, n, s, int(reps), ctypes.byref(ms), ctypes.byref(kvb)),
+                 self.h)
+        return float(ms.value), int(kvb.value)
+
     def probe_wait_timeout(self, limit_ns: int) -> int:
         """ijb_probe_wait_timeout: the status code of a step whose bounded wait expired."""
         return int(self.lib.ijb_probe_wait_timeout(self.h, int(limit_ns)))

@@ -83,6 +83,7 @@ def load():
         "ijb_prefill_traced": ([P, IP, I, IP, P, P, P], I),
         "ijb_last_step_size": ([P], I),
         "ijb_time_layer_projections": ([P, I, I, ctypes.POINTER(ctypes.c_float)], I),
+        "ijb_time_layer_attention": ([P, I, IP, I, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_longlong)], I),
         "ijb_weight_create": ([I, P, I, I, I, ctypes.POINTER(P)], I),
         "ijb_weight_destroy": ([P], None),
         "ijb_weight_matmul": ([P, P, I, P, ctypes.c_float, I, P, L64, I, P, P], I),

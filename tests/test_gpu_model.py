@@ -240,3 +240,34 @@ def test_errors_are_reported_not_raised_on_device(cuda):
     eng.seq_close(s)
     assert eng.forward(3, 0) >= 0
     eng.close()
+
+
+@pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_HD128_G3], ids=lambda c: c.name)
+def test_attention_timing_reads_the_cache_only(cuda, cfg):
+    """ijb_time_layer_attention times layer 0's attention over the listed
+    sequences' whole contexts and reports their K/V bytes; the sequences then
+    decode exactly as on an engine that was never timed."""
+    weights = synth.make_model(cfg, seed=21)
+    lens = (40, 300, 129)
+    engines = [Engine(cfg, weights, context=512, max_batch=16, max_seqs=5) for _ in range(2)]
+    ids, firsts = [], []
+    for eng in engines:
+        ids.append([eng.seq_open() for _ in lens])
+        firsts.append([eng.seq_prefill(s, synth.prompt_tokens(n, seed=30 + n, vocab_limit=cfg.vocab))
+                       for s, n in zip(ids[-1], lens)])
+    assert firsts[0] == firsts[1]
+    ms, kv_bytes = engines[0].time_layer_attention(ids[0], 5)
+    assert ms > 0
+    assert kv_bytes == sum(lens) * cfg.kv_heads * 2 * cfg.head_dim * 2  # K and V rows, fp16
+    closed = next(i for i in range(1, 5) if i not in ids[0])
+    with pytest.raises(lib.IjbError):
+        engines[0].time_layer_attention([closed], 1)  # a sequence that is not open
+    toks = [list(f) for f in firsts]
+    for _ in range(3):
+        outs = [eng.decode_step(i, t) for eng, i, t in zip(engines, ids, toks)]
+        np.testing.assert_array_equal(outs[0], outs[1])
+        np.testing.assert_array_equal(engines[0].logits(len(lens)).view(np.uint32),
+                                      engines[1].logits(len(lens)).view(np.uint32))
+        toks = [list(o) for o in outs]
+    for eng in engines:
+        eng.close()
