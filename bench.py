@@ -784,7 +784,8 @@ def decode1_record(cuda, local, cfg, weights, peak, steps, warmup, prompt_len=51
     ms = dev_ms / steps
     return {"metric": "decode tokens/s (1B Q4_K_M, batch 1)", "value": steps / (dev_ms / 1e3), "unit": "tokens/s",
             "ms_per_step": ms, "steps": steps, "warmup": warmup, "dtype": DTYPE_DP4A,
-            "e2e": {"value": steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
+            "e2e": {"value": steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 16,
+                    "d2h_bytes_per_step": 8},  # the next token and the device status word
             "generate": {"value": (len(toks) - 1) / gen_wall, "unit": "tokens/s",
                          "device_ms_per_step": gen_ms,
                          "method": f"one ijb_generate call for {steps} decode steps after the {prompt_len}-token "
@@ -997,7 +998,8 @@ def run_ours(args):
                        "l2": f"inputs larger than L2 ({w_bytes / 1e6:.0f} MB weights/step)",
                        "mean_context": kv_tokens / args.steps / batch,
                        "replaced_in_window": (server.replaced - replaced0) if ragged else 0},
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * batch},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4 * batch + 4},  # next tokens + the device status word
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": dom["frac"], "traffic": dom["traffic"], "kernel": dom["kernel"],

@@ -502,13 +502,11 @@ void enqueue_step(ijb_engine *e, int n, bool need_logits, cudaStream_t s, bool t
     ++g_launches;
 }
 
-// Reads the engine's device status word after the stream has synchronised:
-// a kernel that gave up a bounded wait, or failed a bounds check, left a
-// non-zero code there.  The word is cleared and the call fails with
-// IJB_ERR_DEVICE; the engine stays usable (nothing faulted).
-void check_device_status(ijb_engine *e) {
-    uint32_t st = 0;
-    ck(cudaMemcpy(&st, e->status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
+// The engine's device status word, read after the stream has synchronised: a
+// kernel that gave up a bounded wait, or failed a bounds check, left a non-zero
+// code there.  The word is cleared and the call fails with IJB_ERR_DEVICE; the
+// engine stays usable (nothing faulted).
+void check_status_word(ijb_engine *e, uint32_t st) {
     if (st) {
         ck(cudaMemset(e->status, 0, sizeof(uint32_t)), "status clear");
         std::string what;
@@ -516,6 +514,13 @@ void check_device_status(ijb_engine *e) {
         if (st & kDevErrBadIndex) what += " (an index failed its bounds check)";
         throw Error(IJB_ERR_DEVICE, "kernel reported device error code " + std::to_string(st) + what);
     }
+}
+
+// The same, reading the word from the device.
+void check_device_status(ijb_engine *e) {
+    uint32_t st = 0;
+    ck(cudaMemcpy(&st, e->status, sizeof(st), cudaMemcpyDeviceToHost), "status read");
+    check_status_word(e, st);
 }
 
 // Captures (once per n / need_logits) and replays the whole step: H2D of the
@@ -532,9 +537,14 @@ void run_step(ijb_engine *e, int n, bool need_logits, bool traced = false) {
                                e->stream),
                "meta H2D");
             enqueue_step(e, n, need_logits, e->stream, traced);
+            // the next tokens with the status word behind them, or the status word alone
+            const int B = e->d.max_batch;
             if (need_logits)
-                ck(cudaMemcpyAsync(e->next_host, e->next_dev, n * sizeof(int), cudaMemcpyDeviceToHost, e->stream),
+                ck(cudaMemcpyAsync(e->next_host, e->next_dev, (B + 1) * sizeof(int), cudaMemcpyDeviceToHost, e->stream),
                    "next D2H");
+            else
+                ck(cudaMemcpyAsync(e->next_host + B, e->next_dev + B, sizeof(int), cudaMemcpyDeviceToHost, e->stream),
+                   "status D2H");
         } catch (...) {
             cudaStreamEndCapture(e->stream, &graph);
             throw;
@@ -556,7 +566,7 @@ void run_step(ijb_engine *e, int n, bool need_logits, bool traced = false) {
     ck(cudaEventRecord(e->ev_end, e->stream), "step timer end");
     ck(cudaStreamSynchronize(e->stream), "step synchronize");
     ck(cudaEventElapsedTime(&e->last_step_ms, e->ev_start, e->ev_end), "step timer");
-    check_device_status(e);
+    check_status_word(e, static_cast<uint32_t>(e->next_host[e->d.max_batch]));
     e->last_n = n;
 }
 
@@ -876,11 +886,12 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         e->h = dev_alloc<float>(B * d.hidden, "ffn hidden");
         e->logits = dev_alloc<float>(B * d.vocab, "logits");
         e->keys = dev_alloc<unsigned long long>(B, "argmax keys");
-        e->next_dev = dev_alloc<int>(B, "next tokens");
+        // the next tokens, then the device status word: one copy brings both back
+        e->next_dev = dev_alloc<int>(B + 1, "next tokens");
         e->meta_dev = dev_alloc<int>(4 * B, "step meta");
         ck(cudaMemset(e->meta_dev, 0, 4 * B * sizeof(int)), "meta clear");
         ck(cudaMallocHost(&e->meta_host, 4 * B * sizeof(int)), "meta staging");
-        ck(cudaMallocHost(&e->next_host, B * sizeof(int)), "next staging");
+        ck(cudaMallocHost(&e->next_host, (B + 1) * sizeof(int)), "next staging");
         std::memset(e->meta_host, 0, 4 * B * sizeof(int));
         // attention: partial softmax records per (token, head) at work-item granularity
         e->attn_split_len = attention_split_len();
@@ -888,7 +899,7 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
         e->attn_partial = dev_alloc<float>(B * d.heads * e->attn_max_splits * (e->head_dim + 2), "attention partials");
         e->attn_counters = dev_alloc<int>(B * d.kv_heads + 2, "attention counters");
         ck(cudaMemset(e->attn_counters, 0, (B * d.kv_heads + 2) * sizeof(int)), "counters clear");
-        e->status = dev_alloc<uint32_t>(1, "status");
+        e->status = reinterpret_cast<uint32_t *>(e->next_dev + B);
         ck(cudaMemset(e->status, 0, sizeof(uint32_t)), "status clear");
         e->scratch_key = dev_alloc<unsigned long long>(1, "argmax scratch");
         ck(cudaStreamSynchronize(e->stream), "create synchronize");
@@ -934,7 +945,6 @@ void ijb_destroy(ijb_engine *e) {
     cudaFree(e->x_inv);
     cudaFree(e->attn_partial);
     cudaFree(e->attn_counters);
-    cudaFree(e->status);
     cudaFree(e->scratch_key);
     cudaFree(e->trace_x);
     cudaFree(e->trace_q);

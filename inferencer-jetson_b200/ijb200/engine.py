@@ -153,12 +153,16 @@ class Engine:
         return nxt.value
 
     def decode_step(self, seq_ids, tokens) -> np.ndarray:
-        n = len(seq_ids)
-        s = (ctypes.c_int * n)(*[int(v) for v in seq_ids])
-        t = (ctypes.c_int * n)(*[int(v) for v in tokens])
-        out = (ctypes.c_int * n)()
-        _L.check(self.lib.ijb_decode_step(self.h, n, s, t, out), self.h)
-        return np.frombuffer(out, dtype=np.int32).copy()
+        s = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        n = len(s)
+        if len(t) != n:
+            raise ValueError("seq_ids and tokens differ in length")
+        out = np.empty(n, dtype=np.int32)
+        ip = ctypes.POINTER(ctypes.c_int)
+        _L.check(self.lib.ijb_decode_step(self.h, n, s.ctypes.data_as(ip), t.ctypes.data_as(ip),
+                                          out.ctypes.data_as(ip)), self.h)
+        return out
 
     def generate(self, seq_id: int, first_token: int, max_tokens: int, stop_ids=()) -> list:
         """ijb_generate: greedy tokens from first_token on, fed back on the device
