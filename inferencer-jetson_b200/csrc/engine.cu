@@ -126,6 +126,7 @@ struct ijb_engine {
     cudaStream_t side[kMaxSide] = {};
     cudaEvent_t ev_fork = nullptr, ev_join[kMaxSide] = {};
     int mma_max_split = 8, mma_split_cost = 1;
+    bool mma_wide = true;
     int mma_bulk_out = 0;  // thread stores measured faster than per-row bulk copies
     int mma_min_batch = kMmaMinBatch;
     int attn_split_len = 64, attn_max_splits = 1;
@@ -180,8 +181,9 @@ cudaStream_t pick(ijb_engine *e, void *s) { return s ? static_cast<cudaStream_t>
 constexpr int kGenMaxStop = 16;  // stop ids of ijb_generate
 constexpr int kGenRound = 8;     // ijb_generate steps queued per host check
 
-// Bytes of one 64-token fp16 activation tile (the widest row, kMaxCols).
-constexpr size_t kX16ChunkBytes = static_cast<size_t>(kMaxCols / 128) * kMmaMaxN * 256;
+// Bytes of one chunk's fp16 activation tile (up to kMmaMaxNWide tokens of the
+// widest row, kMaxCols).
+constexpr size_t kX16ChunkBytes = static_cast<size_t>(kMaxCols / 128) * kMmaMaxNWide * 256;
 
 // ------------------------------------------------------------ GEMV params --
 
@@ -275,22 +277,32 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
     require(!x16_ready || (mma_ok && gn <= kMmaMaxN), "prepared activation without a single tensor-core chunk");
     const int cols = e->w[segs[0].w0].cols;
     if (mma_ok) {
+        // the projection's tiles and K split (the same for every chunk); a launch
+        // whose CTAs each hold one tile takes up to kMmaMaxNWide tokens
+        int tiles = 0;
+        for (int i = 0; i < nsegs; ++i) {
+            const int rows = e->w[segs[i].w0].rows;
+            tiles += segs[i].w1 >= 0 ? (rows + 63) / 64 : (rows + kMmaTileM - 1) / kMmaTileM;
+        }
+        int bps = 0;
+        const int ksplit = mma_choose_split(tiles, cols / 256, e->mma_max_split, e->mma_split_cost, &bps);
+        const int chunk = e->mma_wide && gn > kMmaMaxN && mma_wide_ok(tiles, ksplit) ? kMmaMaxNWide : kMmaMaxN;
         // the chunks are independent (their own tokens, activation tile and outputs)
         // and read the same weights, so they run side by side and the later reads
         // of each weight tile hit L2
-        const int nchunks = (gn + kMmaMaxN - 1) / kMmaMaxN;
+        const int nchunks = (gn + chunk - 1) / chunk;
         const int nbranch = std::min(nchunks - 1, e->nside);
         if (nbranch > 0) {
             ck(cudaEventRecord(e->ev_fork, s), "chunk fork");
             for (int i = 0; i < nbranch; ++i) ck(cudaStreamWaitEvent(e->side[i], e->ev_fork, 0), "chunk fork");
         }
-        for (int t0 = 0; t0 < gn; t0 += kMmaMaxN) {
-            const int tn = std::min(kMmaMaxN, gn - t0);
+        for (int t0 = 0; t0 < gn; t0 += chunk) {
+            const int tn = std::min(chunk, gn - t0);
             const int n_pad = (tn + 15) / 16 * 16;
-            const int c = t0 / kMmaMaxN;
+            const int c = t0 / chunk;
             cudaStream_t cs = c == 0 || nbranch == 0 ? s : e->side[(c - 1) % nbranch];
             uint8_t *x16 = e->x16 + static_cast<size_t>(c) * kX16ChunkBytes;
-            float *x_inv = e->x_inv + c * kMmaMaxN;
+            float *x_inv = e->x_inv + c * kMmaMaxNWide;
             if (!x16_ready) {
                 ck(mma_prep_launch(x + static_cast<long>(t0) * x_stride, x_stride, norm_w, d.eps, cols, tn, n_pad, dp,
                                    x16, x_inv, cs, e->mma_pdl),
@@ -339,7 +351,9 @@ void launch_projection(ijb_engine *e, cudaStream_t s, int g0, int gn, const floa
             m.page_stride = e->page_stride;
             m.argmax_keys = e->keys + g0 + t0;
             m.status = e->status;
-            m.ksplit = mma_choose_split(m.total_tiles, cols / 256, e->mma_max_split, e->mma_split_cost, &m.bps);
+            require(m.total_tiles == tiles, "projection tile count");
+            m.ksplit = ksplit;
+            m.bps = bps;
             m.bulk_out = e->mma_bulk_out;
             ck(mma_gemm_launch(m, cs, e->mma_pdl), "tensor-core GEMM launch");
             ++g_launches;
@@ -819,7 +833,7 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             const int nchunks = (d.max_batch + kMmaMaxN - 1) / kMmaMaxN;
             e->x16 = dev_alloc<uint8_t>(static_cast<size_t>(nchunks) * kX16ChunkBytes, "fp16 activation");
             ck(cudaMemset(e->x16, 0, static_cast<size_t>(nchunks) * kX16ChunkBytes), "fp16 activation clear");
-            e->x_inv = dev_alloc<float>(static_cast<size_t>(nchunks) * kMmaMaxN, "activation scales");
+            e->x_inv = dev_alloc<float>(static_cast<size_t>(nchunks) * kMmaMaxNWide, "activation scales");
             e->nside = std::min(nchunks - 1, ijb_engine::kMaxSide);
             if (e->nside > 0) ck(cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming), "event");
             for (int i = 0; i < e->nside; ++i) {
@@ -832,6 +846,8 @@ int ijb_create(const ijb_model_desc *desc, const ijb_tensor_view *tensors, int n
             if ((env = std::getenv("IJB_MMA_MAX_SPLIT"))) e->mma_max_split = std::max(1, std::atoi(env));
             if ((env = std::getenv("IJB_MMA_SPLIT_COST"))) e->mma_split_cost = std::max(0, std::atoi(env));
             if ((env = std::getenv("IJB_MMA_BULK_OUT"))) e->mma_bulk_out = std::atoi(env) != 0;
+            // 128-token chunks where every CTA of the launch holds one tile
+            if ((env = std::getenv("IJB_MMA_WIDE"))) e->mma_wide = std::atoi(env) != 0;
         }
 
         // RoPE tables, computed on the host the way FastRunner's constructor

@@ -1,4 +1,5 @@
-// Tensor-core (tcgen05) quantised GEMM for packed steps of 16..64 tokens.
+// Tensor-core (tcgen05) quantised GEMM for packed steps: up to 64 tokens per
+// launch, or up to 128 when every CTA of the launch holds one tile.
 //
 // Replaces, for a ragged batch, what the reference does one token at a time
 // (gemv_batch_dp4a, qkv_batch_cuda, gate_up_batch_cuda, inferencer.cu:678-751):
@@ -12,7 +13,8 @@
 //     copies the raw quantised bytes of the tile's two 64-row groups, each a
 //     contiguous chunk of the weight's chunked copy (Q4_K: [64 rows][144 B];
 //     Q6_K: [64][208 B] block bodies and [64] fp16 d), with plain bulk copies
-//     into a 4-stage ring.
+//     into a 4-stage ring (3 stages in 128-token launches, whose activation
+//     stages are twice as large).
 //   * warp 6, lane 0: activation producer: per 64-wide K stage, one bulk copy
 //     of the prepared fp16 activation chunk into an 8-stage ring (two block
 //     columns in flight).
@@ -24,14 +26,15 @@
 //     scale and offset; the K order inside each 8-wide core is permuted so that
 //     this needs no byte shuffles, and the activation tile is written in the
 //     same order.
-//   * MMA issue: tcgen05.mma (kind::f16, M=128, N = tokens rounded up to 16,
-//     K=16) into two fp32 accumulator chains in TMEM (even and odd 64-wide
-//     groups); tcgen05.commit releases stages and signals finished
-//     accumulators.  A thread issues about one MMA per 100 cycles whatever N,
-//     so a CTA with a single tile has warps 2 and 3 issue one chain each
-//     before their epilogue work; a CTA with several tiles issues from warp 1
-//     with the accumulators double-buffered across tiles.
-//   * warps 2..5 (one per TMEM lane quadrant): read and add the two chains with
+//   * warps 1 and 23, lane 0: MMA issue, tcgen05.mma (kind::f16, M=128, N =
+//     tokens rounded up to 16, K=16) into two fp32 accumulator chains in TMEM
+//     (warp 1: even 64-wide groups, columns from 0; warp 23: odd groups, from
+//     384; up to 128 columns each beside the 256 columns of weight stages);
+//     tcgen05.commit releases stages and signals finished accumulators.  Every
+//     launch width sums a token's products in this order.  CTAs with several
+//     tiles double-buffer the chains across tiles.
+//   * warps 2..5 (one per TMEM lane quadrant), joined by the converter warps
+//     when the CTA has a single tile: read and add the two chains with
 //     tcgen05.ld, undo the two power-of-two scales and apply the fused
 //     epilogue of the GEMV (store, residual add, RoPE + paged K write, V write,
 //     SiLU * up, logits + argmax key) through a [token][row] shared-memory
@@ -59,38 +62,40 @@ constexpr int kQ6DOff = 128 * 208;                    // d box within a Q6_K raw
 constexpr uint32_t kTmemCols = 512;  // accumulator chain 0 [0, 128), fp16 weight stages [128, 384), chain 1 [384, 512)
 constexpr uint32_t kTmemA = 128;     // first column of the weight stages (32 per stage)
 constexpr uint32_t kTmemAcc1 = 384;  // chain 1 of the accumulators
-constexpr int kX16Bytes = kMmaMaxN * kKChunk * 2;     // 8 KB
+constexpr int kRawStagesWide = kRawStages - 1;       // raw stages of a launch wider than kMmaMaxN tokens
 constexpr int kCoreStride = 128;                      // bytes between 8-wide K cores
 constexpr int kGroupStride = (kKChunk / 8) * 128;     // bytes between 8-row groups (1 KB)
 constexpr int kMaxCluster = 8;
 // the epilogue's output tile, [token][kStage] floats (a token's 128 rows contiguous,
 // 16-byte aligned rows for bulk stores)
 constexpr int kStage = kMmaTileM + 4;
-constexpr int kRedBytes = kMmaMaxN * kStage * 4;
 constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kXWarp = 6, kConvWarp0 = 7, kConvWarps = 16;
 constexpr int kMma2Warp = kConvWarp0 + kConvWarps;  // second MMA issuer of CTAs with several tiles
 constexpr int kMmaThreads = (kMma2Warp + 1) * 32;
 constexpr int kEpiThreadsSingle = (4 + kConvWarps) * 32;  // epilogue + converter warps of a one-tile CTA
-// TMEM column of accumulator chain g (0..3) of a one-tile CTA: chains 0 and 1
-// sit where a several-tile CTA keeps its double-buffered chains 0 and 1
-__host__ __device__ constexpr uint32_t chain_col_single(int g) { return ((g & 1) ? 384u : 0u) + ((g & 2) ? 64u : 0u); }
 constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 4 + 2;
 
+// Two layouts share the block.  Launches of up to kMmaMaxN tokens: kRawStages
+// raw weight stages, the activation stages, then the output tile.  Wider
+// launches (one tile per CTA): kRawStagesWide raw stages and activation stages
+// twice as large; their output tile reuses the raw stages, which are idle once
+// the tile's last MMA has committed.
 struct MmaSmem {
-    int raw, x16, red, tok, segs, bars, tmem, total;
+    int raw, x16, red, x16w, redw, tok, segs, bars, tmem, total;
 };
 
 __host__ __device__ constexpr MmaSmem mma_smem() {
     MmaSmem L{};
-    int off = 0;
-    L.raw = off;
-    off += kRawStages * kRawStageBytes;
-    L.x16 = off;
-    off += kStages * kX16Bytes;
-    L.red = off;
-    off += kRedBytes;
+    L.raw = 0;
+    L.x16 = kRawStages * kRawStageBytes;
+    L.red = L.x16 + kStages * kMmaMaxN * kKChunk * 2;
+    const int narrow_end = L.red + kMmaMaxN * kStage * 4;
+    L.x16w = kRawStagesWide * kRawStageBytes;
+    L.redw = 0;
+    const int wide_end = L.x16w + kStages * kMmaMaxNWide * kKChunk * 2;
+    int off = narrow_end > wide_end ? narrow_end : wide_end;
     L.tok = off;  // x_inv, positions and KV slots of the launch's tokens, then argmax keys
-    off += 3 * kMmaMaxN * 4 + kMmaMaxN * 8;
+    off += 3 * kMmaMaxNWide * 4 + kMmaMaxNWide * 8;
     L.segs = off;  // the launch's segments and weight scale exponents
     off += kMaxSegs * static_cast<int>(sizeof(MmaSeg)) + 2 * kMaxSegs * 4;
     off = (off + 7) / 8 * 8;
@@ -102,6 +107,8 @@ __host__ __device__ constexpr MmaSmem mma_smem() {
     return L;
 }
 static_assert(mma_smem().total <= 227 * 1024, "shared memory of the tensor-core GEMM");
+static_assert(mma_smem().redw + kMmaMaxNWide * kStage * 4 <= mma_smem().x16w, "wide output tile within the raw stages");
+static_assert(mma_smem().x16 % 128 == 0 && mma_smem().x16w % 128 == 0, "activation stages aligned");
 static_assert((kStage * 4) % 16 == 0, "bulk-store rows");
 
 // Tokens per part's epilogue slice (a multiple of 4).
@@ -594,17 +601,26 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
     uint64_t *part_ready = acc_empty + 2, *part_free = part_ready + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem);
     uint32_t *cta_abort = tmem_slot + 1;
-    float *red = reinterpret_cast<float *>(smem + L.red);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = p.cols / 256;
     const int n_pad = p.n_pad;
+    // more than kMmaMaxN tokens: the wide layout (one tile per CTA, checked below)
+    const bool wide = n_pad > kMmaMaxN;
+    const int nraw = wide ? kRawStagesWide : kRawStages;
+    uint8_t *const x16_s = smem + (wide ? L.x16w : L.x16);
+    const uint32_t xstage = static_cast<uint32_t>(n_pad) * kKChunk * 2;  // bytes of one activation stage
+    float *red = reinterpret_cast<float *>(smem + (wide ? L.redw : L.red));
     const int ksplit = p.ksplit;
     const int rank = static_cast<int>(cluster_rank());
     const int tile_first = static_cast<int>(cluster_id()), tile_step = static_cast<int>(cluster_count());
     const int b0 = rank * p.bps, b1 = min(nb, b0 + p.bps);  // this part's block columns
     const uint32_t tmem_cols = kTmemCols;
     const bool single = tile_first + tile_step >= p.total_tiles;  // this CTA has one tile
+    if (wide && !single) {  // the host only launches wide tiles one per CTA (mma_wide_ok)
+        if (threadIdx.x == 0) atomicOr(p.status, kDevErrBadIndex);
+        return;  // the whole cluster leaves before any barrier or TMEM allocation
+    }
 
     MmaSeg *seg_s = reinterpret_cast<MmaSeg *>(smem + L.segs);
     int *wexp_s = reinterpret_cast<int *>(seg_s + kMaxSegs);
@@ -630,7 +646,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
             mbar_init(empty + i, 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(acc_full + i, single ? 4 : 2);  // a commit from each issuing thread
+            mbar_init(acc_full + i, 2);  // a commit from each issuing thread
             mbar_init(acc_empty + i, 4);
         }
         mbar_init(part_ready, ksplit);
@@ -652,15 +668,16 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
     // MMA issue for the 64-wide groups in `mask` of every block column: D (fp32)
     // [128 x n_pad] = A (fp16 weights in TMEM) * B (fp16 activation, K-major)^T,
     // into one accumulator chain per issuing thread (summed by the epilogue).
-    // A thread issues a tcgen05.mma only every ~130 cycles whatever N, while
-    // several threads issuing into separate accumulators share the tensor core
-    // (four reach ~43 cycles per M=128 N=64 K=16 MMA), so a CTA with a single
-    // tile has its four epilogue warps, idle until then, issue one group's chain
-    // each; a CTA with several tiles issues from warps 1 (even groups) and 23
-    // (odd groups) with the accumulators double-buffered across tiles.
+    // A thread issues a tcgen05.mma only every ~130 cycles whatever N, while two
+    // threads issuing into separate accumulators share the tensor core (~69
+    // cycles per MMA): warps 1 (even groups, TMEM columns from 0) and 23 (odd
+    // groups, from 384) issue, for every CTA, so every launch sums a token's
+    // products in the same order whatever its width (chains of up to 128
+    // columns beside the 256 columns of weight stages); CTAs with several tiles
+    // double-buffer the chains across tiles.
     auto mma_loop = [&](uint32_t mask, uint32_t chain_col) {
         const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(n_pad >> 3) << 17) | (8u << 24);
-        const uint64_t b_desc0 = umma_desc(smem_u32(smem + L.x16), kCoreStride, kGroupStride);
+        const uint64_t b_desc0 = umma_desc(smem_u32(x16_s), kCoreStride, kGroupStride);
         uint32_t blk = 0, i = 0;
         for (int t = tile_first; t < p.total_tiles; t += tile_step, ++i) {
             const int a = i & 1;
@@ -679,7 +696,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                     // A: stage st's 32 TMEM columns, 8 per K=16 step; B: the descriptor's
                     // address field advances by 16 B units (stage, then 256 B per K=16 step)
                     const uint32_t ta = tmem_base + kTmemA + static_cast<uint32_t>(st * 32);
-                    const uint64_t bd = b_desc0 + static_cast<uint64_t>(st * (kX16Bytes >> 4));
+                    const uint64_t bd = b_desc0 + static_cast<uint64_t>(st * (xstage >> 4));
 #pragma unroll
                     for (int kk = 0; kk < kKChunk / 16; ++kk) {
                         umma_f16_ta(dcol, ta + kk * 8, bd + kk * 16, idesc, acc);
@@ -706,8 +723,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                 const MmaWeight &wa = p.w[sg.w0], &wb = pair ? p.w[sg.w1] : p.w[sg.w0];
                 const long ga = pair ? lt : 2L * lt, gb = pair ? lt : 2L * lt + 1;
                 for (int b = b0; b < b1; ++b, ++rc) {
-                    if (rc >= kRawStages)
-                        mbar_wait_bounded(empty_raw + r, ((rc / kRawStages) - 1) & 1, p.status, cta_abort);
+                    if (rc >= static_cast<uint32_t>(nraw))
+                        mbar_wait_bounded(empty_raw + r, ((rc / nraw) - 1) & 1, p.status, cta_abort);
                     uint8_t *dst = smem + L.raw + r * kRawStageBytes;
                     if (sg.type == kQ4K) {
                         mbar_arrive_expect_tx(full_raw + r, 2 * kMmaChunkQ4);
@@ -722,7 +739,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                         bulk_g2s_evict_first(dst + kQ6DOff, ca + kMmaChunkQ6Body, kMmaRowGroup * 2, full_raw + r, pol);
                         bulk_g2s_evict_first(dst + kQ6DOff + kMmaRowGroup * 2, cb + kMmaChunkQ6Body, kMmaRowGroup * 2, full_raw + r, pol);
                     }
-                    if (++r == kRawStages) r = 0;
+                    if (++r == nraw) r = 0;
                 }
             }
         }
@@ -740,14 +757,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                         const int st = (blk & 1) * kGroups + g;
                         if (use) mbar_wait_bounded(empty + st, (use - 1) & 1, p.status, cta_abort);
                         mbar_arrive_expect_tx(full + st, xbytes);
-                        bulk_g2s(smem + L.x16 + st * kX16Bytes, p.x16 + static_cast<long>(b * kGroups + g) * xbytes,
+                        bulk_g2s(x16_s + st * xstage, p.x16 + static_cast<long>(b * kGroups + g) * xbytes,
                                  xbytes, full + st);
                     }
                 }
             }
         }
     } else if (warp == kMmaWarp || warp == kMma2Warp) {
-        if (lane == 0 && !single) mma_loop(warp == kMmaWarp ? 0x5u : 0xAu, warp == kMmaWarp ? 0u : kTmemAcc1);
+        if (lane == 0) mma_loop(warp == kMmaWarp ? 0x5u : 0xAu, warp == kMmaWarp ? 0u : kTmemAcc1);
     } else {
         const bool conv = warp >= kConvWarp0;
         if (conv) {
@@ -766,7 +783,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                     const int st = (blk & 1) * kGroups + g;
                     const uint32_t use = blk >> 1;
                     const uint32_t tmem_row = tmem_lane + static_cast<uint32_t>(st * 32);
-                    mbar_wait_bounded(full_raw + r, (blk / kRawStages) & 1, p.status, cta_abort);
+                    mbar_wait_bounded(full_raw + r, (blk / nraw) & 1, p.status, cta_abort);
                     if (use) mbar_wait_bounded(empty + st, (use - 1) & 1, p.status, cta_abort);
                     tc_fence_after();
                     const uint8_t *raw = smem + L.raw + r * kRawStageBytes;
@@ -779,7 +796,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                         mbar_arrive(full + st);
                         mbar_arrive(empty_raw + r);
                     }
-                    if (++r == kRawStages) r = 0;
+                    if (++r == nraw) r = 0;
                 }
             }
         }
@@ -797,16 +814,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
             // warp of the quadrant takes all
             const int jq = conv ? (warp - kConvWarp0) / 4 : -1;
             const int cb_first = single ? jq : 0, cb_step = single ? 4 : 1;
-            if (!conv) {
-                if (single) {  // first issue group (warp - 2)'s accumulation chain
-                    if (lane == 0) mma_loop(1u << (warp - kEpiWarp0), chain_col_single(warp - kEpiWarp0));
-                    __syncwarp();
-                }
-                pdl_wait();
-            }
+            if (!conv) pdl_wait();
             float *xinv_s = reinterpret_cast<float *>(smem + L.tok);
-            int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxN), *slot_s = pos_s + kMmaMaxN;
-            unsigned long long *keys_s = reinterpret_cast<unsigned long long *>(slot_s + kMmaMaxN);
+            int *pos_s = reinterpret_cast<int *>(xinv_s + kMmaMaxNWide), *slot_s = pos_s + kMmaMaxNWide;
+            unsigned long long *keys_s = reinterpret_cast<unsigned long long *>(slot_s + kMmaMaxNWide);
             if (!conv && dr < n_pad) {
                 xinv_s[dr] = p.x_inv[dr];
                 pos_s[dr] = p.tok_pos && dr < p.batch ? p.tok_pos[dr] : 0;
@@ -848,34 +859,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1) ijb_mma_gemm_kernel(const __gr
                 // accumulator chains -> stage[token][row], summed in a fixed order and scaled
                 float *stage = red;
                 if (cb_first >= 0) {
-                    // 8 columns at a time: (chain 0 + chain 1) [+ (chain 2 + chain 3)]
+                    // 8 columns at a time: chain 0 + chain 1
                     for (int c0 = cb_first * 16; c0 < n_pad; c0 += cb_step * 16) {
 #pragma unroll 1
                         for (int h = 0; h < 16; h += 8) {
                             const int c = c0 + h;
-                            uint32_t v[8], w[8], v2[8], w2[8];
+                            uint32_t v[8], w[8];
                             float sum[8];
-                            if (single) {
-                                tmem_ld8_nw(taddr + chain_col_single(0) + c, v);
-                                tmem_ld8_nw(taddr + chain_col_single(1) + c, w);
-                                tmem_ld8_nw(taddr + chain_col_single(2) + c, v2);
-                                tmem_ld8_nw(taddr + chain_col_single(3) + c, w2);
-                                tmem_wait8(v);
-                                tmem_wait8(w);
-                                tmem_wait8(v2);
-                                tmem_wait8(w2);
+                            tmem_ld8_nw(taddr + a * n_pad + c, v);
+                            tmem_ld8_nw(taddr + kTmemAcc1 + a * n_pad + c, w);
+                            tmem_wait8(v);
+                            tmem_wait8(w);
 #pragma unroll
-                                for (int k = 0; k < 8; ++k)
-                                    sum[k] = (__uint_as_float(v[k]) + __uint_as_float(w[k])) +
-                                             (__uint_as_float(v2[k]) + __uint_as_float(w2[k]));
-                            } else {
-                                tmem_ld8_nw(taddr + a * n_pad + c, v);
-                                tmem_ld8_nw(taddr + kTmemAcc1 + a * n_pad + c, w);
-                                tmem_wait8(v);
-                                tmem_wait8(w);
-#pragma unroll
-                                for (int k = 0; k < 8; ++k) sum[k] = __uint_as_float(v[k]) + __uint_as_float(w[k]);
-                            }
+                            for (int k = 0; k < 8; ++k) sum[k] = __uint_as_float(v[k]) + __uint_as_float(w[k]);
 #pragma unroll
                             for (int k = 0; k < 8; ++k) stage[(c + k) * kStage + dr] = sum[k] * wscale * xinv_s[c + k];
                         }
@@ -1152,7 +1148,7 @@ __global__ void ijb_mma_scale_scan_kernel(int type, const uint8_t *w, long nbloc
 
 cudaError_t mma_prep_launch(const float *x, long x_stride, const float *norm_w, float eps, int cols, int batch,
                             int n_pad, int use_dp4a, uint8_t *x16, float *x_inv, cudaStream_t stream, bool pdl) {
-    if (cols % 256 || cols > kMaxCols || batch < 1 || n_pad > kMmaMaxN || n_pad % 16) return cudaErrorInvalidValue;
+    if (cols % 256 || cols > kMaxCols || batch < 1 || n_pad > kMmaMaxNWide || n_pad % 16) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_pad);
     cfg.blockDim = dim3(256);
@@ -1270,8 +1266,13 @@ int mma_choose_split(int tiles, int nblocks, int max_split, int split_cost, int 
     return best_k;
 }
 
+bool mma_wide_ok(int tiles, int ksplit) {
+    return ksplit >= 1 && ksplit <= kMaxCluster && tiles >= 1 && g_cluster_cap[ksplit] >= tiles;
+}
+
 cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl) {
-    if (p.n_pad < 16 || p.n_pad > kMmaMaxN || p.n_pad % 16 || p.cols % 256 || p.total_tiles < 1 || p.ksplit < 1 ||
+    if (p.n_pad > kMmaMaxN && !mma_wide_ok(p.total_tiles, p.ksplit)) return cudaErrorInvalidValue;
+    if (p.n_pad < 16 || p.n_pad > kMmaMaxNWide || p.n_pad % 16 || p.cols % 256 || p.total_tiles < 1 || p.ksplit < 1 ||
         p.ksplit > kMaxCluster || p.bps < 1 || (p.ksplit - 1) * p.bps >= p.cols / 256 ||
         p.ksplit * p.bps < p.cols / 256 || g_cluster_cap[p.ksplit] < 1)
         return cudaErrorInvalidValue;

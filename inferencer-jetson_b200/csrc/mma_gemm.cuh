@@ -1,5 +1,5 @@
 // Host-visible description of the tensor-core (tcgen05) quantised GEMM used
-// for packed steps of 16..64 tokens.
+// for packed steps of 3..128 tokens per launch.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -11,6 +11,10 @@ namespace ijb {
 
 constexpr int kMmaTileM = 128;    // weight rows per tile (TMEM lanes)
 constexpr int kMmaMaxN = 64;      // tokens per launch (MMA N, padded to 16)
+// Tokens per launch when every CTA of the launch holds one tile
+// (mma_wide_ok): the activation stages double and the output tile reuses the
+// raw weight stages, so each weight tile is dequantised once for 128 tokens.
+constexpr int kMmaMaxNWide = 128;
 // Engines with max_batch >= kMmaEngineMinBatch hold the tensor-core weight copy
 // and run steps of kMmaMinBatch or more tokens on it (measured on B200, 1B decode
 // steps: 2 tokens 1.01 ms on CUDA cores / 1.20 ms on the tensor cores; 3 tokens
@@ -70,7 +74,7 @@ struct MmaParams {
     int bps;
     int bulk_out;  // finished token rows leave as bulk (TMA engine) copies, else as coalesced thread stores
     int cols;             // K
-    int batch;            // tokens in this launch (<= kMmaMaxN)
+    int batch;            // tokens in this launch (<= kMmaMaxN, or kMmaMaxNWide when mma_wide_ok)
     int n_pad;            // MMA N: batch rounded up to 16
     const uint8_t *x16;   // prepared activation (mma_prep_launch), [cols/128][n_pad/8][16][8][16 B]
     const float *x_inv;   // [n_pad] 2^-kx of each token
@@ -117,6 +121,10 @@ cudaError_t mma_gemm_launch(const MmaParams &p, cudaStream_t stream, bool pdl);
 // columns of time); *bps receives block columns per part.  Needs
 // mma_prepare() first.
 int mma_choose_split(int tiles, int nblocks, int max_split, int split_cost, int *bps);
+// Whether a launch of `tiles` tiles in clusters of `ksplit` parts gives every
+// CTA a single tile (all clusters resident at once), which launches of more
+// than kMmaMaxN tokens require.  Needs mma_prepare() first.
+bool mma_wide_ok(int tiles, int ksplit);
 // Sets the kernel's shared-memory limit and measures cluster occupancy for
 // the current device.
 cudaError_t mma_prepare();

@@ -1,4 +1,4 @@
-"""The tensor-core (tcgen05) path for packed steps of 16..64 tokens.
+"""The tensor-core (tcgen05) path for packed steps (up to 128 tokens per launch).
 
 Weights are dequantised exactly (the reference's q4_value / q6_value) and
 rounded once to fp16 with a per-matrix power-of-two scale; activations are
@@ -12,11 +12,13 @@ next projection, so the test measures the path's own floor (two oracle
 variants differing in one multiply-add contraction) on the same sequences and
 holds the GPU to twice it, with the same greedy bar.  The same checks at the
 1B widths and 64 sequences are in test_gpu_headline.py."""
+import os
+
 import numpy as np
 import pytest
 
 import oracle as O
-from ijb200 import synth
+from ijb200 import lib, synth
 from ijb200.engine import Engine
 
 pytestmark = pytest.mark.gpu
@@ -149,14 +151,18 @@ def test_ragged_step_tensor_core_vs_oracle(cuda, dp4a):
 
 
 @pytest.mark.parametrize("cfg", [synth.TINY, synth.TINY_HD128_G3], ids=lambda c: c.name)
-def test_wide_step_chunks_match_narrow_steps(cuda, cfg):
-    """A 150-token step runs its three 64-token tensor-core chunks on parallel
-    graph branches (own activation tiles, same weights).  Its logits and next
+@pytest.mark.parametrize("n", [150, 100])
+def test_wide_step_chunks_match_narrow_steps(cuda, cfg, n):
+    """A step of more than 64 tokens runs its per-layer projections in chunks
+    of up to 128 tokens (every CTA of those launches holds one tile: the wide
+    shared-memory layout, N = 128 accumulator chains) on parallel graph
+    branches, and the vocab projection in 64-token chunks.  Its logits and next
     tokens equal, bit for bit, those of an engine with max_batch 64 that
-    decodes the same sequences in three steps of 64, 64 and 22 tokens (the same
-    chunks through the same kernels), over three steps with prefill."""
+    decodes the same sequences in steps of at most 64 tokens: every launch
+    width sums a token's products in the same order.  150 tokens: a full
+    128-token chunk and a 22-token one; 100 tokens: one chunk padded to 112."""
     weights = synth.make_model(cfg, seed=12)
-    reqs = synth.ragged_requests(150, prompt_range=(3, 40), output_range=(8, 16), seed=4, vocab_limit=cfg.vocab)
+    reqs = synth.ragged_requests(n, prompt_range=(3, 40), output_range=(8, 16), seed=4, vocab_limit=cfg.vocab)
     wide = Engine(cfg, weights, context=64, max_batch=160, max_seqs=151)
     narrow = Engine(cfg, weights, context=64, max_batch=64, max_seqs=151)
     ws = [wide.seq_open() for _ in reqs]
@@ -164,10 +170,10 @@ def test_wide_step_chunks_match_narrow_steps(cuda, cfg):
     cw = [wide.seq_prefill(s, r.prompt) for s, r in zip(ws, reqs)]
     cn = [narrow.seq_prefill(s, r.prompt) for s, r in zip(ns, reqs)]
     assert cw == cn
-    cuts = [(0, 64), (64, 128), (128, 150)]
+    cuts = [(a, min(n, a + 64)) for a in range(0, n, 64)]
     for step in range(3):
         out_w = list(wide.decode_step(ws, cw))
-        lw = wide.logits(150)
+        lw = wide.logits(n)
         out_n, ln = [], []
         for a, b in cuts:
             out_n += list(narrow.decode_step(ns[a:b], cn[a:b]))
@@ -176,5 +182,23 @@ def test_wide_step_chunks_match_narrow_steps(cuda, cfg):
         assert out_w == out_n, step
         assert np.array_equal(lw.view(np.uint32), ln.view(np.uint32)), step
         cw, cn = out_w, out_n
+    # the wide engine's step really ran 128-token chunks: fewer launches than the
+    # same engine with 128-token chunks switched off (IJB_MMA_WIDE=0)
+    os.environ["IJB_MMA_WIDE"] = "0"
+    try:
+        off = Engine(cfg, weights, context=64, max_batch=160, max_seqs=151)
+    finally:
+        del os.environ["IJB_MMA_WIDE"]
+    os_ = [off.seq_open() for _ in reqs]
+    co = [off.seq_prefill(s, r.prompt) for s, r in zip(os_, reqs)]
+    L = lib.load()
+    counts = []
+    for eng, seqs, toks in ((wide, ws, cw), (off, os_, co)):
+        eng.decode_step(seqs, toks)  # captures the step graph
+        before = L.ijb_kernel_launches()
+        eng.decode_step(seqs, toks)
+        counts.append(L.ijb_kernel_launches() - before)
+    assert counts[0] < counts[1], counts
+    off.close()
     wide.close()
     narrow.close()
