@@ -6,11 +6,11 @@
 // cache.  Two kernels here, both splitting a sequence's positions and keeping
 // an online-softmax state (max, sum, unnormalised output) per split, the KV
 // group's query heads sharing every K/V row loaded:
-//  * ijb_attention_stream_kernel (fp16 cache, head_dim 64): persistent, one CTA of
+//  * ijb_attention_stream_kernel (fp16 cache, head_dim 64 or 128): persistent, one CTA of
 //    streaming warps per SM, 128-position work items, tensor-core chunks; the
 //    splits are merged by ijb_attention_finish_kernel (one CTA per token);
-//  * ijb_attention_kernel (fp32 cache or head_dim 128, and beyond the streaming
-//    kernel's limits): one CTA per (token, kv head, split of 512 positions) on
+//  * ijb_attention_kernel (fp32 cache, and beyond the streaming kernel's
+//    limits): one CTA per (token, kv head, split of up to 512 positions) on
 //    CUDA cores, lanes owning positions while scoring and head-dim elements
 //    while accumulating V; the last CTA of a (token, kv head) to finish merges
 //    the splits (elected with an atomic counter that it resets for the next
@@ -300,10 +300,10 @@ __global__ void __launch_bounds__(kAttnThreads) ijb_attention_kernel(const __gri
 
 // ------------------------------------------------ tensor-core variant --
 //
-// fp16 cache, head_dim 64: the same CTA/warp/chunk schedule as above, but
+// fp16 cache, head_dim 64 or 128 (HD / 64 swizzled 128-byte halves per row):
 // scores and P·V run on mma.sync.m16n8k16 (fp16 in, fp32 accumulate).  The
-// query heads of the KV group are the M rows (G of 16, the rest zero), a
-// chunk's 32 positions the N (scores) or K (P·V) extent.  K/V page runs arrive
+// chunk's positions (scores) or the head dims (P·V) are the M rows, the KV
+// group's query heads the 8 columns (attn_chunk_t below).  K/V page runs arrive
 // through a 3-D TMA map with 128-byte swizzle, so the ldmatrix reads of both
 // tiles are free of bank conflicts; the P fragment is built in registers from
 // the score accumulators.  The query and the probabilities enter the MMAs as
@@ -464,7 +464,7 @@ __device__ __forceinline__ void attn_chunk_t(uint32_t kt, uint32_t vt, int cnt, 
 
 // ------------------------------------------------ streaming variant --
 //
-// fp16 cache, head_dim 64, tensor-core chunks as above, as a persistent
+// fp16 cache, head_dim 64 or 128, tensor-core chunks as above, as a persistent
 // kernel: one CTA of stream_warps<HD>() independent warps per SM.  The work is cut
 // into items of up to kAttnItem positions of one (token, kv head): a warp's
 // first item is fixed by its index, the next ones come from a device-wide

@@ -8,7 +8,7 @@
 namespace ijb {
 
 struct AttnParams {
-    // fp16 cache with head_dim 64: 3-D TMA map over this layer's pool, box =
+    // fp16 cache with head_dim 64 or 128: 3-D TMA map over this layer's pool, box =
     // one (page, kv head) run of page_size rows, 128-byte swizzled (see
     // attention_make_kv_map); the tensor-core kernel is used when has_map
     CUtensorMap kv_map;
@@ -47,7 +47,7 @@ cudaError_t attention_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
 int attention_kernels(const AttnParams &p);  // kernels attention_launch launches for p
 // Encodes the TMA map of one layer's fp16 KV pool for the tensor-core
 // kernel: dims {head_dim, 2 * kv_heads * page_size rows, num_pages}; returns
-// 0 on success, -1 where the tensor-core kernel does not apply (head_dim != 64).
+// 0 on success, -1 where the tensor-core kernel does not apply (head_dim not 64 or 128).
 int attention_make_kv_map(CUtensorMap *map, const void *layer_base, int head_dim, int kv_heads, int page_size,
                           long page_stride_elems, long num_pages);
 int attention_split_len();      // longest split of the split kernel (positions)
