@@ -298,6 +298,35 @@ uint64_t ijb_kernel_launches(void);
  * counterpart of FastGPU's event timer (start_timer/stop_timer, inferencer.cu:1172-1179). */
 float ijb_last_step_ms(const ijb_engine *engine);
 
+/* ---- tokenizer (host only; no GPU involved) ----
+ * Llama-3 byte-level BPE over a GGUF vocabulary, replacing the reference's
+ * Tokenizer (inferencer.cu:361-451) with the same results: its pre-tokenizer
+ * pattern matched by PCRE2 (the runtime library libpcre2-8.so.0, loaded on
+ * first use), its byte-symbol map, merges applied lowest rank first and
+ * leftmost first, and its error messages.  Thread-safe after creation. */
+typedef struct ijb_tokenizer ijb_tokenizer;
+
+/* Builds a tokenizer from tokenizer.ggml.tokens (exactly 128256 strings, as
+ * the reference requires: "Expected Llama 3 tokenizer") and
+ * tokenizer.ggml.merges ("left right" strings, rank = index); on failure the
+ * message is available from ijb_tokenizer_last_error(NULL) in this thread.
+ * Replaces Tokenizer::Tokenizer (inferencer.cu:368-390). */
+int ijb_tokenizer_create(const char *const *tokens, int n_tokens, const char *const *merges, int n_merges,
+                         ijb_tokenizer **out);
+void ijb_tokenizer_destroy(ijb_tokenizer *tokenizer);
+/* Message of the last failed call on `tokenizer` (NULL: of the last failed
+ * ijb_tokenizer_create in this thread).  Never NULL. */
+const char *ijb_tokenizer_last_error(const ijb_tokenizer *tokenizer);
+/* Token ids of len bytes of text (Tokenizer::encode, :415-431): writes the
+ * first min(cap, *n) ids to ids and the full count to *n (call again with a
+ * larger buffer when *n > cap). */
+int ijb_tokenizer_encode(ijb_tokenizer *tokenizer, const char *text, long len, int *ids, long cap, long *n);
+/* The bytes token id stands for (Tokenizer::decode, :432-445): writes the
+ * first min(cap, *len) bytes and the full length to *len. */
+int ijb_tokenizer_decode(ijb_tokenizer *tokenizer, int id, char *bytes, int cap, int *len);
+/* Id of a token by its exact string, e.g. "<|eot_id|>" (Tokenizer::special, :446-450). */
+int ijb_tokenizer_special(ijb_tokenizer *tokenizer, const char *name, int *id);
+
 #ifdef __cplusplus
 }
 #endif

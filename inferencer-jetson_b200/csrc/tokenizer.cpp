@@ -1,0 +1,478 @@
+// Llama-3 byte-level BPE tokenizer (host code behind the C ABI).
+//
+// Replaces the reference's Tokenizer (inferencer.cu:361-451) with the same
+// results: the same Unicode pre-tokenizer pattern (matched by PCRE2 with UTF
+// and UCP, as the reference does), each match's bytes mapped to the GGUF
+// byte symbols (bytes 33-126, 161-172 and 174-255 stand for themselves, the
+// others for code points 256, 257, ... in byte order), then merges applied
+// lowest rank first, leftmost first among equal ranks, until none applies.
+//
+// What differs is the cost.  The reference rebuilds a "left right" string
+// and hashes it for every adjacent pair on every merge step (quadratic in
+// the piece length, with string allocations), and lets PCRE2 re-check the
+// text's UTF-8 on every match call.  Here the merges are a hash map from a
+// pair of token ids to (rank, merged id); a piece of up to kScanMax symbols
+// is merged by scanning an id array, a longer one through a min-heap of
+// (rank, position) entries over a linked list (n log n); the text's UTF-8 is
+// validated once and the pattern runs JIT-compiled; and pieces already seen
+// are served from a cache.  PCRE2 is loaded from its runtime library
+// (libpcre2-8.so.0) when the first tokenizer is created.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <mutex>
+#include <queue>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <utility>
+#include <vector>
+
+#include "../../include/ijb200.h"
+
+namespace {
+
+// ------------------------------------------------------------------ PCRE2 --
+// The 8-bit entry points and option values of PCRE2's public API.
+struct Pcre2 {
+    void *(*compile)(const uint8_t *, size_t, uint32_t, int *, size_t *, void *) = nullptr;
+    int (*jit_compile)(void *, uint32_t) = nullptr;
+    void *(*match_data_create)(const void *, void *) = nullptr;
+    int (*match)(const void *, const uint8_t *, size_t, size_t, uint32_t, void *, void *) = nullptr;
+    size_t *(*ovector)(void *) = nullptr;
+    void (*match_data_free)(void *) = nullptr;
+    void (*code_free)(void *) = nullptr;
+};
+constexpr uint32_t kPcre2Ucp = 0x00020000u, kPcre2Utf = 0x00080000u, kPcre2NoUtfCheck = 0x40000000u;
+constexpr uint32_t kPcre2JitComplete = 0x00000001u;
+constexpr size_t kPcre2ZeroTerminated = ~static_cast<size_t>(0);
+
+const Pcre2 &pcre2() {
+    static Pcre2 api;
+    static std::once_flag once;
+    static std::string error;
+    std::call_once(once, [] {
+        void *lib = dlopen("libpcre2-8.so.0", RTLD_NOW | RTLD_LOCAL);
+        if (!lib) {
+            error = "PCRE2 runtime library (libpcre2-8.so.0) not found";
+            return;
+        }
+        auto sym = [&](const char *name) { return dlsym(lib, name); };
+        api.compile = reinterpret_cast<decltype(api.compile)>(sym("pcre2_compile_8"));
+        api.jit_compile = reinterpret_cast<decltype(api.jit_compile)>(sym("pcre2_jit_compile_8"));
+        api.match_data_create =
+            reinterpret_cast<decltype(api.match_data_create)>(sym("pcre2_match_data_create_from_pattern_8"));
+        api.match = reinterpret_cast<decltype(api.match)>(sym("pcre2_match_8"));
+        api.ovector = reinterpret_cast<decltype(api.ovector)>(sym("pcre2_get_ovector_pointer_8"));
+        api.match_data_free = reinterpret_cast<decltype(api.match_data_free)>(sym("pcre2_match_data_free_8"));
+        api.code_free = reinterpret_cast<decltype(api.code_free)>(sym("pcre2_code_free_8"));
+        if (!api.compile || !api.match_data_create || !api.match || !api.ovector || !api.match_data_free ||
+            !api.code_free)
+            error = "PCRE2 runtime library lacks its 8-bit API";
+    });
+    if (!error.empty()) throw std::runtime_error(error);
+    return api;
+}
+
+// Llama 3's pre-tokenizer (the pattern inferencer.cu:379-383 compiles).
+const char *const kPattern =
+    "(?:'[sS]|'[tT]|'[rR][eE]|'[vV][eE]|'[mM]|'[lL][lL]|'[dD])|"
+    "[^\\r\\n\\p{L}\\p{N}]?\\p{L}+|\\p{N}{1,3}|"
+    " ?[^\\s\\p{L}\\p{N}]+[\\r\\n]*|\\s*[\\r\\n]+|\\s+(?!\\S)|\\s+";
+
+// Strict UTF-8 (RFC 3629: no overlong forms, no surrogates, nothing above
+// U+10FFFF) — the check PCRE2 applies to a UTF subject.
+bool valid_utf8(const uint8_t *s, size_t n) {
+    size_t i = 0;
+    while (i < n) {
+        const uint8_t c = s[i];
+        if (c < 0x80) {
+            ++i;
+            continue;
+        }
+        int len;
+        uint32_t cp;
+        if (c >= 0xc2 && c <= 0xdf) {
+            len = 2;
+            cp = c & 0x1f;
+        } else if (c >= 0xe0 && c <= 0xef) {
+            len = 3;
+            cp = c & 0x0f;
+        } else if (c >= 0xf0 && c <= 0xf4) {
+            len = 4;
+            cp = c & 0x07;
+        } else {
+            return false;
+        }
+        if (i + len > n) return false;
+        for (int k = 1; k < len; ++k) {
+            const uint8_t t = s[i + k];
+            if ((t & 0xc0) != 0x80) return false;
+            cp = (cp << 6) | (t & 0x3f);
+        }
+        if ((len == 3 && cp < 0x800) || (len == 4 && (cp < 0x10000 || cp > 0x10ffff)) ||
+            (cp >= 0xd800 && cp <= 0xdfff))
+            return false;
+        i += len;
+    }
+    return true;
+}
+
+std::string utf8_of(uint32_t cp) {
+    std::string s;
+    if (cp < 0x80) {
+        s.push_back(static_cast<char>(cp));
+    } else if (cp < 0x800) {
+        s.push_back(static_cast<char>(0xc0 | (cp >> 6)));
+        s.push_back(static_cast<char>(0x80 | (cp & 63)));
+    } else {
+        s.push_back(static_cast<char>(0xe0 | (cp >> 12)));
+        s.push_back(static_cast<char>(0x80 | ((cp >> 6) & 63)));
+        s.push_back(static_cast<char>(0x80 | (cp & 63)));
+    }
+    return s;
+}
+
+constexpr int kLlama3Vocab = 128256;
+constexpr int kScanMax = 24;          // pieces up to this many symbols merge by array scans
+constexpr size_t kCacheMaxPiece = 64;  // pieces up to this many bytes are cached
+constexpr size_t kCacheMaxEntries = 1u << 20;
+
+}  // namespace
+
+struct ijb_tokenizer {
+    std::vector<std::string> tokens;
+    std::unordered_map<std::string, int> ids;            // first occurrence of a token string
+    std::unordered_map<std::string, int> rank;           // first occurrence of a merge string
+    std::unordered_map<uint64_t, uint64_t> pair;         // (left id, right id) -> rank << 32 | merged id
+    int byte_id[256];                                    // token id of each byte's symbol
+    std::string byte_symbol[256];
+    std::unordered_map<std::string, uint8_t> symbol_byte;
+    bool regular = true;  // every byte symbol and every merge result is a token: the id fast path applies
+    std::vector<std::string> decoded;  // bytes of each token
+    std::vector<uint8_t> decode_err;   // 0, 1 malformed UTF-8, 2 a character that is no byte symbol
+    void *code = nullptr;
+    bool jit = false;
+    mutable std::mutex cache_mu;
+    mutable std::unordered_map<std::string, std::vector<int>> cache;
+    std::string error;
+
+    ~ijb_tokenizer() {
+        if (code) pcre2().code_free(code);
+    }
+
+    // ------------------------------------------------------- BPE, by ids --
+    uint64_t lookup(int a, int b) const {
+        const auto it = pair.find(static_cast<uint64_t>(static_cast<uint32_t>(a)) << 32 | static_cast<uint32_t>(b));
+        return it == pair.end() ? ~0ull : it->second;
+    }
+
+    void merge_ids(const uint8_t *p, size_t n, std::vector<int> &out) const {
+        if (n <= static_cast<size_t>(kScanMax)) {
+            int sym[kScanMax];
+            int m = static_cast<int>(n);
+            for (int i = 0; i < m; ++i) sym[i] = byte_id[p[i]];
+            while (m > 1) {
+                uint64_t best = ~0ull;
+                int at = -1;
+                for (int i = 0; i + 1 < m; ++i) {
+                    const uint64_t v = lookup(sym[i], sym[i + 1]);
+                    if ((v >> 32) < (best >> 32)) {  // lower rank; leftmost among equals
+                        best = v;
+                        at = i;
+                    }
+                }
+                if (at < 0) break;
+                sym[at] = static_cast<int>(best & 0xffffffffu);
+                for (int i = at + 1; i + 1 < m; ++i) sym[i] = sym[i + 1];
+                --m;
+            }
+            out.insert(out.end(), sym, sym + m);
+            return;
+        }
+        // linked symbols; heap entries (rank, left position) checked against
+        // the current pair when popped (a node's id only ever grows longer)
+        struct Node {
+            int id, prev, next;
+        };
+        std::vector<Node> s(n);
+        for (size_t i = 0; i < n; ++i)
+            s[i] = {byte_id[p[i]], static_cast<int>(i) - 1, i + 1 < n ? static_cast<int>(i) + 1 : -1};
+        struct Entry {
+            uint64_t key;  // rank << 32 | left position
+            int left_id, right_id;
+            bool operator>(const Entry &o) const { return key > o.key; }
+        };
+        std::priority_queue<Entry, std::vector<Entry>, std::greater<Entry>> heap;
+        auto push = [&](int i) {
+            if (i < 0 || s[i].next < 0) return;
+            const uint64_t v = lookup(s[i].id, s[s[i].next].id);
+            if (v != ~0ull) heap.push({(v >> 32) << 32 | static_cast<uint32_t>(i), s[i].id, s[s[i].next].id});
+        };
+        for (size_t i = 0; i + 1 < n; ++i) push(static_cast<int>(i));
+        while (!heap.empty()) {
+            const Entry e = heap.top();
+            heap.pop();
+            const int i = static_cast<int>(e.key & 0xffffffffu);
+            const int j = s[i].next;
+            if (s[i].id != e.left_id || j < 0 || s[j].id != e.right_id) continue;  // stale
+            s[i].id = static_cast<int>(lookup(e.left_id, e.right_id) & 0xffffffffu);
+            s[i].next = s[j].next;
+            if (s[j].next >= 0) s[s[j].next].prev = i;
+            s[j].id = -1;
+            push(s[i].prev);
+            push(i);
+        }
+        for (int i = 0; i >= 0; i = s[i].next) out.push_back(s[i].id);
+    }
+
+    // ------------------------------------------- BPE, by strings (fallback) --
+    // The merge loop on symbol strings, for vocabularies whose merges make
+    // strings that are not tokens (no id to stand for them).
+    void merge_strings(const uint8_t *p, size_t n, std::vector<int> &out) const {
+        std::vector<std::string> parts;
+        parts.reserve(n);
+        for (size_t i = 0; i < n; ++i) parts.push_back(byte_symbol[p[i]]);
+        while (parts.size() > 1) {
+            int best = std::numeric_limits<int>::max();
+            size_t at = 0;
+            for (size_t i = 0; i + 1 < parts.size(); ++i) {
+                const auto it = rank.find(parts[i] + " " + parts[i + 1]);
+                if (it != rank.end() && it->second < best) {
+                    best = it->second;
+                    at = i;
+                }
+            }
+            if (best == std::numeric_limits<int>::max()) break;
+            parts[at] += parts[at + 1];
+            parts.erase(parts.begin() + static_cast<long>(at) + 1);
+        }
+        for (const auto &s : parts) {
+            const auto it = ids.find(s);
+            if (it == ids.end()) throw std::runtime_error("Tokenizer produced an unknown token");
+            out.push_back(it->second);
+        }
+    }
+
+    void piece(const uint8_t *p, size_t n, std::vector<int> &out) const {
+        if (n == 0) return;
+        if (!regular) {
+            merge_strings(p, n, out);
+            return;
+        }
+        if (n == 1) {
+            out.push_back(byte_id[p[0]]);
+            return;
+        }
+        if (n <= kCacheMaxPiece) {
+            const std::string key(reinterpret_cast<const char *>(p), n);
+            {
+                std::lock_guard<std::mutex> lock(cache_mu);
+                const auto it = cache.find(key);
+                if (it != cache.end()) {
+                    out.insert(out.end(), it->second.begin(), it->second.end());
+                    return;
+                }
+            }
+            const size_t first = out.size();
+            merge_ids(p, n, out);
+            std::lock_guard<std::mutex> lock(cache_mu);
+            if (cache.size() >= kCacheMaxEntries) cache.clear();
+            cache.emplace(key, std::vector<int>(out.begin() + static_cast<long>(first), out.end()));
+            return;
+        }
+        merge_ids(p, n, out);
+    }
+
+    // ----------------------------------------------------- pre-tokenizer --
+    void encode(const uint8_t *text, size_t n, std::vector<int> &out) const {
+        const Pcre2 &api = pcre2();
+        // a valid text needs no UTF check per match; an invalid one is matched
+        // exactly as the reference matches it (the failing call ends the loop)
+        const uint32_t opts = valid_utf8(text, n) ? kPcre2NoUtfCheck : 0u;
+        std::unique_ptr<void, void (*)(void *)> md(api.match_data_create(code, nullptr), api.match_data_free);
+        if (!md) throw std::runtime_error("PCRE2 match data allocation failed");
+        size_t pos = 0;
+        while (pos < n) {
+            const int status = api.match(code, text, n, pos, opts, md.get(), nullptr);
+            if (status < 0) {
+                piece(text + pos, n - pos, out);
+                break;
+            }
+            const size_t *span = api.ovector(md.get());
+            if (span[0] > pos) piece(text + pos, span[0] - pos, out);
+            if (span[1] == span[0]) throw std::runtime_error("Tokenizer regex made no progress");
+            piece(text + span[0], span[1] - span[0], out);
+            pos = span[1];
+        }
+    }
+};
+
+namespace {
+
+void build(ijb_tokenizer &t, const char *const *tokens, int n_tokens, const char *const *merges, int n_merges) {
+    if (n_tokens != kLlama3Vocab) throw std::runtime_error("Expected Llama 3 tokenizer");
+    t.tokens.reserve(n_tokens);
+    t.ids.reserve(n_tokens);
+    for (int i = 0; i < n_tokens; ++i) {
+        if (!tokens[i]) throw std::runtime_error("null token string");
+        t.tokens.emplace_back(tokens[i]);
+        t.ids.emplace(t.tokens.back(), i);
+    }
+    t.rank.reserve(n_merges);
+    for (int i = 0; i < n_merges; ++i) {
+        if (!merges[i]) throw std::runtime_error("null merge string");
+        t.rank.emplace(merges[i], i);
+    }
+    uint32_t cp = 256;
+    for (int b = 0; b < 256; ++b) {
+        const bool plain = (b >= 33 && b <= 126) || (b >= 161 && b <= 172) || b >= 174;
+        t.byte_symbol[b] = utf8_of(plain ? static_cast<uint32_t>(b) : cp++);
+        t.symbol_byte.emplace(t.byte_symbol[b], static_cast<uint8_t>(b));
+        const auto it = t.ids.find(t.byte_symbol[b]);
+        t.byte_id[b] = it == t.ids.end() ? -1 : it->second;
+        if (t.byte_id[b] < 0) t.regular = false;
+    }
+    // merges as id pairs: "A B" applies where a part A meets a part B; with
+    // every result a token, each part is always a token (by induction from
+    // the byte symbols), so the pair map covers every merge that can apply
+    t.pair.reserve(static_cast<size_t>(n_merges) * 2);
+    for (const auto &[m, r] : t.rank) {
+        for (size_t sp = m.find(' '); sp != std::string::npos; sp = m.find(' ', sp + 1)) {
+            const auto a = t.ids.find(m.substr(0, sp)), b = t.ids.find(m.substr(sp + 1));
+            if (a == t.ids.end() || b == t.ids.end()) continue;
+            const auto ab = t.ids.find(a->first + b->first);
+            if (ab == t.ids.end()) {
+                t.regular = false;  // a merge whose result is no token
+                continue;
+            }
+            const uint64_t key = static_cast<uint64_t>(static_cast<uint32_t>(a->second)) << 32 |
+                                 static_cast<uint32_t>(b->second);
+            const uint64_t val = static_cast<uint64_t>(static_cast<uint32_t>(r)) << 32 |
+                                 static_cast<uint32_t>(ab->second);
+            const auto ins = t.pair.emplace(key, val);
+            if (!ins.second && (val >> 32) < (ins.first->second >> 32)) ins.first->second = val;
+        }
+    }
+    // decode table: each UTF-8 character of a token string is one byte symbol
+    // (lead-byte lengths as inferencer.cu:434-441 reads them)
+    t.decoded.resize(n_tokens);
+    t.decode_err.assign(n_tokens, 0);
+    for (int id = 0; id < n_tokens; ++id) {
+        const std::string &s = t.tokens[id];
+        std::string bytes;
+        for (size_t i = 0; i < s.size();) {
+            const uint8_t first = static_cast<uint8_t>(s[i]);
+            const size_t n = first < 0x80 ? 1 : first < 0xe0 ? 2 : first < 0xf0 ? 3 : 4;
+            if (i + n > s.size()) {
+                t.decode_err[id] = 1;
+                break;
+            }
+            const auto it = t.symbol_byte.find(s.substr(i, n));
+            if (it == t.symbol_byte.end()) {
+                t.decode_err[id] = 2;
+                break;
+            }
+            bytes.push_back(static_cast<char>(it->second));
+            i += n;
+        }
+        t.decoded[id] = std::move(bytes);
+    }
+    const Pcre2 &api = pcre2();
+    int err = 0;
+    size_t off = 0;
+    t.code = api.compile(reinterpret_cast<const uint8_t *>(kPattern), kPcre2ZeroTerminated, kPcre2Utf | kPcre2Ucp, &err,
+                         &off, nullptr);
+    if (!t.code) throw std::runtime_error("Could not compile tokenizer regex");
+    t.jit = api.jit_compile && api.jit_compile(t.code, kPcre2JitComplete) == 0;
+}
+
+thread_local std::string t_create_err;  // message of the last failed ijb_tokenizer_create in this thread
+
+int fail(ijb_tokenizer *t, const std::exception &e) {
+    t->error = e.what();
+    return IJB_ERR_INVALID;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ijb_tokenizer_create(const char *const *tokens, int n_tokens, const char *const *merges, int n_merges,
+                         ijb_tokenizer **out) {
+    t_create_err.clear();
+    if (!out) {
+        t_create_err = "bad arguments";
+        return IJB_ERR_INVALID;
+    }
+    *out = nullptr;
+    try {
+        if (!tokens || n_tokens < 0 || (n_merges > 0 && !merges) || n_merges < 0)
+            throw std::runtime_error("bad arguments");
+        std::unique_ptr<ijb_tokenizer> t(new ijb_tokenizer());
+        build(*t, tokens, n_tokens, merges, n_merges);
+        *out = t.release();
+        return IJB_OK;
+    } catch (const std::bad_alloc &) {
+        t_create_err = "host allocation failed";
+        return IJB_ERR_NOMEM;
+    } catch (const std::exception &e) {
+        t_create_err = e.what();
+        return IJB_ERR_INVALID;
+    }
+}
+
+void ijb_tokenizer_destroy(ijb_tokenizer *t) { delete t; }
+
+const char *ijb_tokenizer_last_error(const ijb_tokenizer *t) { return t ? t->error.c_str() : t_create_err.c_str(); }
+
+int ijb_tokenizer_encode(ijb_tokenizer *t, const char *text, long len, int *ids, long cap, long *n) {
+    if (!t) return IJB_ERR_INVALID;
+    try {
+        if (!n || len < 0 || (len > 0 && !text) || cap < 0 || (cap > 0 && !ids)) throw std::runtime_error("bad arguments");
+        if (!t->code) throw std::runtime_error("tokenizer was not created");
+        std::vector<int> out;
+        out.reserve(static_cast<size_t>(len) / 3 + 8);
+        t->encode(reinterpret_cast<const uint8_t *>(text), static_cast<size_t>(len), out);
+        *n = static_cast<long>(out.size());
+        std::memcpy(ids, out.data(), std::min(out.size(), static_cast<size_t>(cap)) * sizeof(int));
+        return IJB_OK;
+    } catch (const std::exception &e) {
+        return fail(t, e);
+    }
+}
+
+int ijb_tokenizer_decode(ijb_tokenizer *t, int id, char *bytes, int cap, int *len) {
+    if (!t) return IJB_ERR_INVALID;
+    try {
+        if (!len || cap < 0 || (cap > 0 && !bytes)) throw std::runtime_error("bad arguments");
+        if (id < 0 || id >= static_cast<int>(t->tokens.size())) throw std::runtime_error("Invalid token id");
+        if (t->decode_err[id] == 1) throw std::runtime_error("Malformed token UTF-8");
+        if (t->decode_err[id] == 2) throw std::runtime_error("Cannot decode token");
+        const std::string &s = t->decoded[id];
+        *len = static_cast<int>(s.size());
+        std::memcpy(bytes, s.data(), std::min(s.size(), static_cast<size_t>(cap)));
+        return IJB_OK;
+    } catch (const std::exception &e) {
+        return fail(t, e);
+    }
+}
+
+int ijb_tokenizer_special(ijb_tokenizer *t, const char *name, int *id) {
+    if (!t) return IJB_ERR_INVALID;
+    try {
+        if (!name || !id) throw std::runtime_error("bad arguments");
+        const auto it = t->ids.find(name);
+        if (it == t->ids.end()) throw std::runtime_error(std::string("Missing special token ") + name);
+        *id = it->second;
+        return IJB_OK;
+    } catch (const std::exception &e) {
+        return fail(t, e);
+    }
+}
+
+}  // extern "C"

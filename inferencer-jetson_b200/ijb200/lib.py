@@ -90,6 +90,13 @@ def load():
         "ijb_weight_status": ([P], I),
         "ijb_keys_to_tokens": ([P, I, P, P], I),
         "ijb_kernel_launches": ([], ctypes.c_uint64),
+        "ijb_tokenizer_create": ([ctypes.POINTER(ctypes.c_char_p), I, ctypes.POINTER(ctypes.c_char_p), I,
+                                  ctypes.POINTER(P)], I),
+        "ijb_tokenizer_destroy": ([P], None),
+        "ijb_tokenizer_last_error": ([P], ctypes.c_char_p),
+        "ijb_tokenizer_encode": ([P, ctypes.c_char_p, L64, IP, L64, ctypes.POINTER(L64)], I),
+        "ijb_tokenizer_decode": ([P, I, ctypes.c_char_p, I, IP], I),
+        "ijb_tokenizer_special": ([P, ctypes.c_char_p, IP], I),
         "ijb_last_step_ms": ([P], ctypes.c_float),
     }
     for name, (args, res) in sig.items():

@@ -1,0 +1,78 @@
+"""Python mirror of the reference's Tokenizer (inferencer.cu:361-451) over
+the C ABI's ijb_tokenizer_* entry points (host code; no GPU involved).
+
+    tok = Tokenizer(model_tokens, model_merges)   # tokenizer.ggml.tokens / .merges
+    ids = tok.encode("Hello world")               # Tokenizer::encode
+    tok.decode(ids[0])                            # Tokenizer::decode -> bytes
+    tok.special("<|eot_id|>")                     # Tokenizer::special
+
+Failures raise TokenizerError with the reference's messages ("Expected Llama 3
+tokenizer", "Invalid token id", "Missing special token ...", ...).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import lib as _L
+
+
+class TokenizerError(RuntimeError):
+    pass
+
+
+class Tokenizer:
+    def __init__(self, tokens, merges):
+        self.lib = _L.load()
+        toks = [t.encode() if isinstance(t, str) else bytes(t) for t in tokens]
+        mrgs = [m.encode() if isinstance(m, str) else bytes(m) for m in merges]
+        ta = (ctypes.c_char_p * max(1, len(toks)))(*toks)
+        ma = (ctypes.c_char_p * max(1, len(mrgs)))(*mrgs)
+        h = ctypes.c_void_p()
+        rc = self.lib.ijb_tokenizer_create(ta, len(toks), ma, len(mrgs), ctypes.byref(h))
+        if rc != _L.OK:
+            raise TokenizerError(self.lib.ijb_tokenizer_last_error(None).decode())
+        self.h = h
+
+    def _check(self, rc: int) -> None:
+        if rc != _L.OK:
+            raise TokenizerError(self.lib.ijb_tokenizer_last_error(self.h).decode())
+
+    def encode(self, text) -> list[int]:
+        data = text.encode() if isinstance(text, str) else bytes(text)
+        cap = len(data) + 16
+        n = ctypes.c_long()
+        while True:
+            buf = np.empty(cap, np.int32)
+            self._check(self.lib.ijb_tokenizer_encode(self.h, data, len(data),
+                                                      buf.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), cap,
+                                                      ctypes.byref(n)))
+            if n.value <= cap:
+                return buf[:n.value].tolist()
+            cap = n.value
+
+    def decode(self, token_id: int) -> bytes:
+        buf = ctypes.create_string_buffer(256)
+        n = ctypes.c_int()
+        self._check(self.lib.ijb_tokenizer_decode(self.h, int(token_id), buf, 256, ctypes.byref(n)))
+        if n.value > 256:
+            buf = ctypes.create_string_buffer(n.value)
+            self._check(self.lib.ijb_tokenizer_decode(self.h, int(token_id), buf, n.value, ctypes.byref(n)))
+        return buf.raw[:n.value]
+
+    def special(self, name: str) -> int:
+        v = ctypes.c_int()
+        self._check(self.lib.ijb_tokenizer_special(self.h, name.encode(), ctypes.byref(v)))
+        return v.value
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.ijb_tokenizer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

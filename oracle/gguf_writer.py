@@ -90,3 +90,20 @@ def write_gguf(path: str, cfg, weights: dict) -> int:
             f.write(data)
             f.write(b"\0" * ((-len(data)) % ALIGN))
     return offset
+
+
+def _str_array(key: str, values) -> bytes:
+    """A GGUF array of strings (type 9 of element type 8), as the reader's
+    tokenizer keys expect (inferencer.cu:227-232)."""
+    return _str(key) + struct.pack("<IIQ", 9, 8, len(values)) + b"".join(_str(v) for v in values)
+
+
+def write_vocab_gguf(path: str, tokens, merges) -> None:
+    """A GGUF v3 file holding only tokenizer.ggml.tokens and
+    tokenizer.ggml.merges (no tensors), for the reference's Tokenizer; 32 bytes
+    of padding follow the header, since the reader wants data after it."""
+    head = b"GGUF" + struct.pack("<IQQ", 3, 0, 2)
+    head += _str_array("tokenizer.ggml.tokens", tokens) + _str_array("tokenizer.ggml.merges", merges)
+    with open(path, "wb") as f:
+        f.write(head + b"\0" * ((-len(head)) % ALIGN) + b"\0" * ALIGN)
+

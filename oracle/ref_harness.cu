@@ -6,7 +6,9 @@
 // exposes a few extern "C" entry points that run the reference's stock kernels
 // and runner classes on caller data.  It is built into oracle/_ref/ (never
 // committed) and used only to capture golden outputs of the reference on a
-// B200 (tests/golden/make_ref_golden.py) and to time the reference's kernels.
+// B200 (tests/golden/make_ref_golden.py), to time the reference's kernels, and
+// to run the reference's tokenizer on the host for the tokenizer goldens
+// (tests/golden/make_tokenizer_golden.py).
 #include "inferencer.cu"
 
 namespace {
@@ -212,6 +214,60 @@ int ref_time_decode(const char *path, int context, const int *prompt, int n_prom
         auto t0 = Clock::now();
         for (int i = 0; i < steps; ++i) next = runner.forward(next, n_prompt + i, true);
         *decode_seconds = seconds(t0, Clock::now());
+        return 0;
+    } catch (const std::exception &e) { return fail(e); }
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- tokenizer --
+// The reference's Tokenizer (inferencer.cu:361-451) on the tokenizer arrays of
+// a GGUF file (host only; no GPU involved).  The GGUF and Tokenizer of the
+// last path are kept between calls.
+namespace {
+struct RefTok {
+    std::string path;
+    std::unique_ptr<GGUF> model;
+    std::unique_ptr<Tokenizer> tok;
+};
+RefTok &ref_tok(const char *path) {
+    static RefTok t;
+    if (!t.tok || t.path != path) {
+        t.tok.reset();
+        t.model.reset(new GGUF(path));
+        t.tok.reset(new Tokenizer(*t.model));
+        t.path = path;
+    }
+    return t;
+}
+}  // namespace
+
+extern "C" {
+
+// Tokenizer::encode of len bytes; writes min(cap, *n) ids and the count to *n.
+int ref_tokenize(const char *gguf_path, const char *text, long len, int *ids, long cap, long *n) {
+    try {
+        const std::vector<int> out = ref_tok(gguf_path).tok->encode(std::string(text, static_cast<size_t>(len)));
+        *n = static_cast<long>(out.size());
+        for (long i = 0; i < *n && i < cap; ++i) ids[i] = out[i];
+        return 0;
+    } catch (const std::exception &e) { return fail(e); }
+}
+
+// Tokenizer::decode of one id; writes min(cap, *len) bytes and the length to *len.
+int ref_detokenize(const char *gguf_path, int id, char *bytes, int cap, int *len) {
+    try {
+        const std::string s = ref_tok(gguf_path).tok->decode(id);
+        *len = static_cast<int>(s.size());
+        for (int i = 0; i < *len && i < cap; ++i) bytes[i] = s[i];
+        return 0;
+    } catch (const std::exception &e) { return fail(e); }
+}
+
+// Tokenizer::special.
+int ref_special_token(const char *gguf_path, const char *name, int *id) {
+    try {
+        *id = ref_tok(gguf_path).tok->special(name);
         return 0;
     } catch (const std::exception &e) { return fail(e); }
 }

@@ -1,0 +1,155 @@
+"""The host tokenizer (ijb_tokenizer_*, the reference's Tokenizer,
+inferencer.cu:361-451) against the reference itself and the oracle.
+
+The fixture holds the reference's own outputs (its unmodified Tokenizer run on
+the host, tests/golden/make_tokenizer_golden.py) over a synthetic 128256-token
+vocabulary: 80 texts (seeded mixed text, edge cases, long runs that take the
+heap merge, and text that is not valid UTF-8), decodes of 333 ids (error
+messages included) and the special-token lookups.  The oracle
+(oracle/bpe.py) is pinned to the same fixture, then checks the product on
+more seeded text (ijb200.synth_vocab).  No GPU involved."""
+import json
+import random
+import threading
+
+import numpy as np
+import pytest
+
+import bpe
+from ijb200 import synth_vocab as sv
+from ijb200.tokenizer import Tokenizer, TokenizerError
+
+
+@pytest.fixture(scope="module")
+def gold():
+    g = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden",
+                                           "tokenizer_golden.npz"))
+    pairs = [tuple(p) for p in json.loads(str(g["pairs"]))]
+    tokens, merges = sv.synthetic_vocab(pairs)
+    tb, to = g["text_bytes"].tobytes(), g["text_off"]
+    ids, io = g["ids"], g["ids_off"]
+    texts = [tb[to[i]:to[i + 1]] for i in range(len(to) - 1)]
+    want = [ids[io[i]:io[i + 1]].tolist() for i in range(len(to) - 1)]
+    dec = [(int(i), bytes.fromhex(h), e) for i, (h, e) in zip(g["dec_ids"], json.loads(str(g["dec_bytes"])))]
+    return {"tokens": tokens, "merges": merges, "texts": texts, "ids": want, "dec": dec,
+            "specials": json.loads(str(g["specials"]))}
+
+
+@pytest.fixture(scope="module")
+def tok(gold):
+    t = Tokenizer(gold["tokens"], gold["merges"])
+    yield t
+    t.close()
+
+
+@pytest.fixture(scope="module")
+def ref(gold):
+    return bpe.Tokenizer(gold["tokens"], gold["merges"])
+
+
+def test_oracle_matches_reference_outputs(gold, ref):
+    for text, want in zip(gold["texts"], gold["ids"]):
+        assert ref.encode(text) == want, text[:80]
+    for i, b, e in gold["dec"]:
+        if e:
+            with pytest.raises(RuntimeError, match=e):
+                ref.decode(i)
+        else:
+            assert ref.decode(i) == b
+
+
+def test_encode_matches_reference(gold, tok):
+    for text, want in zip(gold["texts"], gold["ids"]):
+        assert tok.encode(text) == want, text[:80]
+
+
+def test_decode_and_special_match_reference(gold, tok):
+    for i, b, e in gold["dec"]:
+        if e:
+            with pytest.raises(TokenizerError, match=e):
+                tok.decode(i)
+        else:
+            assert tok.decode(i) == b
+    for name, v in gold["specials"].items():
+        if isinstance(v, str):
+            with pytest.raises(TokenizerError, match=v):
+                tok.special(name)
+        else:
+            assert tok.special(name) == v
+
+
+def test_encode_matches_oracle_on_more_text(tok, ref):
+    rng = random.Random(2024)
+    for n in (1, 3, 10, 40, 150, 600):
+        for _ in range(6):
+            text = sv.random_text(rng, n).encode()
+            assert tok.encode(text) == ref.encode(text), text[:80]
+    # long pieces of one character class (the heap merge) and long mixed runs
+    for text in (b"=" * 333, b" " * 257 + b"z", b"ab" * 150, b"abcdefghij" * 30, "ー".encode() * 90,
+                 b"x" + b"\n" * 70, bytes(range(32, 127)) * 3):
+        assert tok.encode(text) == ref.encode(text), text[:40]
+
+
+def test_round_trip_and_chat_layout(tok, ref):
+    rng = random.Random(5)
+    for _ in range(20):
+        text = sv.random_text(rng, 50).encode()
+        assert b"".join(tok.decode(i) for i in tok.encode(text)) == text
+    # the reference's chat prompt (inferencer.cu:1534-1551) built from these calls
+    prompt = [tok.special("<|begin_of_text|>"), tok.special("<|start_header_id|>")] + tok.encode("user") + \
+        [tok.special("<|end_header_id|>")] + tok.encode("\n\nHello there") + [tok.special("<|eot_id|>")]
+    assert prompt[:2] == [128000, 128006] and prompt[-1] == 128009
+    assert tok.encode("\n\nHello there") == ref.encode(b"\n\nHello there")
+
+
+def test_vocabulary_with_merges_that_make_no_token(gold):
+    """A merge whose result is not a token: the reference keeps merging the
+    string (and fails only if such a part survives); the product then uses its
+    string path and gives the same ids or the same error."""
+    tokens = list(gold["tokens"])
+    merges = ["h e", "l l", "he ll", "hell o"] + list(gold["merges"])
+    i_hell = tokens.index("hell") if "hell" in tokens else None
+    if i_hell is not None:
+        tokens[i_hell] = "<|no_hell|>"  # "he ll" now makes a string that is no token
+    t = Tokenizer(tokens, merges)
+    r = bpe.Tokenizer(tokens, merges)
+    for text in (b"hello", b"hell", b"shell fish", b"hello hello world"):
+        try:
+            want = r.encode(text)
+        except RuntimeError as e:
+            with pytest.raises(TokenizerError, match=str(e)):
+                t.encode(text)
+        else:
+            assert t.encode(text) == want
+    t.close()
+
+
+def test_errors_follow_the_reference(gold):
+    with pytest.raises(TokenizerError, match="Expected Llama 3 tokenizer"):
+        Tokenizer(gold["tokens"][:1000], gold["merges"])
+    t = Tokenizer(gold["tokens"], gold["merges"])
+    for bad in (-1, len(gold["tokens"])):
+        with pytest.raises(TokenizerError, match="Invalid token id"):
+            t.decode(bad)
+    with pytest.raises(TokenizerError, match="Missing special token <|none|>"):
+        t.special("<|none|>")
+    assert t.encode(b"") == []
+    t.close()
+
+
+def test_concurrent_encodes_agree(tok, ref):
+    rng = random.Random(9)
+    texts = [sv.random_text(rng, 80).encode() for _ in range(16)]
+    want = [ref.encode(x) for x in texts]
+    got = [None] * len(texts)
+
+    def run(k):
+        for _ in range(5):
+            got[k] = tok.encode(texts[k])
+
+    threads = [threading.Thread(target=run, args=(k,)) for k in range(len(texts))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert got == want
