@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload ragged64|decode1|ragged256_3b|gemv_q4k|gemv_q6k|gemm_q6k_b64|gemm_layer|
-                                tp_lm_head]
+                                tp_lm_head|tokenize]
 
 Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
   ragged64  (default) Llama-3.2-1B-architecture Q4_K_M, 64 concurrent
@@ -29,6 +29,10 @@ Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
             an NCCL all-gather of the logits (the line's value) or one
             all-reduce of the packed argmax keys (`keys_only`); total work is
             fixed (strong scaling), checked against one GPU's full lm_head.
+  tokenize  host tokenizer throughput (no GPU): ijb_tokenizer_encode over a
+            seeded ~1 MB text corpus on one core, a fresh tokenizer (empty
+            piece cache) per step, against the reference's own Tokenizer
+            (oracle/_ref, same vocabulary) on the same corpus.
 `value` is whole-job decode tokens/s: tokens generated in the K timed steps
 on all ranks / max over ranks of the device time of those steps (CUDA events
 around each step's graph).  Replacement prefills run between timed steps and
@@ -48,6 +52,7 @@ import argparse
 import ctypes
 import json
 import os
+import random
 import re
 import subprocess
 import sys
@@ -80,7 +85,8 @@ def parse(argv=None):
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["ragged64", "decode1", "ragged256_3b", "gemv_q4k", "gemv_q6k",
-                                           "gemm_q6k_b64", "gemm_layer", "tp_lm_head"], default="ragged64")
+                                           "gemm_q6k_b64", "gemm_layer", "tp_lm_head", "tokenize"],
+                    default="ragged64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="ragged64: skip the decode1 record, kernel timings and reference CUDA timings")
@@ -855,8 +861,89 @@ def run_tp_lm_head(args):
             "check": check}
 
 
+TOKENIZE_ITEMS = 240_000  # random_text items of the corpus (~1.1 MB)
+
+
+def tokenize_setup():
+    """The synthetic vocabulary and the seeded corpus of the tokenize workload."""
+    from ijb200 import synth_vocab as sv
+    tokens, merges = sv.vocabulary()
+    rng = random.Random(31)
+    corpus = [sv.random_text(rng, 400).encode() for _ in range(TOKENIZE_ITEMS // 400)]
+    return tokens, merges, corpus
+
+
+def reference_tokenize(tokens, merges, corpus, budget_s=15.0):
+    """The reference's Tokenizer (inferencer.cu:361-451, oracle/_ref) over the
+    corpus's texts in order until budget_s: (tokens/s, bytes/s, sample)."""
+    if not os.path.exists(REF_HARNESS):
+        return None
+    import tempfile
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    from gguf_writer import write_vocab_gguf
+    lib = ctypes.CDLL(REF_HARNESS)
+    lib.ref_last_error.restype = ctypes.c_char_p
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "vocab.gguf").encode()
+        write_vocab_gguf(path.decode(), tokens, merges)
+        n = ctypes.c_long()
+        buf = (ctypes.c_int * 1)()
+        lib.ref_tokenize(path, b"warm", 4, buf, 0, ctypes.byref(n))  # builds the GGUF and Tokenizer
+        toks = nbytes = done = 0
+        t0 = time.perf_counter()
+        for text in corpus:
+            if lib.ref_tokenize(path, text, len(text), buf, 0, ctypes.byref(n)):
+                raise RuntimeError(lib.ref_last_error().decode())
+            toks += n.value
+            nbytes += len(text)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = time.perf_counter() - t0
+    return toks / dt, nbytes / dt, f"{done} of {len(corpus)} corpus texts ({nbytes} bytes) in {dt:.1f} s"
+
+
+def run_tokenize(args):
+    """Host tokenizer throughput; `value` is encode tokens/s on one core."""
+    from ijb200.tokenizer import Tokenizer
+    tokens, merges, corpus = tokenize_setup()
+    nbytes = sum(map(len, corpus))
+    ref = reference_tokenize(tokens, merges, corpus)
+    ref_rec = ({"value": ref[0], "unit": "tokens/s", "bytes_per_s": ref[1], "cores": 1, "kind": "reference",
+                "sample": ref[2]} if ref else
+               {"unavailable": "oracle/_ref/libref_harness.so not built (the reference tree was absent at build)"})
+    if args.impl == "reference":
+        if not ref:
+            return {"impl": "reference", **ref_rec}
+        return {"impl": "reference", "metric": "tokenizer encode tokens/s (host, 1 core)", "value": ref[0],
+                "unit": "tokens/s", "higher_is_better": True, "cpu_baseline": ref_rec,
+                "e2e": {"value": ref[0], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "config": {"workload": "tokenize"}}
+    times = []
+    count = 0
+    for k in range(args.warmup + args.steps):
+        tok = Tokenizer(tokens, merges)  # empty piece cache every step
+        t0 = time.perf_counter()
+        count = sum(len(tok.encode(text)) for text in corpus)
+        dt = time.perf_counter() - t0
+        tok.close()
+        if k >= args.warmup:
+            times.append(dt)
+    dt = float(np.median(times))
+    return {"metric": "tokenizer encode tokens/s (host, 1 core)", "value": count / dt, "unit": "tokens/s",
+            "higher_is_better": True, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "bytes_per_s": nbytes / dt, "tokens_per_step": count, "n_gpus": 0, "gpu_launches": 0,
+            "data": "synthetic (seeded text; 128256-token vocabulary around 700 trained merges)",
+            "config": {"workload": "tokenize", "corpus_bytes": nbytes, "texts": len(corpus),
+                       "method": "one pass of ijb_tokenizer_encode over the corpus per step, a fresh tokenizer "
+                                 "(empty piece cache) each step, median step"},
+            "reference": ref_rec}
+
+
 def run_ours(args):
     import torch
+    if args.workload == "tokenize":
+        return run_tokenize(args)
     if args.workload == "tp_lm_head":
         return run_tp_lm_head(args)
     if args.workload.startswith("gemv"):
@@ -1048,6 +1135,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
+    if args.workload == "tokenize":
+        return run_tokenize(args)
     import oracle as O
     big = args.workload == "ragged256_3b"
     cfg = synth.LLAMA_3B if big else synth.LLAMA_1B

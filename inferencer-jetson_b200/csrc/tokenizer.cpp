@@ -411,7 +411,7 @@ int ijb_tokenizer_create(const char *const *tokens, int n_tokens, const char *co
     }
     *out = nullptr;
     try {
-        if (!tokens || n_tokens < 0 || (n_merges > 0 && !merges) || n_merges < 0)
+        if ((n_tokens > 0 && !tokens) || n_tokens < 0 || (n_merges > 0 && !merges) || n_merges < 0)
             throw std::runtime_error("bad arguments");
         std::unique_ptr<ijb_tokenizer> t(new ijb_tokenizer());
         build(*t, tokens, n_tokens, merges, n_merges);

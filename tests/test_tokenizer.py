@@ -153,3 +153,76 @@ def test_concurrent_encodes_agree(tok, ref):
     for th in threads:
         th.join()
     assert got == want
+
+
+_SHIM_MAIN = r"""
+#include "tokenizer.hpp"
+#include <cstdio>
+#include <fstream>
+#include <iostream>
+// the reference's GGUF members the tokenizer reads (inferencer.cu:207)
+struct Model { std::vector<std::string> tokens, merges; };
+static std::string unhex(const std::string &h) {
+    std::string s;
+    for (size_t i = 0; i + 1 < h.size(); i += 2) s.push_back(static_cast<char>(std::stoi(h.substr(i, 2), nullptr, 16)));
+    return s;
+}
+int main(int argc, char **argv) {
+    Model model;
+    std::ifstream v(argv[1]);
+    std::string line;
+    bool merges = false;
+    while (std::getline(v, line)) {
+        if (line == "\x01---") { merges = true; continue; }
+        (merges ? model.merges : model.tokens).push_back(unhex(line));
+    }
+    using ijb_host::Tokenizer;
+    Tokenizer tok(model);
+    std::ifstream t(argv[2]);
+    while (std::getline(t, line)) {
+        for (int id : tok.encode(unhex(line))) std::cout << id << ' ';
+        std::cout << '\n';
+    }
+    std::cout << tok.special("<|eot_id|>") << ' ' << tok.decode(300).size() << '\n';
+    try { tok.decode(-1); } catch (const std::runtime_error &e) { std::cout << e.what() << '\n'; }
+    Model empty;
+    try { Tokenizer bad(empty); } catch (const std::runtime_error &e) { std::cout << e.what() << '\n'; }
+    return 0;
+}
+"""
+
+
+def test_cpp_shim_matches_reference(gold, tmp_path):
+    """The reference's call pattern through host/tokenizer.hpp (Tokenizer from
+    a GGUF-like model; encode, special, decode; exceptions), compiled with g++
+    and linked to libijb200.so, on the golden texts."""
+    import os
+    import shutil
+    import subprocess
+    from ijb200 import lib
+    gxx = shutil.which("g++")
+    if not gxx:
+        pytest.skip("no g++")
+    src = tmp_path / "main.cpp"
+    src.write_text(_SHIM_MAIN)
+    exe = tmp_path / "shim"
+    libdir = os.path.join(lib.PKG_ROOT, "lib")
+    r = subprocess.run([gxx, "-std=c++17", "-O1", "-I", os.path.join(lib.PKG_ROOT, "host"), str(src), "-L", libdir,
+                        "-lijb200", f"-Wl,-rpath,{libdir}", "-Wl,--unresolved-symbols=ignore-in-shared-libs",
+                        "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    vocab = tmp_path / "vocab.txt"
+    vocab.write_text("\n".join(x.encode().hex() for x in gold["tokens"]) + "\n\x01---\n" +
+                     "\n".join(x.encode().hex() for x in gold["merges"]) + "\n")
+    texts = tmp_path / "texts.txt"
+    texts.write_text("".join(t.hex() + "\n" for t in gold["texts"]))
+    out = subprocess.run([str(exe), str(vocab), str(texts)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    lines = out.stdout.split("\n")
+    for k, want in enumerate(gold["ids"]):
+        assert [int(v) for v in lines[k].split()] == want, k
+    n = len(gold["ids"])
+    eot, n300 = lines[n].split()
+    assert int(eot) == 128009 and int(n300) == len(bpe.Tokenizer(gold["tokens"], gold["merges"]).decode(300))
+    assert lines[n + 1] == "Invalid token id"
+    assert lines[n + 2] == "Expected Llama 3 tokenizer"
