@@ -326,6 +326,11 @@ int ijb_tokenizer_encode(ijb_tokenizer *tokenizer, const char *text, long len, i
 int ijb_tokenizer_decode(ijb_tokenizer *tokenizer, int id, char *bytes, int cap, int *len);
 /* Id of a token by its exact string, e.g. "<|eot_id|>" (Tokenizer::special, :446-450). */
 int ijb_tokenizer_special(ijb_tokenizer *tokenizer, const char *name, int *id);
+/* The chat layout of one user turn (chat_prompt, inferencer.cu:1534-1551):
+ * <|begin_of_text|> <|start_header_id|> "user" <|end_header_id|> "\n\n" + prompt
+ * <|eot_id|> <|start_header_id|> "assistant" <|end_header_id|> "\n\n"; ids and
+ * *n as in ijb_tokenizer_encode. */
+int ijb_tokenizer_chat_prompt(ijb_tokenizer *tokenizer, const char *prompt, long len, int *ids, long cap, long *n);
 
 #ifdef __cplusplus
 }

@@ -475,4 +475,38 @@ int ijb_tokenizer_special(ijb_tokenizer *t, const char *name, int *id) {
     }
 }
 
+// chat_prompt (inferencer.cu:1534-1551): the Llama 3 chat layout of one user
+// turn followed by the assistant header.
+int ijb_tokenizer_chat_prompt(ijb_tokenizer *t, const char *prompt, long len, int *ids, long cap, long *n) {
+    if (!t) return IJB_ERR_INVALID;
+    try {
+        if (!n || len < 0 || (len > 0 && !prompt) || cap < 0 || (cap > 0 && !ids)) throw std::runtime_error("bad arguments");
+        if (!t->code) throw std::runtime_error("tokenizer was not created");
+        auto special = [&](const char *name) {
+            const auto it = t->ids.find(name);
+            if (it == t->ids.end()) throw std::runtime_error(std::string("Missing special token ") + name);
+            return it->second;
+        };
+        auto append = [&](const std::string &text, std::vector<int> &out) {
+            t->encode(reinterpret_cast<const uint8_t *>(text.data()), text.size(), out);
+        };
+        std::vector<int> out;
+        out.push_back(special("<|begin_of_text|>"));
+        out.push_back(special("<|start_header_id|>"));
+        append("user", out);
+        out.push_back(special("<|end_header_id|>"));
+        append("\n\n" + std::string(prompt ? prompt : "", static_cast<size_t>(len)), out);
+        out.push_back(special("<|eot_id|>"));
+        out.push_back(special("<|start_header_id|>"));
+        append("assistant", out);
+        out.push_back(special("<|end_header_id|>"));
+        append("\n\n", out);
+        *n = static_cast<long>(out.size());
+        std::memcpy(ids, out.data(), std::min(out.size(), static_cast<size_t>(cap)) * sizeof(int));
+        return IJB_OK;
+    } catch (const std::exception &e) {
+        return fail(t, e);
+    }
+}
+
 }  // extern "C"

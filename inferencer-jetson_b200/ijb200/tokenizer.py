@@ -39,18 +39,24 @@ class Tokenizer:
         if rc != _L.OK:
             raise TokenizerError(self.lib.ijb_tokenizer_last_error(self.h).decode())
 
-    def encode(self, text) -> list[int]:
+    def _ids(self, fn, text) -> list[int]:
         data = text.encode() if isinstance(text, str) else bytes(text)
-        cap = len(data) + 16
+        cap = len(data) + 32
         n = ctypes.c_long()
         while True:
             buf = np.empty(cap, np.int32)
-            self._check(self.lib.ijb_tokenizer_encode(self.h, data, len(data),
-                                                      buf.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), cap,
-                                                      ctypes.byref(n)))
+            self._check(fn(self.h, data, len(data), buf.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), cap,
+                           ctypes.byref(n)))
             if n.value <= cap:
                 return buf[:n.value].tolist()
             cap = n.value
+
+    def encode(self, text) -> list[int]:
+        return self._ids(self.lib.ijb_tokenizer_encode, text)
+
+    def chat_prompt(self, prompt) -> list[int]:
+        """The reference's chat_prompt (inferencer.cu:1534-1551)."""
+        return self._ids(self.lib.ijb_tokenizer_chat_prompt, prompt)
 
     def decode(self, token_id: int) -> bytes:
         buf = ctypes.create_string_buffer(256)

@@ -264,6 +264,16 @@ int ref_detokenize(const char *gguf_path, int id, char *bytes, int cap, int *len
     } catch (const std::exception &e) { return fail(e); }
 }
 
+// chat_prompt (inferencer.cu:1534-1551) of len bytes of prompt.
+int ref_chat_prompt(const char *gguf_path, const char *prompt, long len, int *ids, long cap, long *n) {
+    try {
+        const std::vector<int> out = chat_prompt(*ref_tok(gguf_path).tok, std::string(prompt, static_cast<size_t>(len)));
+        *n = static_cast<long>(out.size());
+        for (long i = 0; i < *n && i < cap; ++i) ids[i] = out[i];
+        return 0;
+    } catch (const std::exception &e) { return fail(e); }
+}
+
 // Tokenizer::special.
 int ref_special_token(const char *gguf_path, const char *name, int *id) {
     try {

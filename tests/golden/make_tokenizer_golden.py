@@ -80,6 +80,18 @@ def main():
         dec_ids = list(range(0, 300)) + list(range(256, 256 + len(pairs), 7)) + list(range(127990, 128020)) + \
             [128255, -1, 128256]
         decoded = [dec(i) for i in dec_ids]
+        chat_prompts = [b"", b"Hello", b"What is 2+2?\nAnswer briefly.", "Résumé: 東京 😀".encode(),
+                        sv.random_text(random.Random(3), 150).encode()]
+
+        def chat(t: bytes):
+            cap = 4 * len(t) + 64
+            buf = (ctypes.c_int * cap)()
+            n = ctypes.c_long()
+            if lib.ref_chat_prompt(path, t, ctypes.c_long(len(t)), buf, ctypes.c_long(cap), ctypes.byref(n)):
+                raise RuntimeError(lib.ref_last_error().decode())
+            return list(buf[:n.value])
+
+        chats = [chat(t) for t in chat_prompts]
         specials = {}
         for name in sv.SPECIALS + ["<|nope|>"]:
             v = ctypes.c_int(-1)
@@ -96,6 +108,7 @@ def main():
         dec_ids=np.array(dec_ids, np.int32),
         dec_bytes=np.array(json.dumps([[b.hex(), e] for b, e in decoded])),
         specials=np.array(json.dumps(specials)),
+        chat=np.array(json.dumps([[t.hex(), c] for t, c in zip(chat_prompts, chats)])),
     )
     print("wrote", out, os.path.getsize(out), "bytes")
 

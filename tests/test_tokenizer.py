@@ -32,7 +32,8 @@ def gold():
     want = [ids[io[i]:io[i + 1]].tolist() for i in range(len(to) - 1)]
     dec = [(int(i), bytes.fromhex(h), e) for i, (h, e) in zip(g["dec_ids"], json.loads(str(g["dec_bytes"])))]
     return {"tokens": tokens, "merges": merges, "texts": texts, "ids": want, "dec": dec,
-            "specials": json.loads(str(g["specials"]))}
+            "specials": json.loads(str(g["specials"])),
+            "chat": [(bytes.fromhex(h), c) for h, c in json.loads(str(g["chat"]))]}
 
 
 @pytest.fixture(scope="module")
@@ -100,6 +101,12 @@ def test_round_trip_and_chat_layout(tok, ref):
         [tok.special("<|end_header_id|>")] + tok.encode("\n\nHello there") + [tok.special("<|eot_id|>")]
     assert prompt[:2] == [128000, 128006] and prompt[-1] == 128009
     assert tok.encode("\n\nHello there") == ref.encode(b"\n\nHello there")
+
+
+def test_chat_prompt_matches_reference(gold, tok):
+    """chat_prompt (inferencer.cu:1534-1551) as the reference builds it."""
+    for prompt, want in gold["chat"]:
+        assert tok.chat_prompt(prompt) == want
 
 
 def test_vocabulary_with_merges_that_make_no_token(gold):
