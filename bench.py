@@ -930,6 +930,17 @@ def run_tokenize(args):
         if k >= args.warmup:
             times.append(dt)
     dt = float(np.median(times))
+    # the same corpus through the batch entry point on every host core
+    cores = os.cpu_count() or 1
+    mt = []
+    for k in range(args.warmup + args.steps):
+        tok = Tokenizer(tokens, merges)
+        t0 = time.perf_counter()
+        n_mt = sum(map(len, tok.encode_batch(corpus, cores)))
+        mt.append(time.perf_counter() - t0)
+        tok.close()
+    dt_mt = float(np.median(mt[args.warmup:]))
+    assert n_mt == count
     return {"metric": "tokenizer encode tokens/s (host, 1 core)", "value": count / dt, "unit": "tokens/s",
             "higher_is_better": True, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "bytes_per_s": nbytes / dt, "tokens_per_step": count, "n_gpus": 0, "gpu_launches": 0,
@@ -937,6 +948,9 @@ def run_tokenize(args):
             "config": {"workload": "tokenize", "corpus_bytes": nbytes, "texts": len(corpus),
                        "method": "one pass of ijb_tokenizer_encode over the corpus per step, a fresh tokenizer "
                                  "(empty piece cache) each step, median step"},
+            "batch_all_cores": {"value": count / dt_mt, "unit": "tokens/s", "cores": cores,
+                                "method": "ijb_tokenizer_encode_batch over the corpus's texts, one fresh tokenizer "
+                                          "per step, a piece cache per worker thread, median step"},
             "reference": ref_rec}
 
 

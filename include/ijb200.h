@@ -321,6 +321,13 @@ const char *ijb_tokenizer_last_error(const ijb_tokenizer *tokenizer);
  * first min(cap, *n) ids to ids and the full count to *n (call again with a
  * larger buffer when *n > cap). */
 int ijb_tokenizer_encode(ijb_tokenizer *tokenizer, const char *text, long len, int *ids, long cap, long *n);
+/* ijb_tokenizer_encode of n_texts texts on `threads` host threads (0: all the
+ * hardware has): the ids of text i go to ids[offsets[i] .. offsets[i + 1]),
+ * offsets having n_texts + 1 entries.  When the ids exceed cap, offsets is
+ * still filled (offsets[n_texts] = the count needed) and the call returns
+ * IJB_ERR_CAPACITY without writing ids. */
+int ijb_tokenizer_encode_batch(ijb_tokenizer *tokenizer, const char *const *texts, const long *lens, int n_texts,
+                               int *ids, long cap, long *offsets, int threads);
 /* The bytes token id stands for (Tokenizer::decode, :432-445): writes the
  * first min(cap, *len) bytes and the full length to *len. */
 int ijb_tokenizer_decode(ijb_tokenizer *tokenizer, int id, char *bytes, int cap, int *len);

@@ -20,6 +20,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <limits>
@@ -28,6 +29,7 @@
 #include <queue>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <utility>
 #include <vector>
@@ -258,7 +260,10 @@ struct ijb_tokenizer {
         }
     }
 
-    void piece(const uint8_t *p, size_t n, std::vector<int> &out) const {
+    // local: a piece cache owned by the calling thread (batch workers), else
+    // the tokenizer's shared cache under its lock
+    using Cache = std::unordered_map<std::string, std::vector<int>>;
+    void piece(const uint8_t *p, size_t n, std::vector<int> &out, Cache *local) const {
         if (n == 0) return;
         if (!regular) {
             merge_strings(p, n, out);
@@ -270,26 +275,27 @@ struct ijb_tokenizer {
         }
         if (n <= kCacheMaxPiece) {
             const std::string key(reinterpret_cast<const char *>(p), n);
-            {
-                std::lock_guard<std::mutex> lock(cache_mu);
-                const auto it = cache.find(key);
-                if (it != cache.end()) {
-                    out.insert(out.end(), it->second.begin(), it->second.end());
-                    return;
-                }
+            Cache &c = local ? *local : cache;
+            std::unique_lock<std::mutex> lock(cache_mu, std::defer_lock);
+            if (!local) lock.lock();
+            const auto it = c.find(key);
+            if (it != c.end()) {
+                out.insert(out.end(), it->second.begin(), it->second.end());
+                return;
             }
+            if (!local) lock.unlock();
             const size_t first = out.size();
             merge_ids(p, n, out);
-            std::lock_guard<std::mutex> lock(cache_mu);
-            if (cache.size() >= kCacheMaxEntries) cache.clear();
-            cache.emplace(key, std::vector<int>(out.begin() + static_cast<long>(first), out.end()));
+            if (!local) lock.lock();
+            if (c.size() >= kCacheMaxEntries) c.clear();
+            c.emplace(key, std::vector<int>(out.begin() + static_cast<long>(first), out.end()));
             return;
         }
         merge_ids(p, n, out);
     }
 
     // ----------------------------------------------------- pre-tokenizer --
-    void encode(const uint8_t *text, size_t n, std::vector<int> &out) const {
+    void encode(const uint8_t *text, size_t n, std::vector<int> &out, Cache *local = nullptr) const {
         const Pcre2 &api = pcre2();
         // a valid text needs no UTF check per match; an invalid one is matched
         // exactly as the reference matches it (the failing call ends the loop)
@@ -300,13 +306,13 @@ struct ijb_tokenizer {
         while (pos < n) {
             const int status = api.match(code, text, n, pos, opts, md.get(), nullptr);
             if (status < 0) {
-                piece(text + pos, n - pos, out);
+                piece(text + pos, n - pos, out, local);
                 break;
             }
             const size_t *span = api.ovector(md.get());
-            if (span[0] > pos) piece(text + pos, span[0] - pos, out);
+            if (span[0] > pos) piece(text + pos, span[0] - pos, out, local);
             if (span[1] == span[0]) throw std::runtime_error("Tokenizer regex made no progress");
-            piece(text + span[0], span[1] - span[0], out);
+            piece(text + span[0], span[1] - span[0], out, local);
             pos = span[1];
         }
     }
@@ -470,6 +476,62 @@ int ijb_tokenizer_special(ijb_tokenizer *t, const char *name, int *id) {
         if (it == t->ids.end()) throw std::runtime_error(std::string("Missing special token ") + name);
         *id = it->second;
         return IJB_OK;
+    } catch (const std::exception &e) {
+        return fail(t, e);
+    }
+}
+
+// Many texts at once on `threads` host threads (0: the hardware's), texts
+// taken in turn from a shared counter, each worker with its own piece cache.
+int ijb_tokenizer_encode_batch(ijb_tokenizer *t, const char *const *texts, const long *lens, int n_texts, int *ids,
+                               long cap, long *offsets, int threads) {
+    if (!t) return IJB_ERR_INVALID;
+    try {
+        if (n_texts < 0 || (n_texts > 0 && (!texts || !lens)) || !offsets || cap < 0 || (cap > 0 && !ids) ||
+            threads < 0)
+            throw std::runtime_error("bad arguments");
+        if (!t->code) throw std::runtime_error("tokenizer was not created");
+        for (int i = 0; i < n_texts; ++i)
+            if (lens[i] < 0 || (lens[i] > 0 && !texts[i])) throw std::runtime_error("bad arguments");
+        std::vector<std::vector<int>> out(static_cast<size_t>(n_texts));
+        int nt = threads ? threads : static_cast<int>(std::thread::hardware_concurrency());
+        nt = std::max(1, std::min(nt, n_texts));
+        std::atomic<int> next{0};
+        std::mutex err_mu;
+        std::string err;
+        auto work = [&] {
+            ijb_tokenizer::Cache local;
+            for (int i = next++; i < n_texts; i = next++) {
+                try {
+                    t->encode(reinterpret_cast<const uint8_t *>(texts[i]), static_cast<size_t>(lens[i]), out[i],
+                              &local);
+                } catch (const std::exception &e) {
+                    std::lock_guard<std::mutex> lock(err_mu);
+                    if (err.empty()) err = e.what();
+                }
+            }
+        };
+        std::vector<std::thread> pool;
+        for (int k = 1; k < nt; ++k) pool.emplace_back(work);
+        work();
+        for (auto &th : pool) th.join();
+        if (!err.empty()) throw std::runtime_error(err);
+        long total = 0;
+        for (int i = 0; i < n_texts; ++i) {
+            offsets[i] = total;
+            total += static_cast<long>(out[i].size());
+        }
+        offsets[n_texts] = total;
+        if (total > cap) {
+            t->error = "id buffer too small";
+            return IJB_ERR_CAPACITY;
+        }
+        for (int i = 0; i < n_texts; ++i)
+            if (!out[i].empty()) std::memcpy(ids + offsets[i], out[i].data(), out[i].size() * sizeof(int));
+        return IJB_OK;
+    } catch (const std::bad_alloc &) {
+        t->error = "host allocation failed";
+        return IJB_ERR_NOMEM;
     } catch (const std::exception &e) {
         return fail(t, e);
     }

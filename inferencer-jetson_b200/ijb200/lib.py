@@ -98,6 +98,8 @@ def load():
         "ijb_tokenizer_decode": ([P, I, ctypes.c_char_p, I, IP], I),
         "ijb_tokenizer_special": ([P, ctypes.c_char_p, IP], I),
         "ijb_tokenizer_chat_prompt": ([P, ctypes.c_char_p, L64, IP, L64, ctypes.POINTER(L64)], I),
+        "ijb_tokenizer_encode_batch": ([P, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(L64), I, IP, L64,
+                                        ctypes.POINTER(L64), I], I),
         "ijb_last_step_ms": ([P], ctypes.c_float),
     }
     for name, (args, res) in sig.items():

@@ -54,6 +54,25 @@ class Tokenizer:
     def encode(self, text) -> list[int]:
         return self._ids(self.lib.ijb_tokenizer_encode, text)
 
+    def encode_batch(self, texts, threads: int = 0) -> list[list[int]]:
+        """Many texts at once on `threads` host threads (0: all)."""
+        data = [t.encode() if isinstance(t, str) else bytes(t) for t in texts]
+        n = len(data)
+        ptrs = (ctypes.c_char_p * max(1, n))(*data)
+        lens = (ctypes.c_long * max(1, n))(*[len(d) for d in data])
+        offs = (ctypes.c_long * (n + 1))()
+        cap = sum(lens[:n]) + 16
+        while True:
+            buf = np.empty(max(1, cap), np.int32)
+            rc = self.lib.ijb_tokenizer_encode_batch(self.h, ptrs, lens, n,
+                                                     buf.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), cap, offs,
+                                                     int(threads))
+            if rc == _L.ERR_CAPACITY:
+                cap = offs[n]
+                continue
+            self._check(rc)
+            return [buf[offs[i]:offs[i + 1]].tolist() for i in range(n)]
+
     def chat_prompt(self, prompt) -> list[int]:
         """The reference's chat_prompt (inferencer.cu:1534-1551)."""
         return self._ids(self.lib.ijb_tokenizer_chat_prompt, prompt)

@@ -233,3 +233,23 @@ def test_cpp_shim_matches_reference(gold, tmp_path):
     assert int(eot) == 128009 and int(n300) == len(bpe.Tokenizer(gold["tokens"], gold["merges"]).decode(300))
     assert lines[n + 1] == "Invalid token id"
     assert lines[n + 2] == "Expected Llama 3 tokenizer"
+
+
+def test_batch_encode_matches_single_calls(gold, tok):
+    """ijb_tokenizer_encode_batch on 1, 4 and all host threads (each worker
+    with its own piece cache) gives every text the ids the reference gives it;
+    a too-small buffer reports the count needed (IJB_ERR_CAPACITY) first."""
+    import ctypes
+    from ijb200 import lib
+    texts = gold["texts"] * 3
+    want = gold["ids"] * 3
+    for threads in (1, 4, 0):
+        assert tok.encode_batch(texts, threads) == want
+    L = lib.load()
+    ptrs = (ctypes.c_char_p * len(texts))(*texts)
+    lens = (ctypes.c_long * len(texts))(*[len(t) for t in texts])
+    offs = (ctypes.c_long * (len(texts) + 1))()
+    buf = (ctypes.c_int * 4)()
+    rc = L.ijb_tokenizer_encode_batch(tok.h, ptrs, lens, len(texts), buf, 4, offs, 2)
+    assert rc == lib.ERR_CAPACITY and offs[len(texts)] == sum(map(len, want))
+    assert tok.encode_batch([]) == []
