@@ -51,6 +51,29 @@ def test_matvec_tensor_core_path(cuda, batch, dp4a):
     eng.close()
 
 
+@pytest.mark.parametrize("batch", [100, 128, 150])
+def test_matvec_wide_launches_vs_oracle(cuda, batch):
+    """More than 64 tokens through ijb_matvec: 128-token launches where every
+    CTA holds one tile (the wide layout), at the 1B widths, where the K range
+    is split over up to 8 cluster parts that exchange 128-token partial tiles
+    (Q4_K and Q6_K matrices).  Every 9th token against the oracle, INT8 path."""
+    import torch
+    cfg = synth.ModelConfig("w1b-1layer", dim=2048, layers=1, heads=32, kv_heads=8, hidden=8192, vocab=4096)
+    weights = synth.make_model(cfg, seed=21)
+    eng = Engine(cfg, weights, context=32, max_batch=160)
+    rng = np.random.default_rng(batch)
+    shapes = {n: (t, r, c) for n, t, r, c in cfg.matrices()}
+    for name in ("blk.0.attn_q.weight", "blk.0.ffn_gate.weight", "blk.0.ffn_down.weight", "blk.0.attn_v.weight",
+                 "token_embd.weight"):
+        t, rows, cols = shapes[name]
+        x = rng.standard_normal((batch, cols)).astype(np.float32)
+        y = eng.matvec(name, torch.from_numpy(x).to(cuda), batch).cpu().numpy()
+        for b in range(0, batch, 9):
+            ref = O.matvec(t, weights[name], x[b], cols, rows, True, True)
+            assert rel_l2(y[b], ref) < PROJ_BAR, (name, b, rel_l2(y[b], ref))
+    eng.close()
+
+
 def test_split_k_results_are_bit_identical_across_runs(cuda):
     """Projections wide enough to be split over a thread-block cluster (1B
     widths: K = 2048 and 8192) give bit-identical outputs when run again: the
