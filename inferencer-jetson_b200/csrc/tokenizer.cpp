@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <memory>
@@ -139,6 +140,107 @@ std::string utf8_of(uint32_t cp) {
     return s;
 }
 
+// ASCII classes of the pattern's character sets (PCRE2 with UCP): \p{L} is
+// A-Z a-z, \p{N} is 0-9, \s is HT LF VT FF CR and space; everything else
+// (punctuation, symbols, the other control bytes) is in none of them.
+enum : uint8_t { kOtherCls = 0, kLetterCls = 1, kDigitCls = 2, kSpaceCls = 3, kNewlineCls = 4 };
+struct AsciiClasses {
+    uint8_t c[128];
+    constexpr AsciiClasses() : c() {
+        for (int i = 0; i < 128; ++i) {
+            c[i] = kOtherCls;
+            if ((i >= 'A' && i <= 'Z') || (i >= 'a' && i <= 'z')) c[i] = kLetterCls;
+            else if (i >= '0' && i <= '9') c[i] = kDigitCls;
+            else if (i == '\r' || i == '\n') c[i] = kNewlineCls;
+            else if (i == '\t' || i == 11 || i == 12 || i == ' ') c[i] = kSpaceCls;
+        }
+    }
+};
+constexpr AsciiClasses kCls;
+
+// The pattern's match at position i (an ASCII byte) decided from ASCII bytes
+// alone: its alternatives in their order, each with the backtracking PCRE2
+// would do.  Returns false, for PCRE2 to match at i instead, whenever the
+// outcome depends on a byte of 0x80 or above (a letter, number or space
+// beyond ASCII could extend a run or change a choice).
+bool ascii_piece(const uint8_t *t, size_t n, size_t i, size_t *end) {
+    auto hi = [&](size_t k) { return k < n && t[k] >= 0x80; };
+    auto cls = [&](size_t k) { return kCls.c[t[k]]; };  // k < n, ASCII
+    auto run = [&](size_t k, uint8_t want, size_t *j) {  // end of a run of class `want`; false if cut by a high byte
+        while (k < n && t[k] < 0x80 && cls(k) == want) ++k;
+        *j = k;
+        return !hi(k);
+    };
+    const uint8_t c = cls(i);
+    // '[sS]|'[tT]|'[rR][eE]|'[vV][eE]|'[mM]|'[lL][lL]|'[dD]
+    if (t[i] == '\'') {
+        if (hi(i + 1)) return false;
+        if (i + 1 < n) {
+            const uint8_t a = t[i + 1] | 0x20;  // lower case of a letter; no other byte maps onto these
+            if (a == 's' || a == 't' || a == 'm' || a == 'd') {
+                *end = i + 2;
+                return true;
+            }
+            if (a == 'r' || a == 'v' || a == 'l') {
+                if (hi(i + 2)) return false;
+                const uint8_t b = i + 2 < n ? static_cast<uint8_t>(t[i + 2] | 0x20) : 0;
+                if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l')) {
+                    *end = i + 3;
+                    return true;
+                }
+            }
+        }
+    }
+    // [^\r\n\p{L}\p{N}]?\p{L}+
+    if (c == kLetterCls) return run(i, kLetterCls, end);
+    if (c == kOtherCls || c == kSpaceCls) {
+        if (hi(i + 1)) return false;
+        if (i + 1 < n && cls(i + 1) == kLetterCls) return run(i + 1, kLetterCls, end);
+    }
+    // \p{N}{1,3}
+    if (c == kDigitCls) {
+        size_t j = i;
+        while (j < n && j < i + 3 && t[j] < 0x80 && cls(j) == kDigitCls) ++j;
+        if (j < i + 3 && hi(j)) return false;
+        *end = j;
+        return true;
+    }
+    //  ?[^\s\p{L}\p{N}]+[\r\n]*
+    {
+        const size_t k = t[i] == ' ' ? i + 1 : i;
+        if (hi(k)) return false;
+        if (k < n && cls(k) == kOtherCls) {
+            size_t j;
+            if (!run(k, kOtherCls, &j)) return false;
+            while (j < n && (t[j] == '\r' || t[j] == '\n')) ++j;
+            *end = j;
+            return true;
+        }
+    }
+    if (c == kOtherCls) return false;  // not reached: an "other" byte always starts the alternative above
+    // whitespace run [i, j), ASCII only
+    size_t j = i;
+    while (j < n && t[j] < 0x80 && (cls(j) == kSpaceCls || cls(j) == kNewlineCls)) ++j;
+    if (hi(j)) return false;
+    // \s*[\r\n]+ : up to the run's last CR or LF
+    for (size_t m = j; m > i; --m)
+        if (t[m - 1] == '\r' || t[m - 1] == '\n') {
+            *end = m;
+            return true;
+        }
+    // \s+(?!\S) : the whole run at the end of the text, else all but its last byte
+    if (j == n) {
+        *end = j;
+        return true;
+    }
+    if (j - i >= 2) {
+        *end = j - 1;
+        return true;
+    }
+    *end = j;  // \s+
+    return true;
+}
+
 constexpr int kLlama3Vocab = 128256;
 constexpr int kScanMax = 24;          // pieces up to this many symbols merge by array scans
 constexpr size_t kCacheMaxPiece = 64;  // pieces up to this many bytes are cached
@@ -159,6 +261,7 @@ struct ijb_tokenizer {
     std::vector<uint8_t> decode_err;   // 0, 1 malformed UTF-8, 2 a character that is no byte symbol
     void *code = nullptr;
     bool jit = false;
+    bool ascii_scan = true;  // ascii_piece before PCRE2 (IJB_TOKENIZER_ASCII=0 turns it off)
     mutable std::mutex cache_mu;
     mutable std::unordered_map<std::string, std::vector<int>> cache;
     std::string error;
@@ -302,8 +405,15 @@ struct ijb_tokenizer {
         const uint32_t opts = valid_utf8(text, n) ? kPcre2NoUtfCheck : 0u;
         std::unique_ptr<void, void (*)(void *)> md(api.match_data_create(code, nullptr), api.match_data_free);
         if (!md) throw std::runtime_error("PCRE2 match data allocation failed");
+        const bool scan = ascii_scan && opts == kPcre2NoUtfCheck;
         size_t pos = 0;
         while (pos < n) {
+            size_t e;
+            if (scan && text[pos] < 0x80 && ascii_piece(text, n, pos, &e)) {
+                piece(text + pos, e - pos, out, local);
+                pos = e;
+                continue;
+            }
             const int status = api.match(code, text, n, pos, opts, md.get(), nullptr);
             if (status < 0) {
                 piece(text + pos, n - pos, out, local);
@@ -395,6 +505,8 @@ void build(ijb_tokenizer &t, const char *const *tokens, int n_tokens, const char
                          &off, nullptr);
     if (!t.code) throw std::runtime_error("Could not compile tokenizer regex");
     t.jit = api.jit_compile && api.jit_compile(t.code, kPcre2JitComplete) == 0;
+    const char *env = std::getenv("IJB_TOKENIZER_ASCII");  // diagnostic: PCRE2 for every match
+    t.ascii_scan = !(env && std::atoi(env) == 0);
 }
 
 thread_local std::string t_create_err;  // message of the last failed ijb_tokenizer_create in this thread

@@ -253,3 +253,45 @@ def test_batch_encode_matches_single_calls(gold, tok):
     rc = L.ijb_tokenizer_encode_batch(tok.h, ptrs, lens, len(texts), buf, 4, offs, 2)
     assert rc == lib.ERR_CAPACITY and offs[len(texts)] == sum(map(len, want))
     assert tok.encode_batch([]) == []
+
+
+_ALPHABET = (list("'sStTrReEvVmMlLdDxyzAQ019 \t\n\r\x0b\x0c.,;!?-_()[]{}\"#$%&*/\\@^`|~<>=+\x01\x1c\x1f\x7f") +
+             ["'s", "'re", "'ll", "'VE", "  ", "\r\n", " \n", "\n\n", "é", "ß", "²", "٣", " ", "　",
+              " ", "\u0085", "😀", "中", "Ⅻ", "½", "́"])
+
+
+def test_ascii_scanner_matches_pcre(gold, tok):
+    """The ASCII pre-tokenizer scanner (pieces decided from ASCII bytes alone,
+    PCRE2 otherwise) against PCRE2 on every piece (IJB_TOKENIZER_ASCII=0), on
+    random strings built from the pattern's corner cases: contractions,
+    letters, digits, every ASCII whitespace, CR/LF runs, punctuation, control
+    bytes and non-ASCII letters, numbers, spaces and symbols next to them.
+    Where the reference's own Tokenizer is built (oracle/_ref), it checks a
+    share of the same strings too."""
+    import ctypes
+    import os
+    import tempfile
+    os.environ["IJB_TOKENIZER_ASCII"] = "0"
+    try:
+        pcre_only = Tokenizer(gold["tokens"], gold["merges"])
+    finally:
+        del os.environ["IJB_TOKENIZER_ASCII"]
+    rng = random.Random(77)
+    texts = ["".join(rng.choice(_ALPHABET) for _ in range(rng.randint(1, 40))).encode() for _ in range(4000)]
+    for text in texts:
+        assert tok.encode(text) == pcre_only.encode(text), text
+    pcre_only.close()
+    harness = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                           "libref_harness.so")
+    if not os.path.exists(harness):
+        return
+    from gguf_writer import write_vocab_gguf
+    lib = ctypes.CDLL(harness)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "vocab.gguf").encode()
+        write_vocab_gguf(path.decode(), gold["tokens"], gold["merges"])
+        buf = (ctypes.c_int * 512)()
+        n = ctypes.c_long()
+        for text in texts[:800]:
+            assert lib.ref_tokenize(path, text, ctypes.c_long(len(text)), buf, ctypes.c_long(512), ctypes.byref(n)) == 0
+            assert tok.encode(text) == list(buf[:n.value]), text
