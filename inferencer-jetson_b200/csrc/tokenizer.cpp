@@ -15,7 +15,7 @@
 // is merged by scanning an id array, a longer one through a min-heap of
 // (rank, position) entries over a linked list (n log n); the text's UTF-8 is
 // validated once and the pattern runs JIT-compiled; and pieces already seen
-// are served from a cache.  PCRE2 is loaded from its runtime library
+// are served from a per-thread cache.  PCRE2 is loaded from its runtime library
 // (libpcre2-8.so.0) when the first tokenizer is created.
 #include <dlfcn.h>
 
@@ -244,7 +244,18 @@ bool ascii_piece(const uint8_t *t, size_t n, size_t i, size_t *end) {
 constexpr int kLlama3Vocab = 128256;
 constexpr int kScanMax = 24;          // pieces up to this many symbols merge by array scans
 constexpr size_t kCacheMaxPiece = 64;  // pieces up to this many bytes are cached
-constexpr size_t kCacheMaxEntries = 1u << 20;
+constexpr size_t kCacheMaxEntries = 1u << 16;  // per thread; cleared when full
+
+using PieceCache = std::unordered_map<std::string, std::vector<int>>;
+// Each thread's piece cache, tagged with the generation of the tokenizer that
+// filled it (generations are never reused, so a cache is never read for
+// another tokenizer); using another tokenizer on the thread clears it.
+std::atomic<uint64_t> g_tokenizer_generation{0};
+struct ThreadCache {
+    uint64_t generation = 0;
+    PieceCache map;
+};
+thread_local ThreadCache t_cache;
 
 }  // namespace
 
@@ -262,12 +273,15 @@ struct ijb_tokenizer {
     void *code = nullptr;
     bool jit = false;
     bool ascii_scan = true;  // ascii_piece before PCRE2 (IJB_TOKENIZER_ASCII=0 turns it off)
-    mutable std::mutex cache_mu;
-    mutable std::unordered_map<std::string, std::vector<int>> cache;
+    const uint64_t generation = ++g_tokenizer_generation;
     std::string error;
 
     ~ijb_tokenizer() {
         if (code) pcre2().code_free(code);
+        if (t_cache.generation == generation) {  // this thread's cache memory goes now
+            PieceCache().swap(t_cache.map);
+            t_cache.generation = 0;
+        }
     }
 
     // ------------------------------------------------------- BPE, by ids --
@@ -363,9 +377,9 @@ struct ijb_tokenizer {
         }
     }
 
-    // local: a piece cache owned by the calling thread (batch workers), else
-    // the tokenizer's shared cache under its lock
-    using Cache = std::unordered_map<std::string, std::vector<int>>;
+    // local: a piece cache the caller owns (batch workers), else this
+    // thread's cache (no lock either way)
+    using Cache = PieceCache;
     void piece(const uint8_t *p, size_t n, std::vector<int> &out, Cache *local) const {
         if (n == 0) return;
         if (!regular) {
@@ -378,18 +392,18 @@ struct ijb_tokenizer {
         }
         if (n <= kCacheMaxPiece) {
             const std::string key(reinterpret_cast<const char *>(p), n);
-            Cache &c = local ? *local : cache;
-            std::unique_lock<std::mutex> lock(cache_mu, std::defer_lock);
-            if (!local) lock.lock();
+            if (!local && t_cache.generation != generation) {
+                t_cache.map.clear();
+                t_cache.generation = generation;
+            }
+            Cache &c = local ? *local : t_cache.map;
             const auto it = c.find(key);
             if (it != c.end()) {
                 out.insert(out.end(), it->second.begin(), it->second.end());
                 return;
             }
-            if (!local) lock.unlock();
             const size_t first = out.size();
             merge_ids(p, n, out);
-            if (!local) lock.lock();
             if (c.size() >= kCacheMaxEntries) c.clear();
             c.emplace(key, std::vector<int>(out.begin() + static_cast<long>(first), out.end()));
             return;
