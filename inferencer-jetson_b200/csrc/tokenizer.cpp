@@ -1,22 +1,24 @@
 // Llama-3 byte-level BPE tokenizer (host code behind the C ABI).
 //
 // Replaces the reference's Tokenizer (inferencer.cu:361-451) with the same
-// results: the same Unicode pre-tokenizer pattern (matched by PCRE2 with UTF
-// and UCP, as the reference does), each match's bytes mapped to the GGUF
-// byte symbols (bytes 33-126, 161-172 and 174-255 stand for themselves, the
-// others for code points 256, 257, ... in byte order), then merges applied
-// lowest rank first, leftmost first among equal ranks, until none applies.
+// results: the same Unicode pre-tokenizer pattern (PCRE2 with UTF and UCP, as
+// the reference compiles it), each piece's bytes mapped to the GGUF byte
+// symbols (bytes 33-126, 161-172 and 174-255 stand for themselves, the others
+// for code points 256, 257, ... in byte order), then merges applied lowest
+// rank first, leftmost first among equal ranks, until none applies.
 //
-// What differs is the cost.  The reference rebuilds a "left right" string
-// and hashes it for every adjacent pair on every merge step (quadratic in
-// the piece length, with string allocations), and lets PCRE2 re-check the
-// text's UTF-8 on every match call.  Here the merges are a hash map from a
-// pair of token ids to (rank, merged id); a piece of up to kScanMax symbols
-// is merged by scanning an id array, a longer one through a min-heap of
-// (rank, position) entries over a linked list (n log n); the text's UTF-8 is
-// validated once and the pattern runs JIT-compiled; and pieces already seen
-// are served from a per-thread cache.  PCRE2 is loaded from its runtime library
-// (libpcre2-8.so.0) when the first tokenizer is created.
+// What differs is the cost.  The reference matches every piece with PCRE2
+// (which re-checks the rest of the text's UTF-8 on each call) and rebuilds a
+// "left right" string and hashes it for every adjacent pair on every merge
+// step.  Here valid UTF-8 is checked once and split by a scanner that walks
+// the pattern's alternatives over character classes probed from PCRE2 itself
+// (scan_piece); merges are a hash map from a pair of token ids to (rank,
+// merged id), a piece of up to kScanMax symbols merged in an array that keeps
+// each adjacent pair's rank, a longer one through a min-heap of (rank,
+// position) entries over a linked list; and pieces already seen are served
+// from a flat per-thread cache.  PCRE2 (loaded from libpcre2-8.so.0 when the
+// first tokenizer is created) still matches text that is not valid UTF-8,
+// exactly as the reference matches it.
 #include <dlfcn.h>
 
 #include <algorithm>
@@ -140,105 +142,167 @@ std::string utf8_of(uint32_t cp) {
     return s;
 }
 
-// ASCII classes of the pattern's character sets (PCRE2 with UCP): \p{L} is
-// A-Z a-z, \p{N} is 0-9, \s is HT LF VT FF CR and space; everything else
-// (punctuation, symbols, the other control bytes) is in none of them.
+// Character classes of the pattern (PCRE2 with UTF + UCP) for every code
+// point, probed once per process from PCRE2 itself: the runs that \p{L}+,
+// \p{N}+ and \s+ match over a string of all code points in order.  So the
+// scanner below classifies each character exactly as the matcher would, in
+// whatever Unicode version the installed PCRE2 carries.
 enum : uint8_t { kOtherCls = 0, kLetterCls = 1, kDigitCls = 2, kSpaceCls = 3, kNewlineCls = 4 };
-struct AsciiClasses {
-    uint8_t c[128];
-    constexpr AsciiClasses() : c() {
-        for (int i = 0; i < 128; ++i) {
-            c[i] = kOtherCls;
-            if ((i >= 'A' && i <= 'Z') || (i >= 'a' && i <= 'z')) c[i] = kLetterCls;
-            else if (i >= '0' && i <= '9') c[i] = kDigitCls;
-            else if (i == '\r' || i == '\n') c[i] = kNewlineCls;
-            else if (i == '\t' || i == 11 || i == 12 || i == ' ') c[i] = kSpaceCls;
-        }
-    }
-};
-constexpr AsciiClasses kCls;
+constexpr uint32_t kMaxCp = 0x110000;
 
-// The pattern's match at position i (an ASCII byte) decided from ASCII bytes
-// alone: its alternatives in their order, each with the backtracking PCRE2
-// would do.  Returns false, for PCRE2 to match at i instead, whenever the
-// outcome depends on a byte of 0x80 or above (a letter, number or space
-// beyond ASCII could extend a run or change a choice).
-bool ascii_piece(const uint8_t *t, size_t n, size_t i, size_t *end) {
-    auto hi = [&](size_t k) { return k < n && t[k] >= 0x80; };
-    auto cls = [&](size_t k) { return kCls.c[t[k]]; };  // k < n, ASCII
-    auto run = [&](size_t k, uint8_t want, size_t *j) {  // end of a run of class `want`; false if cut by a high byte
-        while (k < n && t[k] < 0x80 && cls(k) == want) ++k;
-        *j = k;
-        return !hi(k);
+const std::vector<uint8_t> *code_point_classes() {
+    static std::vector<uint8_t> cls;
+    static std::once_flag once;
+    static bool ok = false;
+    std::call_once(once, [] {
+        const Pcre2 &api = pcre2();
+        std::string all;
+        std::vector<uint32_t> start;  // byte offset of each code point in `all` (surrogates skipped)
+        std::vector<uint32_t> cps;
+        all.reserve(4u << 20);
+        for (uint32_t cp = 0; cp < kMaxCp; ++cp) {
+            if (cp >= 0xd800 && cp <= 0xdfff) continue;
+            start.push_back(static_cast<uint32_t>(all.size()));
+            cps.push_back(cp);
+            if (cp < 0x80) {
+                all.push_back(static_cast<char>(cp));
+            } else if (cp < 0x800) {
+                all.push_back(static_cast<char>(0xc0 | (cp >> 6)));
+                all.push_back(static_cast<char>(0x80 | (cp & 63)));
+            } else if (cp < 0x10000) {
+                all.push_back(static_cast<char>(0xe0 | (cp >> 12)));
+                all.push_back(static_cast<char>(0x80 | ((cp >> 6) & 63)));
+                all.push_back(static_cast<char>(0x80 | (cp & 63)));
+            } else {
+                all.push_back(static_cast<char>(0xf0 | (cp >> 18)));
+                all.push_back(static_cast<char>(0x80 | ((cp >> 12) & 63)));
+                all.push_back(static_cast<char>(0x80 | ((cp >> 6) & 63)));
+                all.push_back(static_cast<char>(0x80 | (cp & 63)));
+            }
+        }
+        cls.assign(kMaxCp, kOtherCls);
+        const uint8_t *subject = reinterpret_cast<const uint8_t *>(all.data());
+        auto index_of = [&](size_t off) {
+            return static_cast<size_t>(std::lower_bound(start.begin(), start.end(), static_cast<uint32_t>(off)) -
+                                       start.begin());
+        };
+        const std::pair<const char *, uint8_t> probes[] = {
+            {"\\p{L}+", kLetterCls}, {"\\p{N}+", kDigitCls}, {"\\s+", kSpaceCls}};
+        for (const auto &[pattern, value] : probes) {
+            int err = 0;
+            size_t off = 0;
+            void *code = api.compile(reinterpret_cast<const uint8_t *>(pattern), kPcre2ZeroTerminated,
+                                     kPcre2Utf | kPcre2Ucp, &err, &off, nullptr);
+            if (!code) return;
+            if (api.jit_compile) api.jit_compile(code, kPcre2JitComplete);
+            void *md = api.match_data_create(code, nullptr);
+            if (!md) {
+                api.code_free(code);
+                return;
+            }
+            for (size_t pos = 0; pos < all.size();) {
+                if (api.match(code, subject, all.size(), pos, kPcre2NoUtfCheck, md, nullptr) < 0) break;
+                const size_t *span = api.ovector(md);
+                for (size_t k = index_of(span[0]); k < cps.size() && start[k] < span[1]; ++k) cls[cps[k]] = value;
+                pos = span[1] > span[0] ? span[1] : span[1] + 1;
+            }
+            api.match_data_free(md);
+            api.code_free(code);
+        }
+        cls['\r'] = kNewlineCls;
+        cls['\n'] = kNewlineCls;
+        // the classes the pattern's ASCII reading takes for granted
+        ok = cls['a'] == kLetterCls && cls['Z'] == kLetterCls && cls['7'] == kDigitCls && cls[' '] == kSpaceCls &&
+             cls['\t'] == kSpaceCls && cls['\''] == kOtherCls;
+    });
+    return ok ? &cls : nullptr;
+}
+
+// One code point of valid UTF-8 at t[k] (k < n): its value, *len its bytes.
+inline uint32_t decode_cp(const uint8_t *t, size_t k, uint32_t *len) {
+    const uint8_t c = t[k];
+    if (c < 0x80) {
+        *len = 1;
+        return c;
+    }
+    if (c < 0xe0) {
+        *len = 2;
+        return (static_cast<uint32_t>(c & 0x1f) << 6) | (t[k + 1] & 0x3f);
+    }
+    if (c < 0xf0) {
+        *len = 3;
+        return (static_cast<uint32_t>(c & 0x0f) << 12) | (static_cast<uint32_t>(t[k + 1] & 0x3f) << 6) |
+               (t[k + 2] & 0x3f);
+    }
+    *len = 4;
+    return (static_cast<uint32_t>(c & 0x07) << 18) | (static_cast<uint32_t>(t[k + 1] & 0x3f) << 12) |
+           (static_cast<uint32_t>(t[k + 2] & 0x3f) << 6) | (t[k + 3] & 0x3f);
+}
+
+// The pattern's match at position i of valid UTF-8 text, found without PCRE2:
+// its seven alternatives in their order, each with the backtracking PCRE2
+// would do (the optional leading character of the letter and punctuation
+// alternatives given back when what follows does not match, \s*[\r\n]+ ending
+// at a whitespace run's last CR or LF, \s+(?!\S) giving back a run's last
+// character when a non-space follows).  Every position of valid UTF-8 starts a
+// match, so the pieces are the matches, back to back.
+size_t scan_piece(const uint8_t *t, size_t n, size_t i, const uint8_t *cls) {
+    uint32_t len0;
+    const uint32_t c0 = decode_cp(t, i, &len0);
+    const uint8_t k0 = cls[c0];
+    auto cls_at = [&](size_t k, uint32_t *len) { return cls[decode_cp(t, k, len)]; };
+    auto run = [&](size_t k, uint8_t want) {  // end of a run of class `want` from k
+        uint32_t len;
+        while (k < n && cls_at(k, &len) == want) k += len;
+        return k;
     };
-    const uint8_t c = cls(i);
     // '[sS]|'[tT]|'[rR][eE]|'[vV][eE]|'[mM]|'[lL][lL]|'[dD]
-    if (t[i] == '\'') {
-        if (hi(i + 1)) return false;
-        if (i + 1 < n) {
-            const uint8_t a = t[i + 1] | 0x20;  // lower case of a letter; no other byte maps onto these
-            if (a == 's' || a == 't' || a == 'm' || a == 'd') {
-                *end = i + 2;
-                return true;
-            }
-            if (a == 'r' || a == 'v' || a == 'l') {
-                if (hi(i + 2)) return false;
-                const uint8_t b = i + 2 < n ? static_cast<uint8_t>(t[i + 2] | 0x20) : 0;
-                if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l')) {
-                    *end = i + 3;
-                    return true;
-                }
-            }
+    if (c0 == '\'' && i + 1 < n) {
+        const uint8_t a = t[i + 1] | 0x20;  // lower case of an ASCII letter; no other byte maps onto these
+        if (a == 's' || a == 't' || a == 'm' || a == 'd') return i + 2;
+        if (i + 2 < n) {
+            const uint8_t b = t[i + 2] | 0x20;
+            if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l')) return i + 3;
         }
     }
     // [^\r\n\p{L}\p{N}]?\p{L}+
-    if (c == kLetterCls) return run(i, kLetterCls, end);
-    if (c == kOtherCls || c == kSpaceCls) {
-        if (hi(i + 1)) return false;
-        if (i + 1 < n && cls(i + 1) == kLetterCls) return run(i + 1, kLetterCls, end);
+    if (k0 == kLetterCls) return run(i, kLetterCls);
+    if (k0 == kOtherCls || k0 == kSpaceCls) {
+        uint32_t len;
+        if (i + len0 < n && cls_at(i + len0, &len) == kLetterCls) return run(i + len0, kLetterCls);
     }
     // \p{N}{1,3}
-    if (c == kDigitCls) {
+    if (k0 == kDigitCls) {
         size_t j = i;
-        while (j < n && j < i + 3 && t[j] < 0x80 && cls(j) == kDigitCls) ++j;
-        if (j < i + 3 && hi(j)) return false;
-        *end = j;
-        return true;
+        uint32_t len;
+        for (int m = 0; m < 3 && j < n && cls_at(j, &len) == kDigitCls; ++m) j += len;
+        return j;
     }
     //  ?[^\s\p{L}\p{N}]+[\r\n]*
     {
-        const size_t k = t[i] == ' ' ? i + 1 : i;
-        if (hi(k)) return false;
-        if (k < n && cls(k) == kOtherCls) {
-            size_t j;
-            if (!run(k, kOtherCls, &j)) return false;
+        const size_t k = c0 == ' ' ? i + 1 : i;
+        uint32_t len;
+        if (k < n && cls_at(k, &len) == kOtherCls) {
+            size_t j = run(k, kOtherCls);
             while (j < n && (t[j] == '\r' || t[j] == '\n')) ++j;
-            *end = j;
-            return true;
+            return j;
         }
     }
-    if (c == kOtherCls) return false;  // not reached: an "other" byte always starts the alternative above
-    // whitespace run [i, j), ASCII only
-    size_t j = i;
-    while (j < n && t[j] < 0x80 && (cls(j) == kSpaceCls || cls(j) == kNewlineCls)) ++j;
-    if (hi(j)) return false;
-    // \s*[\r\n]+ : up to the run's last CR or LF
-    for (size_t m = j; m > i; --m)
-        if (t[m - 1] == '\r' || t[m - 1] == '\n') {
-            *end = m;
-            return true;
-        }
-    // \s+(?!\S) : the whole run at the end of the text, else all but its last byte
-    if (j == n) {
-        *end = j;
-        return true;
+    // a whitespace run [i, j) (kSpaceCls or kNewlineCls), `last` its last character's start
+    size_t j = i, last = i, newline_end = 0;
+    bool two = false;
+    for (uint32_t len; j < n;) {
+        const uint8_t k = cls_at(j, &len);
+        if (k != kSpaceCls && k != kNewlineCls) break;
+        if (k == kNewlineCls) newline_end = j + 1;
+        two = j > i;
+        last = j;
+        j += len;
     }
-    if (j - i >= 2) {
-        *end = j - 1;
-        return true;
-    }
-    *end = j;  // \s+
-    return true;
+    if (newline_end) return newline_end;  // \s*[\r\n]+
+    if (j == n) return j;                 // \s+(?!\S) at the end of the text
+    if (two) return last;                 // \s+(?!\S): all but the last character
+    return j;                             // \s+
 }
 
 constexpr int kLlama3Vocab = 128256;
@@ -246,7 +310,81 @@ constexpr int kScanMax = 24;          // pieces up to this many symbols merge by
 constexpr size_t kCacheMaxPiece = 64;  // pieces up to this many bytes are cached
 constexpr size_t kCacheMaxEntries = 1u << 16;  // per thread; cleared when full
 
-using PieceCache = std::unordered_map<std::string, std::vector<int>>;
+// Piece bytes -> token ids: open addressing over 2 * kCacheMaxEntries slots
+// (linear probing, a 64-bit hash per slot), the bytes and the ids of all
+// entries in two arenas.  A slot is in use when it carries the table's current
+// epoch, so emptying the table (when full, or for another tokenizer) is a new
+// epoch, not a pass over the slots.
+class PieceCache {
+public:
+    // the ids cached for p[0, n), or null; *count their number
+    const int *find(const uint8_t *p, size_t n, uint64_t h, uint32_t *count) const {
+        if (slots_.empty()) return nullptr;
+        for (size_t i = h & mask_;; i = (i + 1) & mask_) {
+            const Slot &s = slots_[i];
+            if (s.epoch != epoch_) return nullptr;
+            if (s.hash == h && s.key_len == n && std::memcmp(keys_.data() + s.key_off, p, n) == 0) {
+                *count = s.ids_len;
+                return ids_.data() + s.ids_off;
+            }
+        }
+    }
+    void insert(const uint8_t *p, size_t n, uint64_t h, const int *ids, size_t count) {
+        if (slots_.empty() || entries_ >= kCacheMaxEntries) clear();
+        size_t i = h & mask_;
+        while (slots_[i].epoch == epoch_) i = (i + 1) & mask_;
+        slots_[i] = {h, static_cast<uint32_t>(keys_.size()), static_cast<uint32_t>(ids_.size()),
+                     static_cast<uint16_t>(n), static_cast<uint16_t>(count), epoch_};
+        keys_.insert(keys_.end(), p, p + n);
+        ids_.insert(ids_.end(), ids, ids + count);
+        ++entries_;
+    }
+    void clear() {
+        if (slots_.empty() || ++epoch_ == 0) {  // first use, or the epoch counter wrapped
+            slots_.assign(2 * kCacheMaxEntries, Slot{});
+            mask_ = 2 * kCacheMaxEntries - 1;
+            epoch_ = 1;
+        }
+        keys_.clear();
+        ids_.clear();
+        entries_ = 0;
+    }
+    void release() {
+        std::vector<Slot>().swap(slots_);
+        std::vector<uint8_t>().swap(keys_);
+        std::vector<int>().swap(ids_);
+        entries_ = 0;
+    }
+    // a 64-bit hash of the piece (8-byte words folded by multiply and shift)
+    static uint64_t hash(const uint8_t *p, size_t n) {
+        uint64_t h = 0x9e3779b97f4a7c15ull ^ (n * 0xff51afd7ed558ccdull);
+        size_t k = 0;
+        for (; k + 8 <= n; k += 8) {
+            uint64_t w;
+            std::memcpy(&w, p + k, 8);
+            h = (h ^ w) * 0xc4ceb9fe1a85ec53ull;
+            h ^= h >> 31;
+        }
+        uint64_t w = 0;
+        std::memcpy(&w, p + k, n - k);
+        h = (h ^ w) * 0xc4ceb9fe1a85ec53ull;
+        h ^= h >> 29;
+        return h;
+    }
+
+private:
+    struct Slot {
+        uint64_t hash;
+        uint32_t key_off, ids_off;
+        uint16_t key_len, ids_len;
+        uint32_t epoch;  // 0: never used
+    };
+    std::vector<Slot> slots_;
+    std::vector<uint8_t> keys_;
+    std::vector<int> ids_;
+    size_t mask_ = 0, entries_ = 0;
+    uint32_t epoch_ = 1;
+};
 // Each thread's piece cache, tagged with the generation of the tokenizer that
 // filled it (generations are never reused, so a cache is never read for
 // another tokenizer); using another tokenizer on the thread clears it.
@@ -272,14 +410,14 @@ struct ijb_tokenizer {
     std::vector<uint8_t> decode_err;   // 0, 1 malformed UTF-8, 2 a character that is no byte symbol
     void *code = nullptr;
     bool jit = false;
-    bool ascii_scan = true;  // ascii_piece before PCRE2 (IJB_TOKENIZER_ASCII=0 turns it off)
+    const uint8_t *classes = nullptr;  // code point classes for scan_piece; null: PCRE2 matches every piece
     const uint64_t generation = ++g_tokenizer_generation;
     std::string error;
 
     ~ijb_tokenizer() {
         if (code) pcre2().code_free(code);
         if (t_cache.generation == generation) {  // this thread's cache memory goes now
-            PieceCache().swap(t_cache.map);
+            t_cache.map.release();
             t_cache.generation = 0;
         }
     }
@@ -292,23 +430,28 @@ struct ijb_tokenizer {
 
     void merge_ids(const uint8_t *p, size_t n, std::vector<int> &out) const {
         if (n <= static_cast<size_t>(kScanMax)) {
+            // pair[i] = (rank << 32 | merged id) of symbols i, i + 1 (~0: none);
+            // a merge at `at` changes only the pairs on either side of it
             int sym[kScanMax];
+            uint64_t pr[kScanMax];
             int m = static_cast<int>(n);
             for (int i = 0; i < m; ++i) sym[i] = byte_id[p[i]];
+            for (int i = 0; i + 1 < m; ++i) pr[i] = lookup(sym[i], sym[i + 1]);
             while (m > 1) {
                 uint64_t best = ~0ull;
                 int at = -1;
-                for (int i = 0; i + 1 < m; ++i) {
-                    const uint64_t v = lookup(sym[i], sym[i + 1]);
-                    if ((v >> 32) < (best >> 32)) {  // lower rank; leftmost among equals
-                        best = v;
+                for (int i = 0; i + 1 < m; ++i)
+                    if ((pr[i] >> 32) < (best >> 32)) {  // lower rank; leftmost among equals
+                        best = pr[i];
                         at = i;
                     }
-                }
                 if (at < 0) break;
                 sym[at] = static_cast<int>(best & 0xffffffffu);
                 for (int i = at + 1; i + 1 < m; ++i) sym[i] = sym[i + 1];
+                for (int i = at + 1; i + 2 < m; ++i) pr[i] = pr[i + 1];
                 --m;
+                if (at > 0) pr[at - 1] = lookup(sym[at - 1], sym[at]);
+                if (at + 1 < m) pr[at] = lookup(sym[at], sym[at + 1]);
             }
             out.insert(out.end(), sym, sym + m);
             return;
@@ -391,21 +534,20 @@ struct ijb_tokenizer {
             return;
         }
         if (n <= kCacheMaxPiece) {
-            const std::string key(reinterpret_cast<const char *>(p), n);
             if (!local && t_cache.generation != generation) {
                 t_cache.map.clear();
                 t_cache.generation = generation;
             }
             Cache &c = local ? *local : t_cache.map;
-            const auto it = c.find(key);
-            if (it != c.end()) {
-                out.insert(out.end(), it->second.begin(), it->second.end());
+            const uint64_t h = PieceCache::hash(p, n);
+            uint32_t count = 0;
+            if (const int *ids = c.find(p, n, h, &count)) {
+                out.insert(out.end(), ids, ids + count);
                 return;
             }
             const size_t first = out.size();
             merge_ids(p, n, out);
-            if (c.size() >= kCacheMaxEntries) c.clear();
-            c.emplace(key, std::vector<int>(out.begin() + static_cast<long>(first), out.end()));
+            c.insert(p, n, h, out.data() + first, out.size() - first);
             return;
         }
         merge_ids(p, n, out);
@@ -419,15 +561,16 @@ struct ijb_tokenizer {
         const uint32_t opts = valid_utf8(text, n) ? kPcre2NoUtfCheck : 0u;
         std::unique_ptr<void, void (*)(void *)> md(api.match_data_create(code, nullptr), api.match_data_free);
         if (!md) throw std::runtime_error("PCRE2 match data allocation failed");
-        const bool scan = ascii_scan && opts == kPcre2NoUtfCheck;
-        size_t pos = 0;
-        while (pos < n) {
-            size_t e;
-            if (scan && text[pos] < 0x80 && ascii_piece(text, n, pos, &e)) {
+        if (classes && opts == kPcre2NoUtfCheck) {  // valid UTF-8: the scanner finds every match
+            for (size_t pos = 0; pos < n;) {
+                const size_t e = scan_piece(text, n, pos, classes);
                 piece(text + pos, e - pos, out, local);
                 pos = e;
-                continue;
             }
+            return;
+        }
+        size_t pos = 0;
+        while (pos < n) {
             const int status = api.match(code, text, n, pos, opts, md.get(), nullptr);
             if (status < 0) {
                 piece(text + pos, n - pos, out, local);
@@ -519,8 +662,11 @@ void build(ijb_tokenizer &t, const char *const *tokens, int n_tokens, const char
                          &off, nullptr);
     if (!t.code) throw std::runtime_error("Could not compile tokenizer regex");
     t.jit = api.jit_compile && api.jit_compile(t.code, kPcre2JitComplete) == 0;
-    const char *env = std::getenv("IJB_TOKENIZER_ASCII");  // diagnostic: PCRE2 for every match
-    t.ascii_scan = !(env && std::atoi(env) == 0);
+    const char *env = std::getenv("IJB_TOKENIZER_SCAN");  // diagnostic: 0 = PCRE2 for every match
+    if (!(env && std::atoi(env) == 0)) {
+        const std::vector<uint8_t> *cls = code_point_classes();
+        t.classes = cls ? cls->data() : nullptr;
+    }
 }
 
 thread_local std::string t_create_err;  // message of the last failed ijb_tokenizer_create in this thread

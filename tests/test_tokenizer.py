@@ -257,27 +257,28 @@ def test_batch_encode_matches_single_calls(gold, tok):
 
 _ALPHABET = (list("'sStTrReEvVmMlLdDxyzAQ019 \t\n\r\x0b\x0c.,;!?-_()[]{}\"#$%&*/\\@^`|~<>=+\x01\x1c\x1f\x7f") +
              ["'s", "'re", "'ll", "'VE", "  ", "\r\n", " \n", "\n\n", "é", "ß", "²", "٣", " ", "　",
-              " ", "\u0085", "😀", "中", "Ⅻ", "½", "́"])
+              " ", "\u0085", "😀", "中", "Ⅻ", "½", "́", "\u2028", "Москва", "東京", "١٢٣٤", "\u00a0x", "x\u3000 "])
 
 
-def test_ascii_scanner_matches_pcre(gold, tok):
-    """The ASCII pre-tokenizer scanner (pieces decided from ASCII bytes alone,
-    PCRE2 otherwise) against PCRE2 on every piece (IJB_TOKENIZER_ASCII=0), on
-    random strings built from the pattern's corner cases: contractions,
-    letters, digits, every ASCII whitespace, CR/LF runs, punctuation, control
-    bytes and non-ASCII letters, numbers, spaces and symbols next to them.
-    Where the reference's own Tokenizer is built (oracle/_ref), it checks a
-    share of the same strings too."""
+def test_scanner_matches_pcre(gold, tok):
+    """The pre-tokenizer scanner (the pattern's alternatives over code point
+    classes probed from PCRE2) against PCRE2 matching every piece
+    (IJB_TOKENIZER_SCAN=0), on random strings built from the pattern's corner
+    cases: contractions, letters, digits, every ASCII whitespace, CR/LF runs,
+    punctuation, control bytes, and non-ASCII letters, numbers, spaces (NBSP,
+    U+3000, NEL, U+2028), marks and symbols next to them.  Where the
+    reference's own Tokenizer is built (oracle/_ref), it checks a share of the
+    same strings too."""
     import ctypes
     import os
     import tempfile
-    os.environ["IJB_TOKENIZER_ASCII"] = "0"
+    os.environ["IJB_TOKENIZER_SCAN"] = "0"
     try:
         pcre_only = Tokenizer(gold["tokens"], gold["merges"])
     finally:
-        del os.environ["IJB_TOKENIZER_ASCII"]
+        del os.environ["IJB_TOKENIZER_SCAN"]
     rng = random.Random(77)
-    texts = ["".join(rng.choice(_ALPHABET) for _ in range(rng.randint(1, 40))).encode() for _ in range(4000)]
+    texts = ["".join(rng.choice(_ALPHABET) for _ in range(rng.randint(1, 40))).encode() for _ in range(8000)]
     for text in texts:
         assert tok.encode(text) == pcre_only.encode(text), text
     pcre_only.close()
