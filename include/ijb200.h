@@ -301,9 +301,12 @@ float ijb_last_step_ms(const ijb_engine *engine);
 /* ---- tokenizer (host only; no GPU involved) ----
  * Llama-3 byte-level BPE over a GGUF vocabulary, replacing the reference's
  * Tokenizer (inferencer.cu:361-451) with the same results: its pre-tokenizer
- * pattern matched by PCRE2 (the runtime library libpcre2-8.so.0, loaded on
- * first use), its byte-symbol map, merges applied lowest rank first and
- * leftmost first, and its error messages.  Thread-safe after creation. */
+ * pattern (followed by a scanner over PCRE2's own character classes, or
+ * matched by PCRE2 itself for text that is not valid UTF-8; the runtime
+ * library libpcre2-8.so.0 is loaded on first use), its byte-symbol map,
+ * merges applied lowest rank first and leftmost first, and its error
+ * messages.  Thread-safe after creation; each thread keeps a piece cache of
+ * up to 65,536 pieces for the tokenizer it used last. */
 typedef struct ijb_tokenizer ijb_tokenizer;
 
 /* Builds a tokenizer from tokenizer.ggml.tokens (exactly 128256 strings, as
