@@ -310,9 +310,10 @@ constexpr int kScanMax = 24;          // pieces up to this many symbols merge by
 constexpr size_t kCacheMaxPiece = 64;  // pieces up to this many bytes are cached
 constexpr size_t kCacheMaxEntries = 1u << 16;  // per thread; cleared when full
 
-// Piece bytes -> token ids: open addressing over 2 * kCacheMaxEntries slots
-// (linear probing, a 64-bit hash per slot), the bytes and the ids of all
-// entries in two arenas.  A slot is in use when it carries the table's current
+// Piece bytes -> token ids: open addressing (linear probing, a 64-bit hash
+// per slot, at most half the slots in use; the table starts at 4096 slots and
+// doubles up to 2 * kCacheMaxEntries), the bytes and the ids of all entries in
+// two arenas.  A slot is in use when it carries the table's current
 // epoch, so emptying the table (when full, or for another tokenizer) is a new
 // epoch, not a pass over the slots.
 class PieceCache {
@@ -331,6 +332,7 @@ public:
     }
     void insert(const uint8_t *p, size_t n, uint64_t h, const int *ids, size_t count) {
         if (slots_.empty() || entries_ >= kCacheMaxEntries) clear();
+        if (2 * (entries_ + 1) > slots_.size()) grow();
         size_t i = h & mask_;
         while (slots_[i].epoch == epoch_) i = (i + 1) & mask_;
         slots_[i] = {h, static_cast<uint32_t>(keys_.size()), static_cast<uint32_t>(ids_.size()),
@@ -341,8 +343,8 @@ public:
     }
     void clear() {
         if (slots_.empty() || ++epoch_ == 0) {  // first use, or the epoch counter wrapped
-            slots_.assign(2 * kCacheMaxEntries, Slot{});
-            mask_ = 2 * kCacheMaxEntries - 1;
+            slots_.assign(kFirstSlots, Slot{});
+            mask_ = kFirstSlots - 1;
             epoch_ = 1;
         }
         keys_.clear();
@@ -373,6 +375,18 @@ public:
     }
 
 private:
+    static constexpr size_t kFirstSlots = 4096;
+    void grow() {  // twice the slots, the current entries placed again
+        std::vector<Slot> old(2 * slots_.size(), Slot{});
+        old.swap(slots_);
+        mask_ = slots_.size() - 1;
+        for (const Slot &s : old) {
+            if (s.epoch != epoch_) continue;
+            size_t i = s.hash & mask_;
+            while (slots_[i].epoch == epoch_) i = (i + 1) & mask_;
+            slots_[i] = s;
+        }
+    }
     struct Slot {
         uint64_t hash;
         uint32_t key_off, ids_off;
