@@ -14,7 +14,8 @@ Workloads (seeded synthetic inputs; random-init weights, no checkpoint):
             replacements happen inside the timed window and contexts sit at
             the steady-state mix.  A step is one packed decode step over the
             64 live sequences.  The line also carries a `decode1` record
-            (the batch-1 configuration on the same GPU).
+            (the batch-1 configuration on the same GPU) and a `tokenizer`
+            record (the tokenize workload below, host only).
   decode1   same model, one sequence: 512-token prompt (ids U[0,128000),
             seed 1), then greedy decode steps.
   ragged256_3b  Llama-3.2-3B-architecture Q4_K_M (head_dim 128, 24 / 8
@@ -1126,6 +1127,12 @@ def run_ours(args):
         if cpu_extra:
             result["cpu_baseline_extra"] = cpu_extra
         if extras:
+            try:  # the host tokenizer (no GPU), one warm-up and three timed passes beside the reference's
+                tk = run_tokenize(parse(["--workload", "tokenize", "--steps", "3", "--warmup", "1"]))
+                result["tokenizer"] = {k: tk[k] for k in ("metric", "value", "unit", "bytes_per_s", "batch_all_cores",
+                                                          "reference", "data", "config")}
+            except Exception as ex:  # reported, not fatal
+                result["tokenizer"] = {"error": repr(ex)}
             result["reference_cuda"] = {"gemv": reference_cuda_gemv()}
             try:
                 result["reference_cuda"]["decode_3b_b1"] = decode_3b_b1(local)
