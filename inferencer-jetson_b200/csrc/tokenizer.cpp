@@ -12,8 +12,8 @@
 // "left right" string and hashes it for every adjacent pair on every merge
 // step.  Here valid UTF-8 is checked once and split by a scanner that walks
 // the pattern's alternatives over character classes probed from PCRE2 itself
-// (scan_piece); merges are a hash map from a pair of token ids to (rank,
-// merged id), a piece of up to kScanMax symbols merged in an array that keeps
+// (scan_piece); merges are a flat hash table from a pair of token ids to
+// (rank, merged id), a piece of up to kScanMax symbols merged in an array that keeps
 // each adjacent pair's rank, a longer one through a min-heap of (rank,
 // position) entries over a linked list; and pieces already seen are served
 // from a flat per-thread cache.  PCRE2 (loaded from libpcre2-8.so.0 when the
@@ -416,6 +416,10 @@ struct ijb_tokenizer {
     std::unordered_map<std::string, int> ids;            // first occurrence of a token string
     std::unordered_map<std::string, int> rank;           // first occurrence of a merge string
     std::unordered_map<uint64_t, uint64_t> pair;         // (left id, right id) -> rank << 32 | merged id
+    // the same map frozen for lookups: open addressing over 2^pair_bits slots
+    // (Fibonacci hashing, linear probing, key ~0 = empty)
+    std::vector<uint64_t> pair_keys, pair_vals;
+    int pair_bits = 0;
     int byte_id[256];                                    // token id of each byte's symbol
     std::string byte_symbol[256];
     std::unordered_map<std::string, uint8_t> symbol_byte;
@@ -438,8 +442,26 @@ struct ijb_tokenizer {
 
     // ------------------------------------------------------- BPE, by ids --
     uint64_t lookup(int a, int b) const {
-        const auto it = pair.find(static_cast<uint64_t>(static_cast<uint32_t>(a)) << 32 | static_cast<uint32_t>(b));
-        return it == pair.end() ? ~0ull : it->second;
+        const uint64_t key = static_cast<uint64_t>(static_cast<uint32_t>(a)) << 32 | static_cast<uint32_t>(b);
+        const size_t mask = pair_keys.size() - 1;
+        for (size_t i = static_cast<size_t>((key * 0x9e3779b97f4a7c15ull) >> (64 - pair_bits));; i = (i + 1) & mask) {
+            const uint64_t k = pair_keys[i];
+            if (k == key) return pair_vals[i];
+            if (k == ~0ull) return ~0ull;
+        }
+    }
+    void freeze_pairs() {
+        pair_bits = 4;
+        while ((size_t{1} << pair_bits) < 2 * pair.size() + 2) ++pair_bits;
+        pair_keys.assign(size_t{1} << pair_bits, ~0ull);
+        pair_vals.assign(size_t{1} << pair_bits, ~0ull);
+        const size_t mask = pair_keys.size() - 1;
+        for (const auto &[key, val] : pair) {
+            size_t i = static_cast<size_t>((key * 0x9e3779b97f4a7c15ull) >> (64 - pair_bits));
+            while (pair_keys[i] != ~0ull) i = (i + 1) & mask;
+            pair_keys[i] = key;
+            pair_vals[i] = val;
+        }
     }
 
     void merge_ids(const uint8_t *p, size_t n, std::vector<int> &out) const {
@@ -645,6 +667,7 @@ void build(ijb_tokenizer &t, const char *const *tokens, int n_tokens, const char
             if (!ins.second && (val >> 32) < (ins.first->second >> 32)) ins.first->second = val;
         }
     }
+    t.freeze_pairs();
     // decode table: each UTF-8 character of a token string is one byte symbol
     // (lead-byte lengths as inferencer.cu:434-441 reads them)
     t.decoded.resize(n_tokens);
